@@ -1,0 +1,461 @@
+#!/usr/bin/env python
+"""Benchmark of the fused layer-op hot path on B200 (one process per GPU).
+
+Workload (the Llama-3-8B-shaped prefill layer ops, bf16):
+batch 8 x seq 4096 = 32768 token rows per GPU, hidden 4096, 32 query / 8 KV
+heads of 128, intermediate 14336, vocabulary 128256. One step is one pass of
+the hot path over that batch:
+  1. embedding gather  x = table[ids]                  (xn_index_select)
+  2. RMSNorm           y1 = rms_norm(x)                  (xn_rms_norm)
+  3. RoPE on Q and K   theta = 500000, positions 0..4095 (xn_rope_qk)
+  4. residual+RMSNorm  h = x + attn_out; y2 = rms_norm(h) (xn_rms_norm, fused)
+  5. SwiGLU            act = silu(gate) * up              (xn_swiglu)
+Inputs are seeded synthetic tensors already resident in HBM; every tensor is
+larger than the 126 MB L2 except the weights and cos/sin tables, so no L2
+flush is needed between steps.
+
+The metric is algorithmic HBM bytes per second (GB/s) over the whole job:
+each op's bytes are its compulsory reads and writes (formulas in
+op_bytes()), summed over the step and over all ranks (weak scaling: every rank
+runs the full per-GPU batch, with no collective on the data path).
+
+`--impl reference` times the reference CPU backend's algorithm (the oracle
+restatement of mimi-rs/src/cpu_backend.rs) on the host cores for the same
+workload and metric, on a bounded sample of rows.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+for _p in (REPO / "random-things_b200", REPO / "oracle"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+METRIC = "fused-op HBM GB/s (% of B200 peak) & Mimi decode frames/s, 1–8 GPUs"
+UNIT = "GB/s"
+FALLBACK_HBM_GBS = 6650.0
+
+CFG = dict(batch=8, seq=4096, hidden=4096, heads_q=32, heads_kv=8, head_dim=128, inter=14336,
+           vocab=128256, theta=500000.0, eps=1e-5)
+OPS = ["embedding_gather", "rms_norm", "rope_qk", "rms_norm_residual", "swiglu"]
+# Kernel-name fragments of each op (ncu launch list and roofline traffic).
+KERNELS = {"embedding_gather": "gather_rows_kernel", "rms_norm": "norm_regs_kernel",
+           "rope_qk": "rope_kernel", "rms_norm_residual": "norm_regs_kernel", "swiglu": "swiglu_kernel"}
+
+
+def op_bytes(cfg: dict, rows: int, s: int = 2, id_bytes: int = 4) -> dict:
+    """Algorithmic HBM bytes per op for `rows` token rows (1-D weights once)."""
+    H, I, D = cfg["hidden"], cfg["inter"], cfg["head_dim"]
+    seq = cfg["seq"]
+    b = rows // seq
+    q_el = b * cfg["heads_q"] * seq * D
+    k_el = b * cfg["heads_kv"] * seq * D
+    return {
+        "embedding_gather": rows * id_bytes + 2 * rows * H * s,
+        "rms_norm": 2 * rows * H * s + H * s,
+        "rope_qk": 2 * (q_el + k_el) * s + 2 * seq * (D // 2) * s,
+        "rms_norm_residual": 4 * rows * H * s + H * s,
+        "swiglu": 3 * rows * I * s,
+    }
+
+
+def measured_peak() -> tuple[float, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback (6.65 TB/s earlier pool measurement)"
+
+
+def load_traffic() -> dict:
+    """Per-launch DRAM bytes from the committed ncu summary, if present."""
+    p = REPO / "profiles" / "traffic.json"
+    try:
+        return json.loads(p.read_text())
+    except Exception:
+        return {}
+
+
+# ---------------------------------------------------------------------------
+# Clock sampling during the timed region (nvidia-smi, 200 ms).
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str | None):
+        self.uuid = uuid
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.fh.close()
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 8:
+                continue
+            if self.uuid and parts[0] != self.uuid:
+                continue
+            rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        try:
+            sm = [float(r[1]) for r in rows]
+            mx = max(float(r[2]) for r in rows)
+        except ValueError:
+            return None
+        loaded = [r for r in rows if float(r[1]) > 0.5 * mx] or rows
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[4 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(float(r[1]) for r in loaded), "sm_max_mhz": mx,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# The GPU workload.
+# ---------------------------------------------------------------------------
+class LlamaPrefillOps:
+    def __init__(self, torch, xn, device, cfg: dict, seed: int = 0):
+        self.torch, self.xn, self.dev, self.cfg = torch, xn, device, cfg
+        g = torch.Generator(device=device)
+        g.manual_seed(seed)
+        bf = torch.bfloat16
+        B, S, H, I, D = cfg["batch"], cfg["seq"], cfg["hidden"], cfg["inter"], cfg["head_dim"]
+        R = B * S
+        self.rows = R
+
+        def randn(shape, std=1.0, mean=0.0):
+            t = torch.empty(shape, dtype=torch.float32, device=device)
+            t.normal_(mean, std, generator=g)
+            return t.to(bf)
+
+        self.table = randn((cfg["vocab"], H), 0.02)
+        self.ids = torch.randint(0, cfg["vocab"], (R,), dtype=torch.int32, device=device, generator=g)
+        self.alpha1 = randn((H,), 0.02, 1.0)
+        self.alpha2 = randn((H,), 0.02, 1.0)
+        self.attn_out = randn((R, H))
+        self.q = randn((B, cfg["heads_q"], S, D))
+        self.k = randn((B, cfg["heads_kv"], S, D))
+        half = D // 2
+        inv = 1.0 / (cfg["theta"] ** (torch.arange(half, dtype=torch.float32) * 2.0 / D))
+        ang = torch.arange(S, dtype=torch.float32)[:, None] * inv[None, :]
+        self.cos = ang.cos().to(bf).to(device)
+        self.sin = ang.sin().to(bf).to(device)
+        self.gate = randn((R, I))
+        self.up = randn((R, I))
+        self.x = torch.empty((R, H), dtype=bf, device=device)
+        self.y1 = torch.empty_like(self.x)
+        self.h = torch.empty_like(self.x)
+        self.y2 = torch.empty_like(self.x)
+        self.qo = torch.empty_like(self.q)
+        self.ko = torch.empty_like(self.k)
+        self.act = torch.empty_like(self.gate)
+        self.bytes = op_bytes(cfg, R)
+
+    def run_op(self, name: str):
+        xn, c = self.xn, self.cfg
+        if name == "embedding_gather":
+            xn.index_select(self.table, self.ids, 0, out=self.x)
+        elif name == "rms_norm":
+            xn.rms_norm_(self.y1, self.x, self.alpha1, c["eps"])
+        elif name == "rope_qk":
+            xn.rope_qk(self.q, self.k, self.cos, self.sin, 0, out=(self.qo, self.ko))
+        elif name == "rms_norm_residual":
+            xn.rms_norm_(self.y2, self.x, self.alpha2, c["eps"], branch=self.attn_out, residual_out=self.h)
+        elif name == "swiglu":
+            xn.swiglu_(self.act, self.gate, self.up)
+
+    def step(self, events=None):
+        for i, name in enumerate(OPS):
+            if events is not None:
+                events[i][0].record()
+            self.run_op(name)
+            if events is not None:
+                events[i][1].record()
+
+    # End-to-end through the public API with host buffers: inputs copied H2D
+    # from pinned memory and all outputs copied D2H inside the timed region.
+    def host_buffers(self):
+        t = self.torch
+        self.h_in = {k: t.empty(v.shape, dtype=v.dtype, pin_memory=True).copy_(v)
+                     for k, v in (("ids", self.ids), ("attn_out", self.attn_out), ("q", self.q), ("k", self.k),
+                                  ("gate", self.gate), ("up", self.up))}
+        self.h_out = {k: t.empty(v.shape, dtype=v.dtype, pin_memory=True)
+                      for k, v in (("x", self.x), ("y1", self.y1), ("h", self.h), ("y2", self.y2),
+                                   ("qo", self.qo), ("ko", self.ko), ("act", self.act))}
+        self.h2d_bytes = sum(v.numel() * v.element_size() for v in self.h_in.values())
+        self.d2h_bytes = sum(v.numel() * v.element_size() for v in self.h_out.values())
+
+    def e2e_step(self):
+        dev = {"ids": self.ids, "attn_out": self.attn_out, "q": self.q, "k": self.k, "gate": self.gate,
+               "up": self.up}
+        for k, v in self.h_in.items():
+            dev[k].copy_(v, non_blocking=True)
+        self.step()
+        out = {"x": self.x, "y1": self.y1, "h": self.h, "y2": self.y2, "qo": self.qo, "ko": self.ko,
+               "act": self.act}
+        for k, v in self.h_out.items():
+            v.copy_(out[k], non_blocking=True)
+
+
+# ---------------------------------------------------------------------------
+# CPU side: the oracle restatement of the reference CPU backend on a sample.
+# ---------------------------------------------------------------------------
+class CpuSample:
+    """The same five ops on `rows` token rows (and 1 batch element of Q/K
+    restricted to rows // heads... see __init__), run by the oracle."""
+
+    def __init__(self, cfg: dict, rows: int, seed: int = 0):
+        import numpy as np
+
+        import xn_oracle as oracle
+
+        self.o, self.np = oracle, np
+        r = np.random.default_rng(seed)
+        H, I, D = cfg["hidden"], cfg["inter"], cfg["head_dim"]
+        self.cfg, self.rows = cfg, rows
+
+        def bf(shape, std=1.0, mean=0.0):
+            a = (r.standard_normal(shape, dtype=np.float32) * np.float32(std) + np.float32(mean))
+            u = a.view(np.uint32)
+            return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+        # The embedding table sample keeps the full vocabulary row count small
+        # enough for host memory: ids index a 16384-row slice.
+        self.vocab = min(cfg["vocab"], 16384)
+        self.table = bf((self.vocab, H), 0.02)
+        self.ids = r.integers(0, self.vocab, size=rows).astype(np.uint32)
+        self.alpha1, self.alpha2 = bf(H, 0.02, 1.0), bf(H, 0.02, 1.0)
+        self.attn_out = bf((rows, H))
+        # RoPE sample: the same number of (head, position) rows per token row
+        # as the full workload: t positions of all heads of one batch element.
+        self.t = max(1, rows)
+        self.q = bf((1, cfg["heads_q"], min(self.t, cfg["seq"]), D))
+        self.k = bf((1, cfg["heads_kv"], min(self.t, cfg["seq"]), D))
+        self.cos, self.sin = oracle.rope_tables(D, cfg["seq"], cfg["theta"], "bf16", "llama")
+        self.gate, self.up = bf((rows, I)), bf((rows, I))
+        qk_rows_el = (self.q.size + self.k.size)
+        self.bytes = {
+            "embedding_gather": rows * 4 + 2 * rows * H * 2,
+            "rms_norm": 2 * rows * H * 2 + H * 2,
+            "rope_qk": 2 * qk_rows_el * 2 + 2 * self.q.shape[2] * (D // 2) * 2,
+            "rms_norm_residual": 4 * rows * H * 2 + H * 2,
+            "swiglu": 3 * rows * I * 2,
+        }
+
+    def step(self):
+        o, eps = self.o, self.cfg["eps"]
+        x = o.index_select(self.table, self.ids, 0)
+        o.rms_norm(x, self.alpha1, eps, "bf16")
+        o.rope(self.q, self.cos, self.sin, 0, "bf16")
+        o.rope(self.k, self.cos, self.sin, 0, "bf16")
+        o.rms_norm_residual(x, self.attn_out, self.alpha2, eps, "bf16")
+        o.swiglu(self.gate, self.up, "bf16")
+
+    def total_bytes(self) -> int:
+        return sum(self.bytes.values())
+
+
+def cpu_rate(rows: int, steps: int, warmup: int) -> dict:
+    import xn_oracle
+
+    xn_oracle.build()
+    threads = os.cpu_count() or 1
+    xn_oracle.set_num_threads(threads)
+    s = CpuSample(CFG, rows)
+    for _ in range(warmup):
+        s.step()
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        s.step()
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return {"value": s.total_bytes() / med / 1e9, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{rows} of 32768 token rows per step (ids into a {s.vocab}-row table slice; Q/K: 1 batch "
+                      f"element x {s.q.shape[2]} positions); median of {steps} steps; row-parallel ops use "
+                      f"{threads} OpenMP threads, unary/binary ops are single-threaded as in the reference "
+                      f"(cpu_backend.rs:1088-1106)",
+            "ms_per_step": med * 1e3}
+
+
+# ---------------------------------------------------------------------------
+def run_reference(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    rows = args.cpu_rows
+    r = cpu_rate(rows, args.steps, args.warmup)
+    line = {"impl": "reference", "metric": METRIC, "value": r["value"], "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) activations, N(0,0.02) table, N(1,0.02) gains, uniform ids)",
+            "config": config_block(args.gpus),
+            "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": r["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def config_block(n: int) -> dict:
+    return {"workload": "llama3-8b-shaped prefill layer ops (BASELINE config 4): embedding gather, RMSNorm, "
+                        "RoPE(Q,K), residual+RMSNorm, SwiGLU",
+            "batch_per_gpu": CFG["batch"], "seq_len": CFG["seq"], "hidden": CFG["hidden"],
+            "heads": "32q/8kv x 128", "intermediate": CFG["inter"], "vocab": CFG["vocab"],
+            "rows_per_gpu": CFG["batch"] * CFG["seq"], "global_batch": CFG["batch"] * n,
+            "parallelism": f"row-sharded x{n}, no collective", "l2": "inputs larger than L2 (126 MB), no flush"}
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["xn", "reference"], default="xn")
+    ap.add_argument("--cpu-rows", type=int, default=1024, help="token rows in the CPU sample step")
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return 0
+
+    import torch
+    import torch.distributed as dist
+
+    import xn_fused as xn
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    distributed = world > 1
+    if distributed:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    xn.lib()
+    wl = LlamaPrefillOps(torch, xn, dev, CFG, seed=1234 + rank)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+
+    for _ in range(max(3, args.warmup)):
+        wl.step()
+    torch.cuda.synchronize()
+
+    events = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in OPS]
+              for _ in range(args.steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    uuid = None
+    try:
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+        uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+    except Exception:
+        pass
+    sampler = ClockSampler(uuid)
+    sampler.start()
+    time.sleep(0.3)
+    if distributed:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start.record(stream)
+    for k in range(args.steps):
+        wl.step(events[k])
+    stop.record(stream)
+    torch.cuda.synchronize()
+    if distributed:
+        dist.barrier()
+    clocks = sampler.stop()
+    elapsed_ms = start.elapsed_time(stop)
+    per_op_ms = {name: statistics.mean(events[k][i][0].elapsed_time(events[k][i][1]) for k in range(args.steps))
+                 for i, name in enumerate(OPS)}
+
+    # End-to-end with host buffers.
+    wl.host_buffers()
+    torch.cuda.synchronize()
+    for _ in range(2):
+        wl.e2e_step()
+    torch.cuda.synchronize()
+    if distributed:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.e2e_steps):
+        wl.e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
+
+    if distributed:
+        t = torch.tensor([elapsed_ms, e2e_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms, e2e_ms = float(t[0]), float(t[1])
+
+    if rank == 0:
+        step_bytes = sum(wl.bytes.values())
+        ms_per_step = elapsed_ms / args.steps
+        value = world * step_bytes / (ms_per_step * 1e-3) / 1e9
+        peak, peak_src = measured_peak()
+        dom = max(per_op_ms, key=per_op_ms.get)
+        achieved = wl.bytes[dom] / (per_op_ms[dom] * 1e-3) / 1e9
+        traffic = load_traffic().get(dom)
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) activations, N(0,0.02) table, N(1,0.02) gains, uniform ids)",
+            "config": config_block(world),
+            "pct_of_hbm_peak": round(100.0 * value / world / peak, 1),
+            "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": peak,
+                         "peak_source": peak_src, "unit": "GB/s", "frac": round(achieved / peak, 3),
+                         "traffic": traffic, "algorithmic_bytes": wl.bytes[dom]},
+            "per_op": {n: {"ms": round(per_op_ms[n], 4), "bytes": wl.bytes[n],
+                           "gbs": round(wl.bytes[n] / (per_op_ms[n] * 1e-3) / 1e9, 1),
+                           "frac": round(wl.bytes[n] / (per_op_ms[n] * 1e-3) / 1e9 / peak, 3)} for n in OPS},
+            "e2e": {"value": round(world * step_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": UNIT,
+                    "h2d_bytes_per_step": wl.h2d_bytes, "d2h_bytes_per_step": wl.d2h_bytes,
+                    "ms_per_step": round(e2e_ms, 3)},
+            "gpu_launches": len(OPS) * args.steps,
+            "clocks": clocks,
+        }
+        if not args.no_cpu_baseline and world == 1:
+            cb = cpu_rate(args.cpu_rows, 3, 1)
+            line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        print(json.dumps(line), flush=True)
+    if distributed:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,222 @@
+// xn_act.cu - SiLU, GELU(erf) and fused SwiGLU, elementwise, for sm_100a.
+//
+// Reference semantics (mimi-rs/src/cpu_backend.rs):
+//   Silu    :213-215  s / (1 + exp(0 - s))     every op in T arithmetic
+//   GeluErf :197-204  T(x*0.5*(1+erf(x*FRAC_1_SQRT_2)))  in f32, one rounding
+//   SwiGLU  = `gate.silu()` then `mul(up)` (mimi-rs/src/models/llama.rs:256-263)
+//             = T(T(silu(g)) * u)
+//
+// Design: 16-byte vector loads/stores, U accesses per thread issued before any
+// math so each thread keeps U*16 (or 2*U*16 for SwiGLU) bytes in flight.
+#include "xn_common.cuh"
+#include "xn_internal.h"
+
+namespace xn {
+namespace {
+
+// f32 value of std::f32::consts::FRAC_1_SQRT_2.
+constexpr float kFrac1Sqrt2 = 0.707106781186547524400844362104849039f;
+
+template <typename T>
+__device__ __forceinline__ float silu_t(float s) {
+  // (T::zero() - s).exp(), then T::one() + e, then s / (...), each rounded to T.
+  const float e = Elem<T>::round(expf(Elem<T>::round(__fsub_rn(0.f, s))));
+  return __fdiv_rn(s, Elem<T>::round(__fadd_rn(1.f, e)));
+}
+
+__device__ __forceinline__ float gelu_erf(float x) {
+  const float erf_val = erff(__fmul_rn(x, kFrac1Sqrt2));
+  return __fmul_rn(__fmul_rn(x, 0.5f), __fadd_rn(1.f, erf_val));
+}
+
+template <typename T, int OP>
+__device__ __forceinline__ float unary_op(float x) {
+  if constexpr (OP == XN_UNARY_SILU) {
+    return silu_t<T>(x);
+  } else {
+    return gelu_erf(x);
+  }
+}
+
+constexpr int kBlock = 256;
+constexpr int kUnroll = 4;
+
+template <typename T, int OP, bool kVector>
+__global__ void __launch_bounds__(kBlock) unary_kernel(void *dst, const void *src, int64_t n) {
+  constexpr int N = kVector ? Elem<T>::kVec : 1;
+  const int64_t nacc = n / N;
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kBlock * kUnroll + threadIdx.x;
+  const T *s = static_cast<const T *>(src);
+  T *d = static_cast<T *>(dst);
+  if constexpr (kVector) {
+    uint4 raw[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t i = base + u * kBlock;
+      if (i < nacc) raw[u] = ld_stream(s + i * N);
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t i = base + u * kBlock;
+      if (i < nacc) {
+        float v[N];
+        unpack<T>(raw[u], v);
+#pragma unroll
+        for (int j = 0; j < N; ++j) v[j] = unary_op<T, OP>(v[j]);
+        st_vec(d + i * N, pack<T>(v));
+      }
+    }
+    // Ragged tail (< N elements), handled by block 0.
+    if (blockIdx.x == 0) {
+      for (int64_t e = nacc * N + threadIdx.x; e < n; e += kBlock)
+        d[e] = Elem<T>::from_f32(unary_op<T, OP>(Elem<T>::to_f32(s[e])));
+    }
+  } else {
+    float v[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t i = base + u * kBlock;
+      if (i < n) v[u] = Elem<T>::to_f32(s[i]);
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t i = base + u * kBlock;
+      if (i < n) d[i] = Elem<T>::from_f32(unary_op<T, OP>(v[u]));
+    }
+  }
+}
+
+// SwiGLU over [rows, cols] with row strides; grid.x covers the columns of a
+// row (in accesses of N elements), grid.y strides over rows.
+template <typename T, bool kVector>
+__global__ void __launch_bounds__(kBlock) swiglu_kernel(void *dst, const void *gate, const void *up,
+                                                         int64_t rows, int64_t cols, int64_t gs,
+                                                         int64_t us) {
+  constexpr int N = kVector ? Elem<T>::kVec : 1;
+  const int64_t cacc = cols / N;
+  const int64_t c0 = static_cast<int64_t>(blockIdx.x) * kBlock * kUnroll + threadIdx.x;
+  const T *g = static_cast<const T *>(gate);
+  const T *u_ = static_cast<const T *>(up);
+  T *d = static_cast<T *>(dst);
+  for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
+    const T *gr = g + r * gs;
+    const T *ur = u_ + r * us;
+    T *dr = d + r * cols;
+    if constexpr (kVector) {
+      uint4 rg[kUnroll], ru[kUnroll];
+#pragma unroll
+      for (int k = 0; k < kUnroll; ++k) {
+        const int64_t i = c0 + k * kBlock;
+        if (i < cacc) {
+          rg[k] = ld_stream(gr + i * N);
+          ru[k] = ld_stream(ur + i * N);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kUnroll; ++k) {
+        const int64_t i = c0 + k * kBlock;
+        if (i < cacc) {
+          float vg[N], vu[N];
+          unpack<T>(rg[k], vg);
+          unpack<T>(ru[k], vu);
+#pragma unroll
+          for (int j = 0; j < N; ++j) vg[j] = __fmul_rn(Elem<T>::round(silu_t<T>(vg[j])), vu[j]);
+          st_vec(dr + i * N, pack<T>(vg));
+        }
+      }
+    } else {
+      float vg[kUnroll], vu[kUnroll];
+#pragma unroll
+      for (int k = 0; k < kUnroll; ++k) {
+        const int64_t i = c0 + k * kBlock;
+        if (i < cols) {
+          vg[k] = Elem<T>::to_f32(gr[i]);
+          vu[k] = Elem<T>::to_f32(ur[i]);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kUnroll; ++k) {
+        const int64_t i = c0 + k * kBlock;
+        if (i < cols) dr[i] = Elem<T>::from_f32(__fmul_rn(Elem<T>::round(silu_t<T>(vg[k])), vu[k]));
+      }
+    }
+  }
+}
+
+template <typename T>
+int launch_unary(void *dst, const void *src, int64_t n, int op, cudaStream_t st) {
+  constexpr int V = Elem<T>::kVec;
+  const bool vec = is_aligned16(dst) && is_aligned16(src);
+  const int64_t nacc = vec ? n / V : n;
+  const int64_t grid = ceil_div(nacc > 0 ? nacc : 1, static_cast<int64_t>(kBlock) * kUnroll);
+  if (grid > 0x7fffffffLL) return fail(XN_E_INVALID, "xn_unary: too many elements");
+  if (op == XN_UNARY_SILU) {
+    if (vec)
+      unary_kernel<T, XN_UNARY_SILU, true><<<grid, kBlock, 0, st>>>(dst, src, n);
+    else
+      unary_kernel<T, XN_UNARY_SILU, false><<<grid, kBlock, 0, st>>>(dst, src, n);
+  } else {
+    if (vec)
+      unary_kernel<T, XN_UNARY_GELU_ERF, true><<<grid, kBlock, 0, st>>>(dst, src, n);
+    else
+      unary_kernel<T, XN_UNARY_GELU_ERF, false><<<grid, kBlock, 0, st>>>(dst, src, n);
+  }
+  return check_launch("xn_unary");
+}
+
+template <typename T>
+int launch_swiglu(void *dst, const void *gate, const void *up, int64_t rows, int64_t cols, int64_t gs,
+                  int64_t us, cudaStream_t st) {
+  constexpr int V = Elem<T>::kVec;
+  // Contiguous operands are one long row: better load balance, no row loop.
+  if (gs == cols && us == cols && rows > 1) {
+    cols = rows * cols;
+    gs = us = cols;
+    rows = 1;
+  }
+  const bool vec = is_aligned16(dst) && is_aligned16(gate) && is_aligned16(up) && cols % V == 0 &&
+                   gs % V == 0 && us % V == 0;
+  const int64_t cacc = vec ? cols / V : cols;
+  const int64_t gx = ceil_div(cacc, static_cast<int64_t>(kBlock) * kUnroll);
+  if (gx > 0x7fffffffLL) return fail(XN_E_INVALID, "xn_swiglu: row too long");
+  const int64_t gy = rows < 65535 ? rows : 65535;
+  dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy));
+  if (vec)
+    swiglu_kernel<T, true><<<grid, kBlock, 0, st>>>(dst, gate, up, rows, cols, gs, us);
+  else
+    swiglu_kernel<T, false><<<grid, kBlock, 0, st>>>(dst, gate, up, rows, cols, gs, us);
+  return check_launch("xn_swiglu");
+}
+
+}  // namespace
+}  // namespace xn
+
+extern "C" {
+
+int xn_unary(void *dst, const void *src, int64_t n, int op, int dtype, void *stream) {
+  using namespace xn;
+  if (!is_float_dtype(dtype)) return fail(XN_E_DTYPE, "xn_unary: unsupported dtype %d", dtype);
+  if (op != XN_UNARY_SILU && op != XN_UNARY_GELU_ERF) return fail(XN_E_INVALID, "xn_unary: unknown op %d", op);
+  if (n < 0) return fail(XN_E_INVALID, "xn_unary: negative size");
+  if (n == 0) return ok();
+  if (dst == nullptr || src == nullptr) return fail(XN_E_INVALID, "xn_unary: null dst or src");
+  XN_DISPATCH_FLOAT(dtype, return launch_unary<T>(dst, src, n, op, as_stream(stream)));
+  return fail(XN_E_DTYPE, "xn_unary: unsupported dtype %d", dtype);
+}
+
+int xn_swiglu(void *dst, const void *gate, const void *up, int64_t rows, int64_t cols,
+              int64_t gate_stride, int64_t up_stride, int dtype, void *stream) {
+  using namespace xn;
+  if (!is_float_dtype(dtype)) return fail(XN_E_DTYPE, "xn_swiglu: unsupported dtype %d", dtype);
+  if (rows < 0 || cols < 0) return fail(XN_E_INVALID, "xn_swiglu: negative size");
+  if (rows == 0 || cols == 0) return ok();
+  if (gate_stride < cols || up_stride < cols)
+    return fail(XN_E_INVALID, "xn_swiglu: row stride smaller than cols (gate %lld, up %lld, cols %lld)",
+                (long long)gate_stride, (long long)up_stride, (long long)cols);
+  if (dst == nullptr || gate == nullptr || up == nullptr) return fail(XN_E_INVALID, "xn_swiglu: null pointer");
+  XN_DISPATCH_FLOAT(dtype, return launch_swiglu<T>(dst, gate, up, rows, cols, gate_stride, up_stride,
+                                                   as_stream(stream)));
+  return fail(XN_E_DTYPE, "xn_swiglu: unsupported dtype %d", dtype);
+}
+
+}  // extern "C"

@@ -1,0 +1,223 @@
+// xn_common.cuh - shared device helpers for the sm_100a fused layer-op kernels.
+//
+// Every kernel here is HBM-bandwidth bound. The helpers below give:
+//   * element traits: load/convert to f32 and round an f32 back to the element
+//     type T with round-to-nearest-even, so a kernel can reproduce each point
+//     where the reference CPU backend rounds a T-typed intermediate;
+//   * 16-byte vector loads/stores with explicit cache hints (streamed data is
+//     read with L1::no_allocate so weights and tables keep L1);
+//   * sub-warp / multi-warp reductions for "row groups" of power-of-two threads.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace xn {
+
+// ---------------------------------------------------------------------------
+// Element traits. `round` maps an f32 value to the nearest T and back to f32:
+// it is the value the reference would hold after one T-typed operation.
+// ---------------------------------------------------------------------------
+template <typename T>
+struct Elem;
+
+template <>
+struct Elem<float> {
+  static constexpr int kVec = 4;  // elements per 16-byte vector
+  __device__ __forceinline__ static float to_f32(float x) { return x; }
+  __device__ __forceinline__ static float from_f32(float x) { return x; }
+  __device__ __forceinline__ static float round(float x) { return x; }
+};
+
+template <>
+struct Elem<__nv_bfloat16> {
+  static constexpr int kVec = 8;
+  __device__ __forceinline__ static float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
+  __device__ __forceinline__ static __nv_bfloat16 from_f32(float x) { return __float2bfloat16_rn(x); }
+  __device__ __forceinline__ static float round(float x) {
+    return __bfloat162float(__float2bfloat16_rn(x));
+  }
+};
+
+template <>
+struct Elem<__half> {
+  static constexpr int kVec = 8;
+  __device__ __forceinline__ static float to_f32(__half x) { return __half2float(x); }
+  __device__ __forceinline__ static __half from_f32(float x) { return __float2half_rn(x); }
+  __device__ __forceinline__ static float round(float x) { return __half2float(__float2half_rn(x)); }
+};
+
+// ---------------------------------------------------------------------------
+// 16-byte vector memory access.
+// ---------------------------------------------------------------------------
+// Streamed, read-once data: do not allocate in L1. This is a coherent load
+// (no .nc), so it stays correct when the kernel also writes the same buffer
+// (dst or residual_out aliasing src is allowed by the C ABI).
+__device__ __forceinline__ uint4 ld_stream(const void *p) {
+  uint4 r;
+  asm volatile("ld.global.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+// Reused data (weights, cos/sin tables, codebooks): read-only, cached.
+__device__ __forceinline__ uint4 ld_cached(const void *p) {
+  return __ldg(reinterpret_cast<const uint4 *>(p));
+}
+
+__device__ __forceinline__ uint2 ld_cached8(const void *p) {
+  return __ldg(reinterpret_cast<const uint2 *>(p));
+}
+
+// Plain coherent load, for buffers a kernel may also write (aliasing allowed).
+__device__ __forceinline__ uint4 ld_plain(const void *p) {
+  return *reinterpret_cast<const uint4 *>(p);
+}
+
+__device__ __forceinline__ void st_vec(void *p, uint4 v) { *reinterpret_cast<uint4 *>(p) = v; }
+
+// Unpack / pack 16 bytes as kVec values of T widened to f32.
+template <typename T>
+__device__ __forceinline__ void unpack(const uint4 &v, float (&f)[Elem<T>::kVec]);
+
+template <>
+__device__ __forceinline__ void unpack<float>(const uint4 &v, float (&f)[4]) {
+  f[0] = __uint_as_float(v.x);
+  f[1] = __uint_as_float(v.y);
+  f[2] = __uint_as_float(v.z);
+  f[3] = __uint_as_float(v.w);
+}
+
+__device__ __forceinline__ float2 bf2_to_f2(uint32_t w) {
+  __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162 *>(&w);
+  return __bfloat1622float2(h);
+}
+
+__device__ __forceinline__ float2 h2_to_f2(uint32_t w) {
+  __half2 h = *reinterpret_cast<__half2 *>(&w);
+  return __half22float2(h);
+}
+
+template <>
+__device__ __forceinline__ void unpack<__nv_bfloat16>(const uint4 &v, float (&f)[8]) {
+  float2 a = bf2_to_f2(v.x), b = bf2_to_f2(v.y), c = bf2_to_f2(v.z), d = bf2_to_f2(v.w);
+  f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
+  f[4] = c.x; f[5] = c.y; f[6] = d.x; f[7] = d.y;
+}
+
+template <>
+__device__ __forceinline__ void unpack<__half>(const uint4 &v, float (&f)[8]) {
+  float2 a = h2_to_f2(v.x), b = h2_to_f2(v.y), c = h2_to_f2(v.z), d = h2_to_f2(v.w);
+  f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
+  f[4] = c.x; f[5] = c.y; f[6] = d.x; f[7] = d.y;
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 pack(const float (&f)[Elem<T>::kVec]);
+
+template <>
+__device__ __forceinline__ uint4 pack<float>(const float (&f)[4]) {
+  return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
+                    __float_as_uint(f[3]));
+}
+
+__device__ __forceinline__ uint32_t f2_to_bf2(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+
+__device__ __forceinline__ uint32_t f2_to_h2(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+
+template <>
+__device__ __forceinline__ uint4 pack<__nv_bfloat16>(const float (&f)[8]) {
+  return make_uint4(f2_to_bf2(f[0], f[1]), f2_to_bf2(f[2], f[3]), f2_to_bf2(f[4], f[5]),
+                    f2_to_bf2(f[6], f[7]));
+}
+
+template <>
+__device__ __forceinline__ uint4 pack<__half>(const float (&f)[8]) {
+  return make_uint4(f2_to_h2(f[0], f[1]), f2_to_h2(f[2], f[3]), f2_to_h2(f[4], f[5]),
+                    f2_to_h2(f[6], f[7]));
+}
+
+// Half a vector (8 bytes): kVec/2 values, used for the interleaved-RoPE tables.
+template <typename T>
+__device__ __forceinline__ void unpack_half(const uint2 &v, float (&f)[Elem<T>::kVec / 2]);
+
+template <>
+__device__ __forceinline__ void unpack_half<float>(const uint2 &v, float (&f)[2]) {
+  f[0] = __uint_as_float(v.x);
+  f[1] = __uint_as_float(v.y);
+}
+
+template <>
+__device__ __forceinline__ void unpack_half<__nv_bfloat16>(const uint2 &v, float (&f)[4]) {
+  float2 a = bf2_to_f2(v.x), b = bf2_to_f2(v.y);
+  f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
+}
+
+template <>
+__device__ __forceinline__ void unpack_half<__half>(const uint2 &v, float (&f)[4]) {
+  float2 a = h2_to_f2(v.x), b = h2_to_f2(v.y);
+  f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
+}
+
+// Scalar element access for the unaligned / ragged fallbacks.
+template <typename T>
+__device__ __forceinline__ float ld_elem(const void *base, int64_t i) {
+  return Elem<T>::to_f32(reinterpret_cast<const T *>(base)[i]);
+}
+
+template <typename T>
+__device__ __forceinline__ void st_elem(void *base, int64_t i, float v) {
+  reinterpret_cast<T *>(base)[i] = Elem<T>::from_f32(v);
+}
+
+// ---------------------------------------------------------------------------
+// Reductions inside a row group of `tpr` threads (power of two, 1..1024).
+// Groups smaller than a warp use xor-shuffles that stay inside the group;
+// larger groups combine per-warp partials through shared memory `red`, which
+// must hold one float per warp of the block. The combination order is fixed,
+// so results are deterministic run to run.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float group_sum(float v, int tpr, float *red) {
+  const int width = tpr < 32 ? tpr : 32;
+  for (int o = width >> 1; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if (tpr <= 32) return v;
+  const int warp = threadIdx.x >> 5;
+  const int wpr = tpr >> 5;
+  const int first = (warp / wpr) * wpr;
+  if ((threadIdx.x & 31) == 0) red[warp] = v;
+  __syncthreads();
+  float s = red[first];
+  for (int w = 1; w < wpr; ++w) s = __fadd_rn(s, red[first + w]);
+  __syncthreads();  // `red` may be reused by the caller's next reduction
+  return s;
+}
+
+__device__ __forceinline__ float group_max(float v, int tpr, float *red) {
+  const int width = tpr < 32 ? tpr : 32;
+  for (int o = width >> 1; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if (tpr <= 32) return v;
+  const int warp = threadIdx.x >> 5;
+  const int wpr = tpr >> 5;
+  const int first = (warp / wpr) * wpr;
+  if ((threadIdx.x & 31) == 0) red[warp] = v;
+  __syncthreads();
+  float s = red[first];
+  for (int w = 1; w < wpr; ++w) s = fmaxf(s, red[first + w]);
+  __syncthreads();
+  return s;
+}
+
+__host__ __device__ __forceinline__ bool aligned16(const void *p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+}  // namespace xn

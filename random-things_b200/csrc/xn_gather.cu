@@ -1,0 +1,314 @@
+// xn_gather.cu - embedding row gather (index_select) with device-resident ids,
+// and the fused RVQ codebook gather-sum, for sm_100a.
+//
+// Reference semantics: mimi-rs/src/cpu_backend.rs:624-645 (index_select, a
+// byte copy) and the RVQ decode chain mimi-rs/src/models/mimi.rs:1627-1744
+// (per codebook: gather rows, transpose to [B, dim, T], add in codebook order
+// with T rounding per add).
+//
+// Design: one warp per output row copies the row with 16-byte vector loads,
+// four loads in flight per lane before the stores. Ids are read on the device
+// (no host round trip); an out-of-range id yields a zero row and raises a
+// device error flag instead of faulting. The RVQ kernel sums the n_q codebook
+// rows of a frame in registers and, for the [B, dim, T] layout, transposes a
+// tile of 32 frames through shared memory so the stores stay coalesced.
+#include "xn_common.cuh"
+#include "xn_internal.h"
+
+namespace xn {
+namespace {
+
+struct GatherParams {
+  void *dst;
+  const void *src;
+  const void *ids;
+  int *err;
+  int64_t n_ids;
+  int64_t out_rows;   // left * n_ids
+  int64_t src_dim;
+  int64_t row_units;  // row length in access units
+  int ids_i64;
+};
+
+__device__ __forceinline__ int64_t load_id(const void *ids, int64_t i, int ids_i64) {
+  return ids_i64 ? static_cast<const int64_t *>(ids)[i]
+                 : static_cast<int64_t>(static_cast<const uint32_t *>(ids)[i]);
+}
+
+// U = access unit type (uint4 for 16-byte vectors, else the element type).
+template <typename U>
+__global__ void __launch_bounds__(256) gather_rows_kernel(const GatherParams p) {
+  constexpr int kUnroll = 4;
+  const int lane = threadIdx.x & 31;
+  const int64_t orow = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (orow >= p.out_rows) return;
+  const int64_t l = orow / p.n_ids;
+  const int64_t i = orow - l * p.n_ids;
+  const int64_t id = load_id(p.ids, i, p.ids_i64);
+  U *d = static_cast<U *>(p.dst) + orow * p.row_units;
+  if (id < 0 || id >= p.src_dim) {
+    if (lane == 0 && p.err != nullptr) atomicOr(p.err, 1);
+    for (int64_t u = lane; u < p.row_units; u += 32) d[u] = U{};
+    return;
+  }
+  const U *s = static_cast<const U *>(p.src) + (l * p.src_dim + id) * p.row_units;
+  for (int64_t u0 = lane; u0 < p.row_units; u0 += 32 * kUnroll) {
+    U v[kUnroll];
+#pragma unroll
+    for (int k = 0; k < kUnroll; ++k) {
+      const int64_t u = u0 + k * 32;
+      if (u < p.row_units) {
+        if constexpr (sizeof(U) == 16) {
+          v[k] = ld_stream(s + u);
+        } else {
+          v[k] = s[u];
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kUnroll; ++k) {
+      const int64_t u = u0 + k * 32;
+      if (u < p.row_units) d[u] = v[k];
+    }
+  }
+}
+
+struct RvqTables {
+  const void *p[XN_RVQ_MAX_CODEBOOKS];
+};
+
+struct RvqParams {
+  RvqTables tab;
+  void *dst;
+  const int64_t *codes;  // [batch, nq, frames]
+  int *err;
+  int64_t batch, frames, dim, bins;
+  int nq;
+  int nvec;  // accesses per row
+};
+
+// Loads this frame's codes: lane q holds code q (nq <= 32), flags bad codes.
+__device__ __forceinline__ int64_t frame_code(const RvqParams &p, int64_t b, int64_t t, int lane) {
+  int64_t c = 0;
+  if (lane < p.nq) {
+    c = __ldg(p.codes + (b * p.nq + lane) * p.frames + t);
+    if (c < 0 || c >= p.bins) {
+      if (p.err != nullptr) atomicOr(p.err, 1);
+      c = -1;
+    }
+  }
+  return c;
+}
+
+// Sum of the nq codebook rows for access unit u of the frame.
+template <typename T, bool kVector>
+__device__ __forceinline__ void frame_sum(const RvqParams &p, int64_t code_lane, int u,
+                                          float (&acc)[kVector ? Elem<T>::kVec : 1]) {
+  constexpr int N = kVector ? Elem<T>::kVec : 1;
+  for (int q = 0; q < p.nq; ++q) {
+    const int64_t code = __shfl_sync(0xffffffffu, code_lane, q);
+    float v[N];
+    if (code >= 0) {
+      const T *row = static_cast<const T *>(p.tab.p[q]) + code * p.dim + static_cast<int64_t>(u) * N;
+      if constexpr (kVector) {
+        unpack<T>(ld_cached(row), v);
+      } else {
+        v[0] = Elem<T>::to_f32(__ldg(row));
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < N; ++j) v[j] = 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < N; ++j) acc[j] = q == 0 ? v[j] : Elem<T>::round(__fadd_rn(acc[j], v[j]));
+  }
+}
+
+// [batch, frames, dim] output: one warp per frame.
+template <typename T, bool kVector>
+__global__ void __launch_bounds__(256) rvq_btd_kernel(const RvqParams p) {
+  constexpr int N = kVector ? Elem<T>::kVec : 1;
+  const int lane = threadIdx.x & 31;
+  const int64_t frame = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (frame >= p.batch * p.frames) return;
+  const int64_t b = frame / p.frames;
+  const int64_t t = frame - b * p.frames;
+  const int64_t code_lane = frame_code(p, b, t, lane);
+  T *out = static_cast<T *>(p.dst) + frame * p.dim;
+  for (int u0 = 0; u0 < p.nvec; u0 += 32) {
+    const int u = u0 + lane;
+    float acc[N];
+    // All lanes run frame_sum (it shuffles); only in-range units are stored.
+    frame_sum<T, kVector>(p, code_lane, u < p.nvec ? u : 0, acc);
+    if (u < p.nvec) {
+      if constexpr (kVector) {
+        st_vec(out + static_cast<int64_t>(u) * N, pack<T>(acc));
+      } else {
+        out[u] = Elem<T>::from_f32(acc[0]);
+      }
+    }
+  }
+}
+
+// [batch, dim, frames] output: a block owns 32 frames of one batch element;
+// warp w computes frames w, w+8, ... into a shared tile [32][dim+1] (f32),
+// then each warp writes 32 consecutive frames of a channel per store.
+template <typename T, bool kVector>
+__global__ void __launch_bounds__(256) rvq_bct_kernel(const RvqParams p) {
+  constexpr int N = kVector ? Elem<T>::kVec : 1;
+  extern __shared__ float tile[];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int64_t tiles_per_b = (p.frames + 31) / 32;
+  const int64_t b = blockIdx.x / tiles_per_b;
+  const int64_t t0 = (blockIdx.x - b * tiles_per_b) * 32;
+  const int64_t ld = p.dim + 1;
+  for (int f = warp; f < 32; f += 8) {
+    const int64_t t = t0 + f;
+    if (t >= p.frames) break;
+    const int64_t code_lane = frame_code(p, b, t, lane);
+    for (int u0 = 0; u0 < p.nvec; u0 += 32) {
+      const int u = u0 + lane;
+      float acc[N];
+      frame_sum<T, kVector>(p, code_lane, u < p.nvec ? u : 0, acc);
+      if (u < p.nvec) {
+#pragma unroll
+        for (int j = 0; j < N; ++j) tile[f * ld + static_cast<int64_t>(u) * N + j] = acc[j];
+      }
+    }
+  }
+  __syncthreads();
+  T *out = static_cast<T *>(p.dst) + b * p.dim * p.frames;
+  const int64_t t = t0 + lane;
+  if (t < p.frames) {
+    for (int64_t c = warp; c < p.dim; c += 8) out[c * p.frames + t] = Elem<T>::from_f32(tile[lane * ld + c]);
+  }
+}
+
+// Fallback for very wide codebook rows in [batch, dim, frames]: strided stores.
+template <typename T>
+__global__ void __launch_bounds__(256) rvq_bct_wide_kernel(const RvqParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t frame = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (frame >= p.batch * p.frames) return;
+  const int64_t b = frame / p.frames;
+  const int64_t t = frame - b * p.frames;
+  const int64_t code_lane = frame_code(p, b, t, lane);
+  T *out = static_cast<T *>(p.dst) + b * p.dim * p.frames + t;
+  for (int u0 = 0; u0 < p.nvec; u0 += 32) {
+    const int u = u0 + lane;
+    float acc[1];
+    frame_sum<T, false>(p, code_lane, u < p.nvec ? u : 0, acc);
+    if (u < p.nvec) out[static_cast<int64_t>(u) * p.frames] = Elem<T>::from_f32(acc[0]);
+  }
+}
+
+constexpr int64_t kRvqTileMaxDim = 1024;
+
+template <typename T>
+int launch_rvq(RvqParams p, int out_bct, cudaStream_t st) {
+  constexpr int V = Elem<T>::kVec;
+  bool vec = p.dim % V == 0;
+  for (int q = 0; q < p.nq; ++q) vec = vec && is_aligned16(p.tab.p[q]);
+  vec = vec && (out_bct || is_aligned16(p.dst));
+  p.nvec = static_cast<int>(vec ? p.dim / V : p.dim);
+  const int64_t frames_total = p.batch * p.frames;
+  if (!out_bct) {
+    const int64_t grid = ceil_div(frames_total, 8);
+    if (vec)
+      rvq_btd_kernel<T, true><<<grid, 256, 0, st>>>(p);
+    else
+      rvq_btd_kernel<T, false><<<grid, 256, 0, st>>>(p);
+  } else if (p.dim <= kRvqTileMaxDim) {
+    const int64_t grid = p.batch * ((p.frames + 31) / 32);
+    const size_t smem = static_cast<size_t>(32) * (p.dim + 1) * sizeof(float);
+    if (vec) {
+      if (smem > 48 * 1024) cudaFuncSetAttribute(rvq_bct_kernel<T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+      rvq_bct_kernel<T, true><<<grid, 256, smem, st>>>(p);
+    } else {
+      if (smem > 48 * 1024) cudaFuncSetAttribute(rvq_bct_kernel<T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+      rvq_bct_kernel<T, false><<<grid, 256, smem, st>>>(p);
+    }
+  } else {
+    p.nvec = static_cast<int>(p.dim);
+    rvq_bct_wide_kernel<T><<<ceil_div(frames_total, 8), 256, 0, st>>>(p);
+  }
+  return check_launch("xn_rvq_decode_sum");
+}
+
+}  // namespace
+}  // namespace xn
+
+extern "C" {
+
+int xn_index_select(void *dst, const void *src, const void *ids, int ids_is_i64, int64_t n_ids,
+                    int64_t left, int64_t src_dim, int64_t right, int dtype, int *err_flag,
+                    void *stream) {
+  using namespace xn;
+  const int eb = dtype_bytes(dtype);
+  if (eb == 0) return fail(XN_E_DTYPE, "xn_index_select: unsupported dtype %d", dtype);
+  if (n_ids < 0 || left < 0 || src_dim < 0 || right < 0)
+    return fail(XN_E_INVALID, "xn_index_select: negative size");
+  const int64_t out_rows = left * n_ids;
+  if (out_rows == 0 || right == 0) return ok();
+  if (dst == nullptr || ids == nullptr || (src == nullptr && src_dim > 0))
+    return fail(XN_E_INVALID, "xn_index_select: null pointer");
+  const int64_t row_bytes = right * eb;
+  GatherParams p{dst, src, ids, err_flag, n_ids, out_rows, src_dim, 0, ids_is_i64 ? 1 : 0};
+  const int64_t grid = ceil_div(out_rows, 8);
+  if (grid > 0x7fffffffLL) return fail(XN_E_INVALID, "xn_index_select: too many rows");
+  cudaStream_t st = as_stream(stream);
+  if (row_bytes % 16 == 0 && is_aligned16(dst) && is_aligned16(src)) {
+    p.row_units = row_bytes / 16;
+    gather_rows_kernel<uint4><<<grid, 256, 0, st>>>(p);
+  } else {
+    p.row_units = right;
+    switch (eb) {
+      case 1:
+        gather_rows_kernel<uint8_t><<<grid, 256, 0, st>>>(p);
+        break;
+      case 2:
+        gather_rows_kernel<uint16_t><<<grid, 256, 0, st>>>(p);
+        break;
+      case 4:
+        gather_rows_kernel<uint32_t><<<grid, 256, 0, st>>>(p);
+        break;
+      default:
+        gather_rows_kernel<unsigned long long><<<grid, 256, 0, st>>>(p);
+        break;
+    }
+  }
+  return check_launch("xn_index_select");
+}
+
+int xn_rvq_decode_sum(void *dst, const void *const *tables, int64_t n_q, const int64_t *codes,
+                      int64_t batch, int64_t frames, int64_t dim, int64_t bins, int out_bct,
+                      int dtype, int *err_flag, void *stream) {
+  using namespace xn;
+  if (!is_float_dtype(dtype)) return fail(XN_E_DTYPE, "xn_rvq_decode_sum: unsupported dtype %d", dtype);
+  if (n_q <= 0 || n_q > XN_RVQ_MAX_CODEBOOKS)
+    return fail(XN_E_INVALID, "xn_rvq_decode_sum: n_q=%lld outside [1, %d]", (long long)n_q, XN_RVQ_MAX_CODEBOOKS);
+  if (batch < 0 || frames < 0 || dim < 0 || bins < 0) return fail(XN_E_INVALID, "xn_rvq_decode_sum: negative size");
+  if (dim > 0x7fffffffLL) return fail(XN_E_INVALID, "xn_rvq_decode_sum: dim too large");
+  if (batch * frames == 0 || dim == 0) return ok();
+  if (dst == nullptr || codes == nullptr || tables == nullptr)
+    return fail(XN_E_INVALID, "xn_rvq_decode_sum: null pointer");
+  RvqParams p{};
+  for (int64_t q = 0; q < n_q; ++q) {
+    if (tables[q] == nullptr) return fail(XN_E_INVALID, "xn_rvq_decode_sum: codebook %lld is null", (long long)q);
+    p.tab.p[q] = tables[q];
+  }
+  p.dst = dst;
+  p.codes = codes;
+  p.err = err_flag;
+  p.batch = batch;
+  p.frames = frames;
+  p.dim = dim;
+  p.bins = bins;
+  p.nq = static_cast<int>(n_q);
+  if (ceil_div(batch * frames, 8) > 0x7fffffffLL) return fail(XN_E_INVALID, "xn_rvq_decode_sum: too many frames");
+  XN_DISPATCH_FLOAT(dtype, return launch_rvq<T>(p, out_bct, as_stream(stream)));
+  return fail(XN_E_DTYPE, "xn_rvq_decode_sum: unsupported dtype %d", dtype);
+}
+
+}  // extern "C"

@@ -1,0 +1,68 @@
+// xn_internal.h - host-side helpers shared by the C-ABI entry points:
+// error reporting (thread-local message + status code), argument checks and
+// launch-error collection. No function here allocates device memory.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "xn_fused.h"
+
+namespace xn {
+
+// Records a formatted message for xn_last_error() and returns `code`.
+int fail(int code, const char *fmt, ...) __attribute__((format(printf, 2, 3)));
+
+// Clears the thread's message; returns XN_OK.
+int ok();
+
+// Collects the launch status of the kernel(s) just enqueued.
+int check_launch(const char *op);
+
+// Bytes per element, or 0 for an unknown dtype.
+int dtype_bytes(int dtype);
+
+// True for the floating-point dtypes the compute kernels handle.
+inline bool is_float_dtype(int dtype) {
+  return dtype == XN_F32 || dtype == XN_BF16 || dtype == XN_F16;
+}
+
+inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline bool is_aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Smallest power of two >= v (v >= 1).
+inline int64_t pow2_ceil(int64_t v) {
+  int64_t p = 1;
+  while (p < v) p <<= 1;
+  return p;
+}
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+}  // namespace xn
+
+// Dispatches a float dtype to a template parameter named T.
+#define XN_DISPATCH_FLOAT(DTYPE, ...)          \
+  switch (DTYPE) {                             \
+    case XN_F32: {                             \
+      using T = float;                         \
+      __VA_ARGS__;                             \
+      break;                                   \
+    }                                          \
+    case XN_BF16: {                            \
+      using T = __nv_bfloat16;                 \
+      __VA_ARGS__;                             \
+      break;                                   \
+    }                                          \
+    case XN_F16: {                             \
+      using T = __half;                        \
+      __VA_ARGS__;                             \
+      break;                                   \
+    }                                          \
+    default:                                   \
+      break;                                   \
+  }

@@ -1,0 +1,332 @@
+// xn_norm.cu - RMSNorm and LayerNorm over the last dimension, each with an
+// optional fused residual add and layer-scale multiply, for sm_100a.
+//
+// Reference semantics: mimi-rs/src/cpu_backend.rs:691-709 (rms_norm) and
+// :711-750 (layer_norm); the fused prologue restates the composite
+// `LayerScale::forward` (broadcast_mul, cpu_backend.rs:1379-1387) followed by
+// `Tensor::add` (binary Add, cpu_backend.rs:224-258) from
+// mimi-rs/src/models/mimi.rs:1433-1439 and llama.rs:310-313.
+//
+// Design: a row is owned by a "row group" of tpr threads (power of two). The
+// whole row is loaded into registers with 16-byte vector loads (NV vectors per
+// thread), so every tensor crosses HBM exactly once: read src (+ branch),
+// write residual_out (+ dst). The reductions are f32 shuffles inside the group
+// (plus one shared-memory step when the group spans several warps). Rows too
+// wide for registers (> 32768 elements) use a multi-pass kernel that re-reads
+// the row (served from L2 for rows up to a few hundred KB).
+#include "xn_common.cuh"
+#include "xn_internal.h"
+
+namespace xn {
+namespace {
+
+struct NormParams {
+  void *dst;
+  const void *src;
+  const void *w;       // RMS alpha or LN weight (NULL = ones)
+  const void *b;       // LN bias (NULL = zeros)
+  const void *branch;  // optional residual branch
+  const void *ls;      // optional layer scale [cols]
+  void *res_out;       // optional residual output
+  int64_t rows;
+  int64_t cols;
+  float eps;
+  int remove_mean;
+  int tpr;   // threads per row
+  int nvec;  // accesses per row
+};
+
+// Element access in units of N elements: N = kVec (16-byte vectors) or 1.
+template <typename T, bool kVector>
+struct Acc {
+  static constexpr int N = kVector ? Elem<T>::kVec : 1;
+  __device__ __forceinline__ static void load_stream(const void *base, int64_t e, float (&f)[N]) {
+    if constexpr (kVector) {
+      unpack<T>(ld_stream(static_cast<const T *>(base) + e), f);
+    } else {
+      f[0] = ld_elem<T>(base, e);
+    }
+  }
+  __device__ __forceinline__ static void load_cached(const void *base, int64_t e, float (&f)[N]) {
+    if constexpr (kVector) {
+      unpack<T>(ld_cached(static_cast<const T *>(base) + e), f);
+    } else {
+      f[0] = Elem<T>::to_f32(__ldg(static_cast<const T *>(base) + e));
+    }
+  }
+  __device__ __forceinline__ static void store(void *base, int64_t e, const float (&f)[N]) {
+    if constexpr (kVector) {
+      st_vec(static_cast<T *>(base) + e, pack<T>(f));
+    } else {
+      st_elem<T>(base, e, f[0]);
+    }
+  }
+};
+
+// One row per row group, the row held in registers.
+template <typename T, bool kVector, int NV, bool kLN>
+__global__ void __launch_bounds__(1024) norm_regs_kernel(const NormParams p) {
+  using A = Acc<T, kVector>;
+  constexpr int N = A::N;
+  __shared__ float red[32];
+  const int tpr = p.tpr;
+  const int g = threadIdx.x / tpr;
+  const int lr = threadIdx.x - g * tpr;
+  const int rpb = blockDim.x / tpr;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * rpb + g;
+  const bool active = row < p.rows;
+  const int64_t base = row * p.cols;
+
+  // 1) h = src (+ T(branch * ls)), rounded to T after each op, kept in registers.
+  float h[NV][N];
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int vi = lr + k * tpr;
+    if (active && vi < p.nvec) {
+      A::load_stream(p.src, base + static_cast<int64_t>(vi) * N, h[k]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < N; ++j) h[k][j] = 0.f;
+    }
+  }
+  if (p.branch != nullptr) {
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int vi = lr + k * tpr;
+      if (active && vi < p.nvec) {
+        const int64_t e = base + static_cast<int64_t>(vi) * N;
+        float br[N];
+        A::load_stream(p.branch, e, br);
+        if (p.ls != nullptr) {
+          float s[N];
+          A::load_cached(p.ls, static_cast<int64_t>(vi) * N, s);
+#pragma unroll
+          for (int j = 0; j < N; ++j) br[j] = Elem<T>::round(__fmul_rn(br[j], s[j]));
+        }
+#pragma unroll
+        for (int j = 0; j < N; ++j) h[k][j] = Elem<T>::round(__fadd_rn(h[k][j], br[j]));
+        if (p.res_out != nullptr) A::store(p.res_out, e, h[k]);
+      }
+    }
+  }
+
+  // 2) Row statistics in f32.
+  const float cols_f = __ll2float_rn(p.cols);
+  float scale_a, shift_m;  // LN: inv_std, mean ; RMS: m (divisor), unused
+  if constexpr (kLN) {
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k)
+#pragma unroll
+      for (int j = 0; j < N; ++j) s = __fadd_rn(s, h[k][j]);
+    s = group_sum(s, tpr, red);
+    const float mean = __fdiv_rn(s, cols_f);
+    float v = 0.f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      if (lr + k * tpr < p.nvec) {
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+          const float d = __fsub_rn(h[k][j], mean);
+          v = __fadd_rn(v, __fmul_rn(d, d));
+        }
+      }
+    }
+    v = group_sum(v, tpr, red);
+    const float var = __fdiv_rn(v, cols_f);
+    scale_a = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(var, p.eps)));
+    shift_m = mean;
+  } else {
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k)
+#pragma unroll
+      for (int j = 0; j < N; ++j) s = __fadd_rn(s, __fmul_rn(h[k][j], h[k][j]));
+    s = group_sum(s, tpr, red);
+    scale_a = __fsqrt_rn(__fadd_rn(__fdiv_rn(s, cols_f), p.eps));
+    shift_m = 0.f;
+  }
+
+  // 3) Epilogue: dst = T(norm(h) * w (+ b)).
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int vi = lr + k * tpr;
+    if (active && vi < p.nvec) {
+      const int64_t col = static_cast<int64_t>(vi) * N;
+      float wv[N], out[N];
+      if (p.w != nullptr) {
+        A::load_cached(p.w, col, wv);
+      } else {
+#pragma unroll
+        for (int j = 0; j < N; ++j) wv[j] = 1.f;
+      }
+      if constexpr (kLN) {
+        float bv[N];
+        if (p.b != nullptr) {
+          A::load_cached(p.b, col, bv);
+        } else {
+#pragma unroll
+          for (int j = 0; j < N; ++j) bv[j] = 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+          const float c = p.remove_mean ? __fsub_rn(h[k][j], shift_m) : h[k][j];
+          out[j] = __fadd_rn(__fmul_rn(__fmul_rn(c, scale_a), wv[j]), bv[j]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < N; ++j) out[j] = __fmul_rn(__fdiv_rn(h[k][j], scale_a), wv[j]);
+      }
+      A::store(p.dst, base + col, out);
+    }
+  }
+}
+
+// Rows wider than the register budget: one block per row, several passes.
+template <typename T, bool kLN>
+__global__ void __launch_bounds__(1024) norm_loop_kernel(const NormParams p) {
+  __shared__ float red[32];
+  const int tpr = blockDim.x;
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * p.cols;
+  auto compute_h = [&](int64_t c) -> float {
+    float x = ld_elem<T>(p.src, base + c);
+    if (p.branch != nullptr) {
+      float br = ld_elem<T>(p.branch, base + c);
+      if (p.ls != nullptr) br = Elem<T>::round(__fmul_rn(br, ld_elem<T>(p.ls, c)));
+      x = Elem<T>::round(__fadd_rn(x, br));
+    }
+    return x;
+  };
+  // After pass 1, residual_out holds h exactly (it may alias src).
+  auto read_h = [&](int64_t c) -> float {
+    return p.res_out != nullptr ? ld_elem<T>(p.res_out, base + c) : compute_h(c);
+  };
+  const float cols_f = __ll2float_rn(p.cols);
+  float s = 0.f;
+  for (int64_t c = threadIdx.x; c < p.cols; c += tpr) {
+    const float h = compute_h(c);
+    if (p.res_out != nullptr) st_elem<T>(p.res_out, base + c, h);
+    s = __fadd_rn(s, kLN ? h : __fmul_rn(h, h));
+  }
+  s = group_sum(s, tpr, red);
+  if constexpr (kLN) {
+    const float mean = __fdiv_rn(s, cols_f);
+    float v = 0.f;
+    for (int64_t c = threadIdx.x; c < p.cols; c += tpr) {
+      const float d = __fsub_rn(read_h(c), mean);
+      v = __fadd_rn(v, __fmul_rn(d, d));
+    }
+    v = group_sum(v, tpr, red);
+    const float inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(v, cols_f), p.eps)));
+    for (int64_t c = threadIdx.x; c < p.cols; c += tpr) {
+      const float h = read_h(c);
+      const float cen = p.remove_mean ? __fsub_rn(h, mean) : h;
+      const float w = p.w != nullptr ? ld_elem<T>(p.w, c) : 1.f;
+      const float b = p.b != nullptr ? ld_elem<T>(p.b, c) : 0.f;
+      st_elem<T>(p.dst, base + c, __fadd_rn(__fmul_rn(__fmul_rn(cen, inv), w), b));
+    }
+  } else {
+    const float m = __fsqrt_rn(__fadd_rn(__fdiv_rn(s, cols_f), p.eps));
+    for (int64_t c = threadIdx.x; c < p.cols; c += tpr) {
+      const float w = p.w != nullptr ? ld_elem<T>(p.w, c) : 1.f;
+      st_elem<T>(p.dst, base + c, __fmul_rn(__fdiv_rn(read_h(c), m), w));
+    }
+  }
+}
+
+template <typename T, bool kVector, bool kLN>
+void launch_regs(NormParams p, int nv, int block, int64_t grid, cudaStream_t st) {
+  constexpr int N = Acc<T, kVector>::N;
+  switch (nv) {
+    case 1:
+      norm_regs_kernel<T, kVector, 1, kLN><<<grid, block, 0, st>>>(p);
+      break;
+    case 2:
+      norm_regs_kernel<T, kVector, 2, kLN><<<grid, block, 0, st>>>(p);
+      break;
+    case 4:
+      norm_regs_kernel<T, kVector, 4, kLN><<<grid, block, 0, st>>>(p);
+      break;
+    default:
+      if constexpr (8 * N <= 32) norm_regs_kernel<T, kVector, 8, kLN><<<grid, block, 0, st>>>(p);
+      break;
+  }
+}
+
+// Chooses the row-group shape and launches. Register budget: <= 32 f32 values
+// of the row per thread, so rows of up to 32768 elements stay in registers.
+template <typename T, bool kLN>
+int launch_norm(NormParams p, cudaStream_t st, const char *op) {
+  constexpr int V = Elem<T>::kVec;
+  const bool vec = (p.cols % V == 0) && is_aligned16(p.dst) && is_aligned16(p.src) &&
+                   is_aligned16(p.w) && is_aligned16(p.b) && is_aligned16(p.branch) &&
+                   is_aligned16(p.ls) && is_aligned16(p.res_out);
+  const int n = vec ? V : 1;
+  const int64_t nvec = p.cols / n;
+  const int nv_cap = (32 / n) < 8 ? (32 / n) : 8;
+  if (nvec <= 1024LL * nv_cap) {
+    int64_t tpr = pow2_ceil(ceil_div(nvec, 4));
+    if (tpr > 1024) tpr = 1024;
+    const int nv = static_cast<int>(pow2_ceil(ceil_div(nvec, tpr)));
+    const int block = tpr < 256 ? 256 : static_cast<int>(tpr);
+    const int64_t rpb = block / tpr;
+    const int64_t grid = ceil_div(p.rows, rpb);
+    if (grid > 0x7fffffffLL) return fail(XN_E_INVALID, "%s: too many rows (%lld)", op, (long long)p.rows);
+    p.tpr = static_cast<int>(tpr);
+    p.nvec = static_cast<int>(nvec);
+    if (vec)
+      launch_regs<T, true, kLN>(p, nv, block, grid, st);
+    else
+      launch_regs<T, false, kLN>(p, nv, block, grid, st);
+  } else {
+    if (p.rows > 0x7fffffffLL) return fail(XN_E_INVALID, "%s: too many rows (%lld)", op, (long long)p.rows);
+    norm_loop_kernel<T, kLN><<<static_cast<unsigned>(p.rows), 1024, 0, st>>>(p);
+  }
+  return check_launch(op);
+}
+
+int check_norm_args(const char *op, const void *dst, const void *src, const void *branch,
+                    const void *ls, int64_t rows, int64_t cols, float eps, int dtype) {
+  if (!is_float_dtype(dtype)) return fail(XN_E_DTYPE, "%s: unsupported dtype %d", op, dtype);
+  if (rows < 0 || cols < 0) return fail(XN_E_INVALID, "%s: negative size rows=%lld cols=%lld", op, (long long)rows, (long long)cols);
+  if (!(eps > 0.f)) return fail(XN_E_INVALID, "%s: eps must be positive (got %g)", op, (double)eps);
+  if (rows > 0 && cols > 0 && (dst == nullptr || src == nullptr))
+    return fail(XN_E_INVALID, "%s: null dst or src", op);
+  if (ls != nullptr && branch == nullptr)
+    return fail(XN_E_INVALID, "%s: layer_scale given without a branch", op);
+  return XN_OK;
+}
+
+}  // namespace
+}  // namespace xn
+
+extern "C" {
+
+int xn_rms_norm(void *dst, const void *src, const void *alpha, const void *branch,
+                const void *layer_scale, void *residual_out, int64_t rows, int64_t cols, float eps,
+                int dtype, void *stream) {
+  using namespace xn;
+  const char *op = "xn_rms_norm";
+  int rc = check_norm_args(op, dst, src, branch, layer_scale, rows, cols, eps, dtype);
+  if (rc != XN_OK) return rc;
+  if (rows == 0 || cols == 0) return ok();
+  NormParams p{dst, src, alpha, nullptr, branch, layer_scale, residual_out, rows, cols, eps, 0, 0, 0};
+  XN_DISPATCH_FLOAT(dtype, return launch_norm<T, false>(p, as_stream(stream), op));
+  return fail(XN_E_DTYPE, "%s: unsupported dtype %d", op, dtype);
+}
+
+int xn_layer_norm(void *dst, const void *src, const void *weight, const void *bias,
+                  const void *branch, const void *layer_scale, void *residual_out, int64_t rows,
+                  int64_t cols, float eps, int remove_mean, int dtype, void *stream) {
+  using namespace xn;
+  const char *op = "xn_layer_norm";
+  int rc = check_norm_args(op, dst, src, branch, layer_scale, rows, cols, eps, dtype);
+  if (rc != XN_OK) return rc;
+  if (rows == 0 || cols == 0) return ok();
+  NormParams p{dst, src, weight, bias, branch, layer_scale, residual_out, rows, cols, eps,
+               remove_mean ? 1 : 0, 0, 0};
+  XN_DISPATCH_FLOAT(dtype, return launch_norm<T, true>(p, as_stream(stream), op));
+  return fail(XN_E_DTYPE, "%s: unsupported dtype %d", op, dtype);
+}
+
+}  // extern "C"

@@ -1,0 +1,74 @@
+"""GPU parity: SiLU, GELU(erf) and the fused SwiGLU against the oracle
+(cpu_backend.rs:184-258; SwiGLU = silu then mul, llama.rs:256-263)."""
+import numpy as np
+import pytest
+import torch
+
+from helpers import assert_close, from_device, randn, rng, to_device, to_storage
+
+pytestmark = pytest.mark.gpu
+
+DTYPES = ["f32", "bf16", "f16"]
+SIZES = [1, 7, 1000, 4096 * 3 + 5, 1 << 20]
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("n", SIZES)
+@pytest.mark.parametrize("op", ["silu", "gelu_erf"])
+def test_unary(oracle, xn, cuda, dtype, n, op):
+    r = rng(n + len(op))
+    x = to_storage(randn(r, n, 3.0), dtype)
+    ref = oracle.unary(x, op, dtype)
+    Y = getattr(xn, op)(to_device(x, dtype, cuda))
+    assert_close(from_device(Y, dtype), ref, dtype, f"{op} {dtype} n={n}")
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_unary_misaligned(oracle, xn, cuda, dtype):
+    r = rng(3)
+    n = 10001
+    x = to_storage(randn(r, n, 2.0), dtype)
+    X = to_device(np.concatenate([x[:1], x]), dtype, cuda)[1:]
+    Y = torch.empty_like(X)
+    xn.unary_(Y, X, "gelu_erf")
+    assert_close(from_device(Y, dtype), oracle.unary(x, "gelu_erf", dtype), dtype, "gelu misaligned")
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("rows,cols", [(1, 1), (3, 5), (512, 5632), (64, 4096), (7, 1000)])
+def test_swiglu_contiguous(oracle, xn, cuda, dtype, rows, cols):
+    r = rng(rows * 3 + cols)
+    g = to_storage(randn(r, (rows, cols), 2.0), dtype)
+    u = to_storage(randn(r, (rows, cols)), dtype)
+    ref = oracle.swiglu(g, u, dtype)
+    Y = xn.swiglu(to_device(g, dtype, cuda), to_device(u, dtype, cuda))
+    assert_close(from_device(Y, dtype), ref, dtype, f"swiglu {dtype} {rows}x{cols}")
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("rows,inter", [(64, 1024), (5, 24), (3, 7)])
+def test_swiglu_packed_projection(oracle, xn, cuda, dtype, rows, inter):
+    """gate and up as the two halves of one [rows, 2*I] projection output."""
+    r = rng(rows + inter)
+    gu = to_storage(randn(r, (rows, 2 * inter), 2.0), dtype)
+    g, u = np.ascontiguousarray(gu[:, :inter]), np.ascontiguousarray(gu[:, inter:])
+    ref = oracle.swiglu(g, u, dtype)
+    GU = to_device(gu, dtype, cuda)
+    Y = xn.swiglu(GU[:, :inter], GU[:, inter:])
+    assert_close(from_device(Y, dtype), ref, dtype, "swiglu packed")
+
+
+def test_config_shapes(oracle, xn, cuda):
+    """Config 1 SwiGLU [1,512,5632] f32; config 2 GELU [4,250,2048] f32 and bf16;
+    config 3 SiLU [16,4096] bf16."""
+    r = rng(9)
+    g, u = randn(r, (1, 512, 5632)), randn(r, (1, 512, 5632))
+    Y = xn.swiglu(to_device(g, "f32", cuda), to_device(u, "f32", cuda))
+    assert_close(from_device(Y, "f32"), oracle.swiglu(g, u, "f32"), "f32", "config1 swiglu")
+    for dtype in ("f32", "bf16"):
+        x = to_storage(randn(r, (4, 250, 2048)), dtype)
+        Y = xn.gelu_erf(to_device(x, dtype, cuda))
+        assert_close(from_device(Y, dtype), oracle.unary(x, "gelu_erf", dtype), dtype, f"config2 gelu {dtype}")
+    x = to_storage(randn(r, (16, 4096), 0.02), "bf16")
+    Y = xn.silu(to_device(x, "bf16", cuda))
+    assert_close(from_device(Y, "bf16"), oracle.unary(x, "silu", "bf16"), "bf16", "config3 silu")

@@ -1,0 +1,59 @@
+"""GPU parity: row softmax, the fused causal softmax and the stand-alone
+causal mask against the oracle (cpu_backend.rs:647-689; the causal composite
+is apply_causality_mask then softmax, llama.rs:201-202)."""
+import numpy as np
+import pytest
+
+from helpers import assert_close, from_device, randn, rng, to_device, to_storage
+
+pytestmark = pytest.mark.gpu
+
+DTYPES = ["f32", "bf16", "f16"]
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("rows,cols", [(1, 1), (2, 3), (5, 7), (64, 64), (300, 250), (64, 512), (8, 1000),
+                                       (4, 4096), (3, 16384), (2, 20000)])
+def test_softmax(oracle, xn, cuda, dtype, rows, cols):
+    r = rng(rows * 13 + cols)
+    x = to_storage(randn(r, (rows, cols), 2.0), dtype)
+    ref = oracle.softmax(x, dtype)
+    Y = xn.softmax(to_device(x, dtype, cuda))
+    assert_close(from_device(Y, dtype), ref, dtype, f"softmax {dtype} {rows}x{cols}")
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("shape,offset", [((1, 16, 512, 512), 0), ((2, 3, 5, 7), 0), ((2, 3, 5, 7), 2),
+                                          ((16, 16, 1, 200), 199), ((4, 8, 64, 96), 32), ((3, 9, 40), 0),
+                                          ((1, 2, 3, 17000), 16990)])
+def test_softmax_causal(oracle, xn, cuda, dtype, shape, offset):
+    r = rng(sum(shape) + offset)
+    x = to_storage(randn(r, shape, 2.0), dtype)
+    ref = oracle.softmax_causal(x, offset, dtype)
+    Y = from_device(xn.softmax_causal(to_device(x, dtype, cuda), offset), dtype)
+    assert_close(Y, ref, dtype, f"softmax_causal {dtype} {shape} off={offset}")
+    # Masked entries are exactly +0.
+    t1, t2 = shape[-2], shape[-1]
+    i = np.arange(t1)[:, None]
+    j = np.arange(t2)[None, :]
+    masked = np.broadcast_to(j > i + offset, Y.shape)
+    assert np.all(Y[masked] == 0)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("shape,offset", [((1, 3, 4), 0), ((1, 2, 4), 2), ((2, 4, 33, 70), 5), ((6, 1, 9), 3)])
+def test_causality_mask(oracle, xn, cuda, dtype, shape, offset):
+    r = rng(len(shape) + offset)
+    x = to_storage(randn(r, shape), dtype)
+    ref = oracle.apply_causality_mask(x, offset, dtype)
+    Y = xn.apply_causality_mask(to_device(x, dtype, cuda), offset)
+    assert np.array_equal(from_device(Y, dtype), ref)
+
+
+def test_softmax_decode_steps(oracle, xn, cuda):
+    """Config 3: softmax over cached scores [16,16,1,t] bf16 for several t."""
+    r = rng(11)
+    for t in (1, 2, 31, 128, 256):
+        x = to_storage(randn(r, (16, 16, 1, t), 1.0), "bf16")
+        Y = xn.softmax(to_device(x, "bf16", cuda))
+        assert_close(from_device(Y, "bf16"), oracle.softmax(x, "bf16"), "bf16", f"decode t={t}")
