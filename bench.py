@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the fused layer-op hot path on B200 (one process per GPU).
 
-Workload (the Llama-3-8B-shaped prefill layer ops, bf16):
+Workload (benchmark config 4, the Llama-3-8B-shaped prefill layer ops, bf16):
 batch 8 x seq 4096 = 32768 token rows per GPU, hidden 4096, 32 query / 8 KV
 heads of 128, intermediate 14336, vocabulary 128256. One step is one pass of
 the hot path over that batch:
@@ -144,8 +144,10 @@ class ClockSampler:
 # The GPU workload.
 # ---------------------------------------------------------------------------
 class LlamaPrefillOps:
-    def __init__(self, torch, xn, device, cfg: dict, seed: int = 0):
-        self.torch, self.xn, self.dev, self.cfg = torch, xn, device, cfg
+    """The per-GPU workload: `batch` sequences of `seq` tokens (rows = batch*seq)."""
+
+    def __init__(self, torch, xn, device, cfg: dict, seed: int = 0, ops=OPS):
+        self.torch, self.xn, self.dev, self.cfg, self.ops = torch, xn, device, cfg, list(ops)
         g = torch.Generator(device=device)
         g.manual_seed(seed)
         bf = torch.bfloat16
@@ -158,73 +160,125 @@ class LlamaPrefillOps:
             t.normal_(mean, std, generator=g)
             return t.to(bf)
 
-        self.table = randn((cfg["vocab"], H), 0.02)
-        self.ids = torch.randint(0, cfg["vocab"], (R,), dtype=torch.int32, device=device, generator=g)
-        self.alpha1 = randn((H,), 0.02, 1.0)
-        self.alpha2 = randn((H,), 0.02, 1.0)
-        self.attn_out = randn((R, H))
-        self.q = randn((B, cfg["heads_q"], S, D))
-        self.k = randn((B, cfg["heads_kv"], S, D))
-        half = D // 2
-        inv = 1.0 / (cfg["theta"] ** (torch.arange(half, dtype=torch.float32) * 2.0 / D))
-        ang = torch.arange(S, dtype=torch.float32)[:, None] * inv[None, :]
-        self.cos = ang.cos().to(bf).to(device)
-        self.sin = ang.sin().to(bf).to(device)
-        self.gate = randn((R, I))
-        self.up = randn((R, I))
-        self.x = torch.empty((R, H), dtype=bf, device=device)
-        self.y1 = torch.empty_like(self.x)
-        self.h = torch.empty_like(self.x)
-        self.y2 = torch.empty_like(self.x)
-        self.qo = torch.empty_like(self.q)
-        self.ko = torch.empty_like(self.k)
-        self.act = torch.empty_like(self.gate)
-        self.bytes = op_bytes(cfg, R)
+        def need(*names):
+            return any(n in self.ops for n in names)
 
-    def run_op(self, name: str):
+        if need("embedding_gather"):
+            self.table = randn((cfg["vocab"], H), 0.02)
+            self.ids = torch.randint(0, cfg["vocab"], (R,), dtype=torch.int32, device=device, generator=g)
+        if need("embedding_gather", "rms_norm", "rms_norm_residual"):
+            self.x = randn((R, H))
+        if need("rms_norm"):
+            self.alpha1 = randn((H,), 0.02, 1.0)
+            self.y1 = torch.empty_like(self.x)
+        if need("rms_norm_residual"):
+            self.alpha2 = randn((H,), 0.02, 1.0)
+            self.attn_out = randn((R, H))
+            self.h = torch.empty_like(self.x)
+            self.y2 = torch.empty_like(self.x)
+        if need("rope_qk"):
+            self.q = randn((B, cfg["heads_q"], S, D))
+            self.k = randn((B, cfg["heads_kv"], S, D))
+            half = D // 2
+            inv = 1.0 / (cfg["theta"] ** (torch.arange(half, dtype=torch.float32) * 2.0 / D))
+            ang = torch.arange(S, dtype=torch.float32)[:, None] * inv[None, :]
+            self.cos = ang.cos().to(bf).to(device)
+            self.sin = ang.sin().to(bf).to(device)
+            self.qo = torch.empty_like(self.q)
+            self.ko = torch.empty_like(self.k)
+        if need("swiglu"):
+            self.gate = randn((R, I))
+            self.up = randn((R, I))
+            self.act = torch.empty_like(self.gate)
+        allb = op_bytes(cfg, R)
+        self.bytes = {n: allb[n] for n in self.ops}
+
+    def run_op(self, name: str, b0: int = 0, b1: int | None = None):
+        """One op on batch elements [b0, b1) (token rows [b0*seq, b1*seq))."""
         xn, c = self.xn, self.cfg
+        b1 = self.cfg["batch"] if b1 is None else b1
+        r0, r1 = b0 * c["seq"], b1 * c["seq"]
         if name == "embedding_gather":
-            xn.index_select(self.table, self.ids, 0, out=self.x)
+            xn.index_select(self.table, self.ids[r0:r1], 0, out=self.x[r0:r1])
         elif name == "rms_norm":
-            xn.rms_norm_(self.y1, self.x, self.alpha1, c["eps"])
+            xn.rms_norm_(self.y1[r0:r1], self.x[r0:r1], self.alpha1, c["eps"])
         elif name == "rope_qk":
-            xn.rope_qk(self.q, self.k, self.cos, self.sin, 0, out=(self.qo, self.ko))
+            xn.rope_qk(self.q[b0:b1], self.k[b0:b1], self.cos, self.sin, 0, out=(self.qo[b0:b1], self.ko[b0:b1]))
         elif name == "rms_norm_residual":
-            xn.rms_norm_(self.y2, self.x, self.alpha2, c["eps"], branch=self.attn_out, residual_out=self.h)
+            xn.rms_norm_(self.y2[r0:r1], self.x[r0:r1], self.alpha2, c["eps"], branch=self.attn_out[r0:r1],
+                         residual_out=self.h[r0:r1])
         elif name == "swiglu":
-            xn.swiglu_(self.act, self.gate, self.up)
+            xn.swiglu_(self.act[r0:r1], self.gate[r0:r1], self.up[r0:r1])
 
     def step(self, events=None):
-        for i, name in enumerate(OPS):
+        for i, name in enumerate(self.ops):
             if events is not None:
                 events[i][0].record()
             self.run_op(name)
             if events is not None:
                 events[i][1].record()
 
-    # End-to-end through the public API with host buffers: inputs copied H2D
-    # from pinned memory and all outputs copied D2H inside the timed region.
+    # -- End to end through the public API with host buffers ------------------
+    # Every step copies its inputs from pinned host memory and all of its
+    # outputs back. The step is cut into per-sequence chunks on three streams
+    # (H2D, compute, D2H) so both PCIe directions and the kernels overlap.
+    IN_NAMES = ("ids", "attn_out", "q", "k", "gate", "up")
+    OUT_NAMES = ("x", "y1", "h", "y2", "qo", "ko", "act")
+
     def host_buffers(self):
         t = self.torch
-        self.h_in = {k: t.empty(v.shape, dtype=v.dtype, pin_memory=True).copy_(v)
-                     for k, v in (("ids", self.ids), ("attn_out", self.attn_out), ("q", self.q), ("k", self.k),
-                                  ("gate", self.gate), ("up", self.up))}
-        self.h_out = {k: t.empty(v.shape, dtype=v.dtype, pin_memory=True)
-                      for k, v in (("x", self.x), ("y1", self.y1), ("h", self.h), ("y2", self.y2),
-                                   ("qo", self.qo), ("ko", self.ko), ("act", self.act))}
+        self.h_in = {k: t.empty(getattr(self, k).shape, dtype=getattr(self, k).dtype, pin_memory=True)
+                     .copy_(getattr(self, k)) for k in self.IN_NAMES if hasattr(self, k)}
+        self.h_out = {k: t.empty(getattr(self, k).shape, dtype=getattr(self, k).dtype, pin_memory=True)
+                      for k in self.OUT_NAMES if hasattr(self, k)}
         self.h2d_bytes = sum(v.numel() * v.element_size() for v in self.h_in.values())
         self.d2h_bytes = sum(v.numel() * v.element_size() for v in self.h_out.values())
+        self.s_h2d, self.s_d2h = t.cuda.Stream(), t.cuda.Stream()
+        self.s_comp = t.cuda.current_stream()
 
-    def e2e_step(self):
-        dev = {"ids": self.ids, "attn_out": self.attn_out, "q": self.q, "k": self.k, "gate": self.gate,
-               "up": self.up}
-        for k, v in self.h_in.items():
-            dev[k].copy_(v, non_blocking=True)
-        self.step()
-        out = {"x": self.x, "y1": self.y1, "h": self.h, "y2": self.y2, "qo": self.qo, "ko": self.ko,
-               "act": self.act}
-        for k, v in self.h_out.items():
-            v.copy_(out[k], non_blocking=True)
+    def _chunk(self, name: str, b0: int, b1: int):
+        seq = self.cfg["seq"]
+        t = getattr(self, name)
+        return t[b0:b1] if name in ("q", "k", "qo", "ko") else t[b0 * seq:b1 * seq]
+
+    def e2e_step(self, chunk: int = 1):
+        """Chunk c's H2D waits for the previous step's kernels on chunk c (its
+        inputs are being overwritten) and chunk c's kernels wait for the
+        previous step's D2H of chunk c (its outputs are being overwritten)."""
+        t = self.torch
+        B = self.cfg["batch"]
+        prev = getattr(self, "_prev_events", {})
+        cur = {}
+        for b0 in range(0, B, chunk):
+            b1 = min(B, b0 + chunk)
+            with t.cuda.stream(self.s_h2d):
+                if b0 in prev:
+                    self.s_h2d.wait_event(prev[b0][0])
+                for k, v in self.h_in.items():
+                    dev = self._chunk(k, b0, b1)
+                    dev.copy_(v[b0:b1] if k in ("q", "k") else v[b0 * self.cfg["seq"]:b1 * self.cfg["seq"]],
+                              non_blocking=True)
+                ev_in = t.cuda.Event()
+                ev_in.record(self.s_h2d)
+            self.s_comp.wait_event(ev_in)
+            if b0 in prev:
+                self.s_comp.wait_event(prev[b0][1])
+            for name in self.ops:
+                self.run_op(name, b0, b1)
+            ev_out = t.cuda.Event()
+            ev_out.record(self.s_comp)
+            with t.cuda.stream(self.s_d2h):
+                self.s_d2h.wait_event(ev_out)
+                for k, v in self.h_out.items():
+                    src = self._chunk(k, b0, b1)
+                    dst = v[b0:b1] if k in ("qo", "ko") else v[b0 * self.cfg["seq"]:b1 * self.cfg["seq"]]
+                    dst.copy_(src, non_blocking=True)
+                ev_d2h = t.cuda.Event()
+                ev_d2h.record(self.s_d2h)
+            cur[b0] = (ev_out, ev_d2h)
+        self._prev_events = cur
+        # The step ends when its last output is on the host.
+        self.s_comp.wait_stream(self.s_d2h)
 
 
 # ---------------------------------------------------------------------------
@@ -324,12 +378,11 @@ def run_reference(args, rank: int, world: int) -> None:
     print(json.dumps(line), flush=True)
 
 
-def config_block(n: int) -> dict:
-    return {"workload": "llama3-8b-shaped prefill layer ops (BASELINE config 4): embedding gather, RMSNorm, "
-                        "RoPE(Q,K), residual+RMSNorm, SwiGLU",
-            "batch_per_gpu": CFG["batch"], "seq_len": CFG["seq"], "hidden": CFG["hidden"],
-            "heads": "32q/8kv x 128", "intermediate": CFG["inter"], "vocab": CFG["vocab"],
-            "rows_per_gpu": CFG["batch"] * CFG["seq"], "global_batch": CFG["batch"] * n,
+def config_block(n: int, cfg: dict = CFG, ops=OPS) -> dict:
+    return {"workload": "llama3-8b-shaped prefill layer ops (benchmark config 4): " + ", ".join(ops),
+            "batch_per_gpu": cfg["batch"], "seq_len": cfg["seq"], "hidden": cfg["hidden"],
+            "heads": "32q/8kv x 128", "intermediate": cfg["inter"], "vocab": cfg["vocab"],
+            "rows_per_gpu": cfg["batch"] * cfg["seq"], "global_batch": cfg["batch"] * n,
             "parallelism": f"row-sharded x{n}, no collective", "l2": "inputs larger than L2 (126 MB), no flush"}
 
 
@@ -340,8 +393,11 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["xn", "reference"], default="xn")
     ap.add_argument("--cpu-rows", type=int, default=1024, help="token rows in the CPU sample step")
-    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--e2e-steps", type=int, default=5, help="0 skips the end-to-end measurement")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--rows", type=int, default=CFG["batch"] * CFG["seq"],
+                    help="token rows per GPU (a multiple of 4096; smaller values for profiling captures)")
+    ap.add_argument("--ops", default=",".join(OPS), help="comma-separated subset of " + ",".join(OPS))
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -364,7 +420,14 @@ def main() -> int:
 
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
     xn.lib()
-    wl = LlamaPrefillOps(torch, xn, dev, CFG, seed=1234 + rank)
+    ops = [o for o in args.ops.split(",") if o]
+    for o in ops:
+        if o not in OPS:
+            raise SystemExit(f"unknown op {o}")
+    if args.rows <= 0 or args.rows % CFG["seq"]:
+        raise SystemExit(f"--rows must be a positive multiple of {CFG['seq']}")
+    cfg = dict(CFG, batch=args.rows // CFG["seq"])
+    wl = LlamaPrefillOps(torch, xn, dev, cfg, seed=1234 + rank, ops=ops)
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
 
@@ -372,7 +435,7 @@ def main() -> int:
         wl.step()
     torch.cuda.synchronize()
 
-    events = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in OPS]
+    events = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in ops]
               for _ in range(args.steps)]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     uuid = None
@@ -397,23 +460,26 @@ def main() -> int:
     clocks = sampler.stop()
     elapsed_ms = start.elapsed_time(stop)
     per_op_ms = {name: statistics.mean(events[k][i][0].elapsed_time(events[k][i][1]) for k in range(args.steps))
-                 for i, name in enumerate(OPS)}
+                 for i, name in enumerate(ops)}
 
-    # End-to-end with host buffers.
-    wl.host_buffers()
-    torch.cuda.synchronize()
-    for _ in range(2):
-        wl.e2e_step()
-    torch.cuda.synchronize()
-    if distributed:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.e2e_steps):
-        wl.e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
+    # End-to-end with host buffers (timed on the compute stream, which waits
+    # for the last D2H copy of each step).
+    e2e_ms = float("nan")
+    if args.e2e_steps > 0:
+        wl.host_buffers()
+        torch.cuda.synchronize()
+        for _ in range(2):
+            wl.e2e_step()
+        torch.cuda.synchronize()
+        if distributed:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.e2e_steps):
+            wl.e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
 
     if distributed:
         t = torch.tensor([elapsed_ms, e2e_ms], dtype=torch.float64, device=dev)
@@ -433,18 +499,20 @@ def main() -> int:
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) activations, N(0,0.02) table, N(1,0.02) gains, uniform ids)",
-            "config": config_block(world),
+            "config": config_block(world, cfg, ops),
             "pct_of_hbm_peak": round(100.0 * value / world / peak, 1),
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": peak,
                          "peak_source": peak_src, "unit": "GB/s", "frac": round(achieved / peak, 3),
                          "traffic": traffic, "algorithmic_bytes": wl.bytes[dom]},
             "per_op": {n: {"ms": round(per_op_ms[n], 4), "bytes": wl.bytes[n],
                            "gbs": round(wl.bytes[n] / (per_op_ms[n] * 1e-3) / 1e9, 1),
-                           "frac": round(wl.bytes[n] / (per_op_ms[n] * 1e-3) / 1e9 / peak, 3)} for n in OPS},
-            "e2e": {"value": round(world * step_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": UNIT,
-                    "h2d_bytes_per_step": wl.h2d_bytes, "d2h_bytes_per_step": wl.d2h_bytes,
-                    "ms_per_step": round(e2e_ms, 3)},
-            "gpu_launches": len(OPS) * args.steps,
+                           "frac": round(wl.bytes[n] / (per_op_ms[n] * 1e-3) / 1e9 / peak, 3)} for n in ops},
+            "e2e": None if args.e2e_steps <= 0 else {
+                "value": round(world * step_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": UNIT,
+                "h2d_bytes_per_step": wl.h2d_bytes, "d2h_bytes_per_step": wl.d2h_bytes,
+                "ms_per_step": round(e2e_ms, 3),
+                "method": "per-sequence chunks; H2D, kernels and D2H on three streams"},
+            "gpu_launches": len(ops) * args.steps,
             "clocks": clocks,
         }
         if not args.no_cpu_baseline and world == 1:

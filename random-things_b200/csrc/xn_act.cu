@@ -8,6 +8,8 @@
 //
 // Design: 16-byte vector loads/stores, U accesses per thread issued before any
 // math so each thread keeps U*16 (or 2*U*16 for SwiGLU) bytes in flight.
+#include <type_traits>
+
 #include "xn_common.cuh"
 #include "xn_internal.h"
 
@@ -27,6 +29,34 @@ __device__ __forceinline__ float silu_t(float s) {
 __device__ __forceinline__ float gelu_erf(float x) {
   const float erf_val = erff(__fmul_rn(x, kFrac1Sqrt2));
   return __fmul_rn(__fmul_rn(x, 0.5f), __fadd_rn(1.f, erf_val));
+}
+
+// bf16 pairs with native bf16x2 arithmetic. For +, - and * of two bf16
+// values, one rounding of the exact result (the bf16x2 instructions) equals the
+// reference's f32 operation followed by rounding to bf16, so every step below
+// is the reference's step; the division uses div_for_bf16 (exact after the
+// final rounding to bf16).
+__device__ __forceinline__ __nv_bfloat162 silu_bf16x2(__nv_bfloat162 s) {
+  const float2 nf = __bfloat1622float2(__hneg2(s));  // T::zero() - s (exact)
+  const __nv_bfloat162 e = __floats2bfloat162_rn(expf(nf.x), expf(nf.y));
+  const __nv_bfloat162 d = __hadd2(__float2bfloat162_rn(1.f), e);  // T::one() + e
+  const float2 sf = __bfloat1622float2(s), df = __bfloat1622float2(d);
+  return __floats2bfloat162_rn(div_for_bf16(sf.x, df.x), div_for_bf16(sf.y, df.y));
+}
+
+__device__ __forceinline__ uint32_t bf2_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t *>(&v); }
+__device__ __forceinline__ __nv_bfloat162 bits_bf2(uint32_t w) { return *reinterpret_cast<__nv_bfloat162 *>(&w); }
+
+__device__ __forceinline__ uint4 silu_bf16x8(uint4 v) {
+  return make_uint4(bf2_bits(silu_bf16x2(bits_bf2(v.x))), bf2_bits(silu_bf16x2(bits_bf2(v.y))),
+                    bf2_bits(silu_bf16x2(bits_bf2(v.z))), bf2_bits(silu_bf16x2(bits_bf2(v.w))));
+}
+
+__device__ __forceinline__ uint4 swiglu_bf16x8(uint4 g, uint4 u) {
+  return make_uint4(bf2_bits(__hmul2(silu_bf16x2(bits_bf2(g.x)), bits_bf2(u.x))),
+                    bf2_bits(__hmul2(silu_bf16x2(bits_bf2(g.y)), bits_bf2(u.y))),
+                    bf2_bits(__hmul2(silu_bf16x2(bits_bf2(g.z)), bits_bf2(u.z))),
+                    bf2_bits(__hmul2(silu_bf16x2(bits_bf2(g.w)), bits_bf2(u.w))));
 }
 
 template <typename T, int OP>
@@ -59,11 +89,15 @@ __global__ void __launch_bounds__(kBlock) unary_kernel(void *dst, const void *sr
     for (int u = 0; u < kUnroll; ++u) {
       const int64_t i = base + u * kBlock;
       if (i < nacc) {
-        float v[N];
-        unpack<T>(raw[u], v);
+        if constexpr (std::is_same_v<T, __nv_bfloat16> && OP == XN_UNARY_SILU) {
+          st_vec(d + i * N, silu_bf16x8(raw[u]));
+        } else {
+          float v[N];
+          unpack<T>(raw[u], v);
 #pragma unroll
-        for (int j = 0; j < N; ++j) v[j] = unary_op<T, OP>(v[j]);
-        st_vec(d + i * N, pack<T>(v));
+          for (int j = 0; j < N; ++j) v[j] = unary_op<T, OP>(v[j]);
+          st_vec(d + i * N, pack<T>(v));
+        }
       }
     }
     // Ragged tail (< N elements), handled by block 0.
@@ -116,12 +150,16 @@ __global__ void __launch_bounds__(kBlock) swiglu_kernel(void *dst, const void *g
       for (int k = 0; k < kUnroll; ++k) {
         const int64_t i = c0 + k * kBlock;
         if (i < cacc) {
-          float vg[N], vu[N];
-          unpack<T>(rg[k], vg);
-          unpack<T>(ru[k], vu);
+          if constexpr (std::is_same_v<T, __nv_bfloat16>) {
+            st_vec(dr + i * N, swiglu_bf16x8(rg[k], ru[k]));
+          } else {
+            float vg[N], vu[N];
+            unpack<T>(rg[k], vg);
+            unpack<T>(ru[k], vu);
 #pragma unroll
-          for (int j = 0; j < N; ++j) vg[j] = __fmul_rn(Elem<T>::round(silu_t<T>(vg[j])), vu[j]);
-          st_vec(dr + i * N, pack<T>(vg));
+            for (int j = 0; j < N; ++j) vg[j] = __fmul_rn(Elem<T>::round(silu_t<T>(vg[j])), vu[j]);
+            st_vec(dr + i * N, pack<T>(vg));
+          }
         }
       }
     } else {

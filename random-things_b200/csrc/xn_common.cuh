@@ -216,6 +216,32 @@ __device__ __forceinline__ float group_max(float v, int tpr, float *red) {
   return s;
 }
 
+// ---------------------------------------------------------------------------
+// Division. The reference divides in f32 with IEEE round-to-nearest; these
+// helpers return the same f32 result more cheaply.
+// ---------------------------------------------------------------------------
+// x / d for many x and one d, given r = __frcp_rn(d) (correctly rounded 1/d):
+// q0 = RN(x*r) is within one ulp of x/d, rem = x - d*q0 is exact with an FMA,
+// and RN(q0 + rem*r) is the correctly rounded quotient (Markstein's theorem;
+// no overflow is possible where it is used: |x/d| stays far inside the f32
+// range). A zero q0 is kept as is so the sign of zero matches x / d.
+__device__ __forceinline__ float div_by(float x, float d, float r) {
+  const float q0 = __fmul_rn(x, r);
+  const float rem = __fmaf_rn(-d, q0, x);
+  const float q = __fmaf_rn(rem, r, q0);
+  return q0 == 0.f ? q0 : q;
+}
+
+// s / d where s and d are bf16 values and the quotient is then rounded to
+// bf16. For 8-bit significands s/d is never an exact bf16 rounding midpoint and
+// lies at least 2^-18 (relative) away from every midpoint, so a quotient with
+// relative error below 2^-21 (MUFU reciprocal + multiply) rounds to the same
+// bf16 value as the IEEE quotient. |s| < 64 keeps 1/d a normal number for the
+// d = 1 + exp(-s) this is used with; larger |s| take the IEEE division.
+__device__ __forceinline__ float div_for_bf16(float s, float d) {
+  return fabsf(s) < 64.f ? __fdividef(s, d) : __fdiv_rn(s, d);
+}
+
 __host__ __device__ __forceinline__ bool aligned16(const void *p) {
   return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
 }

@@ -63,9 +63,12 @@ struct Acc {
   }
 };
 
-// One row per row group, the row held in registers.
-template <typename T, bool kVector, int NV, bool kLN>
-__global__ void __launch_bounds__(1024) norm_regs_kernel(const NormParams p) {
+// One row per row group, the row held in registers. All loads of a thread
+// (src, then branch) are issued before any store, so each thread keeps NV (or
+// 2*NV) 16-byte loads in flight; stores of residual_out / dst come last, which
+// also makes exact aliasing of dst or residual_out with src safe.
+template <typename T, bool kVector, int NV, bool kLN, int kMaxBlock, bool kBranch>
+__global__ void __launch_bounds__(kMaxBlock) norm_regs_kernel(const NormParams p) {
   using A = Acc<T, kVector>;
   constexpr int N = A::N;
   __shared__ float red[32];
@@ -89,30 +92,39 @@ __global__ void __launch_bounds__(1024) norm_regs_kernel(const NormParams p) {
       for (int j = 0; j < N; ++j) h[k][j] = 0.f;
     }
   }
-  if (p.branch != nullptr) {
+  if constexpr (kBranch) {
+    float br[NV][N];
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int vi = lr + k * tpr;
+      if (active && vi < p.nvec) A::load_stream(p.branch, base + static_cast<int64_t>(vi) * N, br[k]);
+    }
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
       const int vi = lr + k * tpr;
       if (active && vi < p.nvec) {
-        const int64_t e = base + static_cast<int64_t>(vi) * N;
-        float br[N];
-        A::load_stream(p.branch, e, br);
         if (p.ls != nullptr) {
           float s[N];
           A::load_cached(p.ls, static_cast<int64_t>(vi) * N, s);
 #pragma unroll
-          for (int j = 0; j < N; ++j) br[j] = Elem<T>::round(__fmul_rn(br[j], s[j]));
+          for (int j = 0; j < N; ++j) br[k][j] = Elem<T>::round(__fmul_rn(br[k][j], s[j]));
         }
 #pragma unroll
-        for (int j = 0; j < N; ++j) h[k][j] = Elem<T>::round(__fadd_rn(h[k][j], br[j]));
-        if (p.res_out != nullptr) A::store(p.res_out, e, h[k]);
+        for (int j = 0; j < N; ++j) h[k][j] = Elem<T>::round(__fadd_rn(h[k][j], br[k][j]));
+      }
+    }
+    if (p.res_out != nullptr) {
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        const int vi = lr + k * tpr;
+        if (active && vi < p.nvec) A::store(p.res_out, base + static_cast<int64_t>(vi) * N, h[k]);
       }
     }
   }
 
   // 2) Row statistics in f32.
   const float cols_f = __ll2float_rn(p.cols);
-  float scale_a, shift_m;  // LN: inv_std, mean ; RMS: m (divisor), unused
+  float scale_a, shift_m, inv_m = 0.f;  // LN: inv_std, mean ; RMS: m, 1/m
   if constexpr (kLN) {
     float s = 0.f;
 #pragma unroll
@@ -144,6 +156,7 @@ __global__ void __launch_bounds__(1024) norm_regs_kernel(const NormParams p) {
       for (int j = 0; j < N; ++j) s = __fadd_rn(s, __fmul_rn(h[k][j], h[k][j]));
     s = group_sum(s, tpr, red);
     scale_a = __fsqrt_rn(__fadd_rn(__fdiv_rn(s, cols_f), p.eps));
+    inv_m = __frcp_rn(scale_a);
     shift_m = 0.f;
   }
 
@@ -174,8 +187,9 @@ __global__ void __launch_bounds__(1024) norm_regs_kernel(const NormParams p) {
           out[j] = __fadd_rn(__fmul_rn(__fmul_rn(c, scale_a), wv[j]), bv[j]);
         }
       } else {
+        // T(x / m * alpha): the IEEE quotient x / m via div_by, then * alpha.
 #pragma unroll
-        for (int j = 0; j < N; ++j) out[j] = __fmul_rn(__fdiv_rn(h[k][j], scale_a), wv[j]);
+        for (int j = 0; j < N; ++j) out[j] = __fmul_rn(div_by(h[k][j], scale_a, inv_m), wv[j]);
       }
       A::store(p.dst, base + col, out);
     }
@@ -234,23 +248,54 @@ __global__ void __launch_bounds__(1024) norm_loop_kernel(const NormParams p) {
   }
 }
 
-template <typename T, bool kVector, bool kLN>
-void launch_regs(NormParams p, int nv, int block, int64_t grid, cudaStream_t st) {
+// Per-thread register budget for row values: 32 without a branch, 16 with one
+// (the branch values are held too). Only shapes within it are instantiated.
+template <int N, bool kBranch>
+constexpr int kMaxNv = ((kBranch ? 16 : 32) / N) < 8 ? ((kBranch ? 16 : 32) / N) : 8;
+
+// Returns false when no instantiated kernel has this shape (a dispatcher bug).
+template <typename T, bool kVector, bool kLN, int kMaxBlock, bool kBranch>
+bool launch_regs_b(NormParams p, int nv, int block, int64_t grid, cudaStream_t st) {
   constexpr int N = Acc<T, kVector>::N;
+  constexpr int cap = kMaxNv<N, kBranch>;
   switch (nv) {
     case 1:
-      norm_regs_kernel<T, kVector, 1, kLN><<<grid, block, 0, st>>>(p);
-      break;
+      norm_regs_kernel<T, kVector, 1, kLN, kMaxBlock, kBranch><<<grid, block, 0, st>>>(p);
+      return true;
     case 2:
-      norm_regs_kernel<T, kVector, 2, kLN><<<grid, block, 0, st>>>(p);
-      break;
+      if constexpr (cap >= 2) {
+        norm_regs_kernel<T, kVector, 2, kLN, kMaxBlock, kBranch><<<grid, block, 0, st>>>(p);
+        return true;
+      }
+      return false;
     case 4:
-      norm_regs_kernel<T, kVector, 4, kLN><<<grid, block, 0, st>>>(p);
-      break;
+      if constexpr (cap >= 4) {
+        norm_regs_kernel<T, kVector, 4, kLN, kMaxBlock, kBranch><<<grid, block, 0, st>>>(p);
+        return true;
+      }
+      return false;
+    case 8:
+      if constexpr (cap >= 8) {
+        norm_regs_kernel<T, kVector, 8, kLN, kMaxBlock, kBranch><<<grid, block, 0, st>>>(p);
+        return true;
+      }
+      return false;
     default:
-      if constexpr (8 * N <= 32) norm_regs_kernel<T, kVector, 8, kLN><<<grid, block, 0, st>>>(p);
-      break;
+      return false;
   }
+}
+
+// Blocks of 256 threads (row groups up to 256) may use more registers per
+// thread than the 1024-thread shape needed by the widest rows.
+template <typename T, bool kVector, bool kLN>
+bool launch_regs(NormParams p, int nv, int block, int64_t grid, cudaStream_t st) {
+  const bool branch = p.branch != nullptr;
+  if (block <= 256) {
+    return branch ? launch_regs_b<T, kVector, kLN, 256, true>(p, nv, block, grid, st)
+                  : launch_regs_b<T, kVector, kLN, 256, false>(p, nv, block, grid, st);
+  }
+  return branch ? launch_regs_b<T, kVector, kLN, 1024, true>(p, nv, block, grid, st)
+                : launch_regs_b<T, kVector, kLN, 1024, false>(p, nv, block, grid, st);
 }
 
 // Chooses the row-group shape and launches. Register budget: <= 32 f32 values
@@ -263,9 +308,15 @@ int launch_norm(NormParams p, cudaStream_t st, const char *op) {
                    is_aligned16(p.ls) && is_aligned16(p.res_out);
   const int n = vec ? V : 1;
   const int64_t nvec = p.cols / n;
-  const int nv_cap = (32 / n) < 8 ? (32 / n) : 8;
+  // Up to 32 row values per thread (16 with a branch, which doubles the
+  // loads held in registers): rows of up to 32768 (16384) elements.
+  const int per_thread = p.branch != nullptr ? 16 : 32;
+  const int nv_cap = (per_thread / n) < 8 ? (per_thread / n) : 8;  // a power of two
   if (nvec <= 1024LL * nv_cap) {
-    int64_t tpr = pow2_ceil(ceil_div(nvec, 4));
+    // Aim for 4 accesses per thread (fewer if the budget is smaller); then
+    // nv <= nv_cap holds by construction.
+    const int target = nv_cap < 4 ? nv_cap : 4;
+    int64_t tpr = pow2_ceil(ceil_div(nvec, target));
     if (tpr > 1024) tpr = 1024;
     const int nv = static_cast<int>(pow2_ceil(ceil_div(nvec, tpr)));
     const int block = tpr < 256 ? 256 : static_cast<int>(tpr);
@@ -274,10 +325,9 @@ int launch_norm(NormParams p, cudaStream_t st, const char *op) {
     if (grid > 0x7fffffffLL) return fail(XN_E_INVALID, "%s: too many rows (%lld)", op, (long long)p.rows);
     p.tpr = static_cast<int>(tpr);
     p.nvec = static_cast<int>(nvec);
-    if (vec)
-      launch_regs<T, true, kLN>(p, nv, block, grid, st);
-    else
-      launch_regs<T, false, kLN>(p, nv, block, grid, st);
+    const bool launched =
+        vec ? launch_regs<T, true, kLN>(p, nv, block, grid, st) : launch_regs<T, false, kLN>(p, nv, block, grid, st);
+    if (!launched) return fail(XN_E_INVALID, "%s: internal error, no kernel for %d accesses per thread", op, nv);
   } else {
     if (p.rows > 0x7fffffffLL) return fail(XN_E_INVALID, "%s: too many rows (%lld)", op, (long long)p.rows);
     norm_loop_kernel<T, kLN><<<static_cast<unsigned>(p.rows), 1024, 0, st>>>(p);

@@ -12,6 +12,8 @@
 // cos/sin chunk is loaded once and reused for several heads. Lanes of a warp
 // own consecutive chunks, so every global access is a full 16-byte vector and
 // warps touch contiguous 128-byte segments.
+#include <type_traits>
+
 #include "xn_common.cuh"
 #include "xn_internal.h"
 
@@ -36,6 +38,47 @@ struct RopeParams {
   int64_t pos;
   int layout;
 };
+
+constexpr int kMaxHpt = 4;  // heads per thread (cos/sin reuse, loads in flight)
+
+// Half-split rotation of one 16-byte chunk of each half:
+//   y1 = T(T(x1*c) - T(x2*s)),  y2 = T(T(x1*s) + T(x2*c)).
+// bf16 / f16 use the native paired instructions, which round each product and
+// sum once, exactly as the reference's T arithmetic does (the product of two
+// 8- or 11-bit significands is exact in f32; see xn_act.cu for the sum).
+template <typename T>
+__device__ __forceinline__ void rotate_halfsplit(const uint4 &x1, const uint4 &x2, const uint4 &c, const uint4 &s,
+                                                 uint4 &y1, uint4 &y2) {
+  if constexpr (std::is_same_v<T, float>) {
+    float a[4], b[4], cv[4], sv[4], o1[4], o2[4];
+    unpack<T>(x1, a);
+    unpack<T>(x2, b);
+    unpack<T>(c, cv);
+    unpack<T>(s, sv);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      o1[j] = __fsub_rn(__fmul_rn(a[j], cv[j]), __fmul_rn(b[j], sv[j]));
+      o2[j] = __fadd_rn(__fmul_rn(a[j], sv[j]), __fmul_rn(b[j], cv[j]));
+    }
+    y1 = pack<T>(o1);
+    y2 = pack<T>(o2);
+  } else {
+    using T2 = std::conditional_t<std::is_same_v<T, __half>, __half2, __nv_bfloat162>;
+    const uint32_t *pa = &x1.x, *pb = &x2.x, *pc = &c.x, *ps = &s.x;
+    uint32_t o1[4], o2[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const T2 a = *reinterpret_cast<const T2 *>(pa + j), b = *reinterpret_cast<const T2 *>(pb + j);
+      const T2 cv = *reinterpret_cast<const T2 *>(pc + j), sv = *reinterpret_cast<const T2 *>(ps + j);
+      const T2 r1 = __hsub2(__hmul2(a, cv), __hmul2(b, sv));
+      const T2 r2 = __hadd2(__hmul2(a, sv), __hmul2(b, cv));
+      o1[j] = *reinterpret_cast<const uint32_t *>(&r1);
+      o2[j] = *reinterpret_cast<const uint32_t *>(&r2);
+    }
+    y1 = make_uint4(o1[0], o1[1], o1[2], o1[3]);
+    y2 = make_uint4(o2[0], o2[1], o2[2], o2[3]);
+  }
+}
 
 template <typename T, bool kInterleaved, bool kVector>
 __global__ void __launch_bounds__(256) rope_kernel(const RopeParams p) {
@@ -75,49 +118,58 @@ __global__ void __launch_bounds__(256) rope_kernel(const RopeParams p) {
   const T *sn = static_cast<const T *>(p.sin);
 
   if constexpr (kVector && !kInterleaved) {
-    // chunk c: elements [c*V, c*V+V) of each half.
-    float cv[V], sv[V];
-    unpack<T>(ld_cached(cs + trow + c * V), cv);
-    unpack<T>(ld_cached(sn + trow + c * V), sv);
-    for (uint32_t hh = 0; hh < p.hpt; ++hh) {
-      const uint32_t h = hg * p.hpt + hh;
-      if (h >= H) break;
-      const int64_t e1 = row0 + h * head_stride + c * V;
-      const int64_t e2 = e1 + half;
-      float x1[V], x2[V], y1[V], y2[V];
-      unpack<T>(ld_stream(src + e1), x1);
-      unpack<T>(ld_stream(src + e2), x2);
+    // chunk c: elements [c*V, c*V+V) of each half. All heads' loads first.
+    uint4 r1[kMaxHpt], r2[kMaxHpt];
 #pragma unroll
-      for (int j = 0; j < V; ++j) {
-        y1[j] = Elem<T>::round(__fsub_rn(Elem<T>::round(__fmul_rn(x1[j], cv[j])),
-                                         Elem<T>::round(__fmul_rn(x2[j], sv[j]))));
-        y2[j] = Elem<T>::round(__fadd_rn(Elem<T>::round(__fmul_rn(x1[j], sv[j])),
-                                         Elem<T>::round(__fmul_rn(x2[j], cv[j]))));
+    for (int hh = 0; hh < kMaxHpt; ++hh) {
+      const uint32_t h = hg * p.hpt + hh;
+      if (hh < static_cast<int>(p.hpt) && h < H) {
+        const int64_t e1 = row0 + h * head_stride + c * V;
+        r1[hh] = ld_stream(src + e1);
+        r2[hh] = ld_stream(src + e1 + half);
       }
-      st_vec(dst + e1, pack<T>(y1));
-      st_vec(dst + e2, pack<T>(y2));
+    }
+    const uint4 cr = ld_cached(cs + trow + c * V);
+    const uint4 sr = ld_cached(sn + trow + c * V);
+#pragma unroll
+    for (int hh = 0; hh < kMaxHpt; ++hh) {
+      const uint32_t h = hg * p.hpt + hh;
+      if (hh < static_cast<int>(p.hpt) && h < H) {
+        const int64_t e1 = row0 + h * head_stride + c * V;
+        uint4 y1, y2;
+        rotate_halfsplit<T>(r1[hh], r2[hh], cr, sr, y1, y2);
+        st_vec(dst + e1, y1);
+        st_vec(dst + e1 + half, y2);
+      }
     }
   } else if constexpr (kVector && kInterleaved) {
     // chunk c: elements [c*V, c*V+V) = pairs [c*V/2, c*V/2 + V/2).
     constexpr int P = V / 2;
+    uint4 rx[kMaxHpt];
+#pragma unroll
+    for (int hh = 0; hh < kMaxHpt; ++hh) {
+      const uint32_t h = hg * p.hpt + hh;
+      if (hh < static_cast<int>(p.hpt) && h < H) rx[hh] = ld_stream(src + row0 + h * head_stride + c * V);
+    }
     float cv[P], sv[P];
     unpack_half<T>(ld_cached8(cs + trow + c * P), cv);
     unpack_half<T>(ld_cached8(sn + trow + c * P), sv);
-    for (uint32_t hh = 0; hh < p.hpt; ++hh) {
-      const uint32_t h = hg * p.hpt + hh;
-      if (h >= H) break;
-      const int64_t e = row0 + h * head_stride + c * V;
-      float x[V], y[V];
-      unpack<T>(ld_stream(src + e), x);
 #pragma unroll
-      for (int j = 0; j < P; ++j) {
-        const float a = x[2 * j], b = x[2 * j + 1];
-        y[2 * j] = Elem<T>::round(__fsub_rn(Elem<T>::round(__fmul_rn(a, cv[j])),
-                                            Elem<T>::round(__fmul_rn(b, sv[j]))));
-        y[2 * j + 1] = Elem<T>::round(__fadd_rn(Elem<T>::round(__fmul_rn(a, sv[j])),
-                                                Elem<T>::round(__fmul_rn(b, cv[j]))));
+    for (int hh = 0; hh < kMaxHpt; ++hh) {
+      const uint32_t h = hg * p.hpt + hh;
+      if (hh < static_cast<int>(p.hpt) && h < H) {
+        float x[V], y[V];
+        unpack<T>(rx[hh], x);
+#pragma unroll
+        for (int j = 0; j < P; ++j) {
+          const float a = x[2 * j], b = x[2 * j + 1];
+          y[2 * j] = Elem<T>::round(__fsub_rn(Elem<T>::round(__fmul_rn(a, cv[j])),
+                                              Elem<T>::round(__fmul_rn(b, sv[j]))));
+          y[2 * j + 1] = Elem<T>::round(__fadd_rn(Elem<T>::round(__fmul_rn(a, sv[j])),
+                                                  Elem<T>::round(__fmul_rn(b, cv[j]))));
+        }
+        st_vec(dst + row0 + h * head_stride + c * V, pack<T>(y));
       }
-      st_vec(dst + e, pack<T>(y));
     }
   } else {
     // Scalar fallback: chunk c is one pair (element c of each half, or pair c).
@@ -157,7 +209,7 @@ int launch_rope(const RopeJob &job, const void *cos, const void *sin, int64_t b,
   const int64_t chunks = vec ? (interleaved ? d / V : half / V) : half;
   int64_t max_heads = 0;
   for (int i = 0; i < job.n; ++i) max_heads = job.heads[i] > max_heads ? job.heads[i] : max_heads;
-  const int64_t hpt = max_heads >= 4 ? 4 : (max_heads > 0 ? max_heads : 1);
+  const int64_t hpt = max_heads >= kMaxHpt ? kMaxHpt : (max_heads > 0 ? max_heads : 1);
   // Work items per batch element for each tensor; launch over batch slices so
   // each launch indexes its items with 32-bit integers.
   int64_t per_b = 0;

@@ -90,6 +90,7 @@ __global__ void __launch_bounds__(512) softmax_regs_kernel(const SoftmaxParams p
     }
   }
   s = group_sum(s, tpr, red);
+  const float rs = __frcp_rn(s);  // s >= 1: the row maximum contributes exp(0)
 #pragma unroll
   for (int k = 0; k < NV; ++k) {
     const int vi = lr + k * tpr;
@@ -97,7 +98,7 @@ __global__ void __launch_bounds__(512) softmax_regs_kernel(const SoftmaxParams p
       const int64_t e0 = static_cast<int64_t>(vi) * N;
       float y[N];
 #pragma unroll
-      for (int j = 0; j < N; ++j) y[j] = e0 + j < lim ? __fdiv_rn(x[k][j], s) : 0.f;
+      for (int j = 0; j < N; ++j) y[j] = e0 + j < lim ? div_by(x[k][j], s, rs) : 0.f;
       if constexpr (kVector) {
         st_vec(dst + base + e0, pack<T>(y));
       } else {
@@ -135,22 +136,28 @@ __global__ void __launch_bounds__(1024) softmax_loop_kernel(const SoftmaxParams 
     dst[base + c] = Elem<T>::from_f32(__fdiv_rn(Elem<T>::to_f32(dst[base + c]), s));
 }
 
+// Returns false when no instantiated kernel has this shape (a dispatcher bug).
 template <typename T, bool kVector>
-void launch_softmax_regs(const SoftmaxParams &p, int nv, int block, int64_t grid, cudaStream_t st) {
+bool launch_softmax_regs(const SoftmaxParams &p, int nv, int block, int64_t grid, cudaStream_t st) {
   constexpr int N = kVector ? Elem<T>::kVec : 1;
   switch (nv) {
     case 1:
       softmax_regs_kernel<T, kVector, 1><<<grid, block, 0, st>>>(p);
-      break;
+      return true;
     case 2:
       softmax_regs_kernel<T, kVector, 2><<<grid, block, 0, st>>>(p);
-      break;
+      return true;
     case 4:
       softmax_regs_kernel<T, kVector, 4><<<grid, block, 0, st>>>(p);
-      break;
+      return true;
+    case 8:
+      if constexpr (8 * N <= 32) {
+        softmax_regs_kernel<T, kVector, 8><<<grid, block, 0, st>>>(p);
+        return true;
+      }
+      return false;
     default:
-      if constexpr (8 * N <= 32) softmax_regs_kernel<T, kVector, 8><<<grid, block, 0, st>>>(p);
-      break;
+      return false;
   }
 }
 
@@ -172,10 +179,9 @@ int launch_softmax(SoftmaxParams p, cudaStream_t st) {
     if (grid > 0x7fffffffLL) return fail(XN_E_INVALID, "xn_softmax: too many rows");
     p.tpr = static_cast<int>(tpr);
     p.nvec = static_cast<int>(nvec);
-    if (vec)
-      launch_softmax_regs<T, true>(p, nv, block, grid, st);
-    else
-      launch_softmax_regs<T, false>(p, nv, block, grid, st);
+    const bool launched = vec ? launch_softmax_regs<T, true>(p, nv, block, grid, st)
+                              : launch_softmax_regs<T, false>(p, nv, block, grid, st);
+    if (!launched) return fail(XN_E_INVALID, "xn_softmax: internal error, no kernel for %d accesses per thread", nv);
   } else {
     if (p.rows > 0x7fffffffLL) return fail(XN_E_INVALID, "xn_softmax: too many rows");
     softmax_loop_kernel<T><<<static_cast<unsigned>(p.rows), 1024, 0, st>>>(p);

@@ -88,7 +88,7 @@ def test_norm_misaligned_and_inplace(oracle, xn, cuda, dtype):
 
 
 def test_norm_config_shapes(oracle, xn, cuda):
-    """BASELINE config 1 (f32 RMSNorm [1,512,2048]) and config 2 (LN + layer-scale
+    """Benchmark config 1 (f32 RMSNorm [1,512,2048]) and config 2 (LN + layer-scale
     + residual on [4,250,512], f32 and bf16)."""
     r = rng(100)
     x = randn(r, (1, 512, 2048))

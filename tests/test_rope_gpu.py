@@ -10,7 +10,7 @@ from helpers import from_device, randn, rng, to_device, to_storage
 pytestmark = pytest.mark.gpu
 
 DTYPES = ["f32", "bf16", "f16"]
-# (b, h, t, d, pos, max_pos): BASELINE config 1 (Q/K 16x128 heads), config 2
+# (b, h, t, d, pos, max_pos): benchmark config 1 (Q/K 16x128 heads), config 2
 # (8x64, 250 frames), config 3 decode (t=1 at a position), config 4-like heads,
 # and ragged half-dims that take the scalar path.
 SHAPES = [
