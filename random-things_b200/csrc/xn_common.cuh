@@ -79,6 +79,16 @@ __device__ __forceinline__ uint4 ld_plain(const void *p) {
 
 __device__ __forceinline__ void st_vec(void *p, uint4 v) { *reinterpret_cast<uint4 *>(p) = v; }
 
+// Returns v unchanged through moves the compiler cannot see through. Used to
+// make a second pass over packed register data unpack it again instead of
+// keeping the first pass's unpacked f32 copies live (which doubles register
+// use for 16-bit rows).
+__device__ __forceinline__ uint4 opaque(uint4 v) {
+  asm volatile("mov.b32 %0, %0;\n\tmov.b32 %1, %1;\n\tmov.b32 %2, %2;\n\tmov.b32 %3, %3;"
+               : "+r"(v.x), "+r"(v.y), "+r"(v.z), "+r"(v.w));
+  return v;
+}
+
 // Unpack / pack 16 bytes as kVec values of T widened to f32.
 template <typename T>
 __device__ __forceinline__ void unpack(const uint4 &v, float (&f)[Elem<T>::kVec]);
@@ -232,14 +242,20 @@ __device__ __forceinline__ float div_by(float x, float d, float r) {
   return q0 == 0.f ? q0 : q;
 }
 
-// s / d where s and d are bf16 values and the quotient is then rounded to
-// bf16. For 8-bit significands s/d is never an exact bf16 rounding midpoint and
-// lies at least 2^-18 (relative) away from every midpoint, so a quotient with
-// relative error below 2^-21 (MUFU reciprocal + multiply) rounds to the same
-// bf16 value as the IEEE quotient. |s| < 64 keeps 1/d a normal number for the
-// d = 1 + exp(-s) this is used with; larger |s| take the IEEE division.
+// s / d where s and d are bf16 values, d >= 1, and the quotient is then
+// rounded to bf16. For 8-bit significands s/d is never an exact bf16 rounding
+// midpoint: s = m*d with m a 9-bit odd significand would need the odd part of
+// m*d (>= 257) to equal the odd part of s (<= 255). The quotient is in fact at
+// least 2^-18 (relative) away from every midpoint, so a quotient with relative
+// error below 2^-21 (__fdividef: MUFU reciprocal + multiply, 2 ulp) rounds to
+// the same bf16 value as the IEEE quotient, and so does the IEEE quotient
+// rounded first to f32 (the reference's path). __fdividef needs |d| < 2^126:
+// larger d (only when exp overflows bf16's range, s < -87) are brought into
+// range by scaling both operands by 2^-64, which is exact there; d = inf gives
+// the IEEE result -0 / +0.
 __device__ __forceinline__ float div_for_bf16(float s, float d) {
-  return fabsf(s) < 64.f ? __fdividef(s, d) : __fdiv_rn(s, d);
+  const float sc = d > 0x1p126f ? 0x1p-64f : 1.f;
+  return __fdividef(__fmul_rn(s, sc), __fmul_rn(d, sc));
 }
 
 __host__ __device__ __forceinline__ bool aligned16(const void *p) {

@@ -12,8 +12,10 @@
 // thread), so every tensor crosses HBM exactly once: read src (+ branch),
 // write residual_out (+ dst). The reductions are f32 shuffles inside the group
 // (plus one shared-memory step when the group spans several warps). Rows too
-// wide for registers (> 32768 elements) use a multi-pass kernel that re-reads
-// the row (served from L2 for rows up to a few hundred KB).
+// wide for registers (more than 4096 16-byte vectors: 32768 bf16 / 16384 f32
+// elements) use a multi-pass kernel that re-reads the row from L2.
+#include <type_traits>
+
 #include "xn_common.cuh"
 #include "xn_internal.h"
 
@@ -63,14 +65,18 @@ struct Acc {
   }
 };
 
-// One row per row group, the row held in registers. All loads of a thread
-// (src, then branch) are issued before any store, so each thread keeps NV (or
-// 2*NV) 16-byte loads in flight; stores of residual_out / dst come last, which
-// also makes exact aliasing of dst or residual_out with src safe.
+// One row per row group, the row held in registers as raw 16-byte vectors
+// (packed T), which halves the registers a bf16 / f16 row needs and lets each
+// thread keep up to 8 loads in flight. All loads of a thread (src, then
+// branch) are issued before any store; stores of residual_out / dst come last,
+// which also makes exact aliasing of dst or residual_out with src safe.
+// 256-thread blocks are held to 64 registers so four fit on an SM (1024
+// threads, each with up to 8 x 16-byte loads in flight); LayerNorm with 8
+// accesses per thread needs a few more and runs three blocks per SM.
 template <typename T, bool kVector, int NV, bool kLN, int kMaxBlock, bool kBranch>
-__global__ void __launch_bounds__(kMaxBlock) norm_regs_kernel(const NormParams p) {
-  using A = Acc<T, kVector>;
-  constexpr int N = A::N;
+__global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? ((kLN && NV == 8) ? 3 : 4) : 1) norm_regs_kernel(const NormParams p) {
+  constexpr int N = Acc<T, kVector>::N;
+  using Raw = std::conditional_t<kVector, uint4, T>;
   __shared__ float red[32];
   const int tpr = p.tpr;
   const int g = threadIdx.x / tpr;
@@ -79,45 +85,81 @@ __global__ void __launch_bounds__(kMaxBlock) norm_regs_kernel(const NormParams p
   const int64_t row = static_cast<int64_t>(blockIdx.x) * rpb + g;
   const bool active = row < p.rows;
   const int64_t base = row * p.cols;
+  const Raw *src = reinterpret_cast<const Raw *>(static_cast<const T *>(p.src) + base);
 
-  // 1) h = src (+ T(branch * ls)), rounded to T after each op, kept in registers.
-  float h[NV][N];
+  auto unpack_raw = [](const Raw &r, float (&f)[N]) {
+    if constexpr (kVector) {
+      unpack<T>(r, f);
+    } else {
+      f[0] = Elem<T>::to_f32(r);
+    }
+  };
+  auto pack_raw = [](const float (&f)[N]) -> Raw {
+    if constexpr (kVector) {
+      return pack<T>(f);
+    } else {
+      return Elem<T>::from_f32(f[0]);
+    }
+  };
+  // Second and third passes re-unpack the packed row (see opaque()).
+  auto unpack_again = [](const Raw &r, float (&f)[N]) {
+    if constexpr (kVector) {
+      unpack<T>(opaque(r), f);
+    } else {
+      f[0] = Elem<T>::to_f32(r);
+    }
+  };
+  auto load_raw = [](const Raw *ptr) -> Raw {
+    if constexpr (kVector) {
+      return ld_stream(ptr);
+    } else {
+      return *ptr;
+    }
+  };
+
+  // 1) h = src (+ T(branch * ls)), each op rounded to T, kept as packed T.
+  Raw h[NV];
 #pragma unroll
   for (int k = 0; k < NV; ++k) {
     const int vi = lr + k * tpr;
     if (active && vi < p.nvec) {
-      A::load_stream(p.src, base + static_cast<int64_t>(vi) * N, h[k]);
+      h[k] = load_raw(src + vi);
     } else {
-#pragma unroll
-      for (int j = 0; j < N; ++j) h[k][j] = 0.f;
+      h[k] = Raw{};
     }
   }
   if constexpr (kBranch) {
-    float br[NV][N];
+    const Raw *br = reinterpret_cast<const Raw *>(static_cast<const T *>(p.branch) + base);
+    Raw b[NV];
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
       const int vi = lr + k * tpr;
-      if (active && vi < p.nvec) A::load_stream(p.branch, base + static_cast<int64_t>(vi) * N, br[k]);
+      if (active && vi < p.nvec) b[k] = load_raw(br + vi);
     }
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
       const int vi = lr + k * tpr;
       if (active && vi < p.nvec) {
+        float x[N], y[N];
+        unpack_raw(h[k], x);
+        unpack_raw(b[k], y);
         if (p.ls != nullptr) {
           float s[N];
-          A::load_cached(p.ls, static_cast<int64_t>(vi) * N, s);
+          Acc<T, kVector>::load_cached(p.ls, static_cast<int64_t>(vi) * N, s);
 #pragma unroll
-          for (int j = 0; j < N; ++j) br[k][j] = Elem<T>::round(__fmul_rn(br[k][j], s[j]));
+          for (int j = 0; j < N; ++j) y[j] = Elem<T>::round(__fmul_rn(y[j], s[j]));
         }
 #pragma unroll
-        for (int j = 0; j < N; ++j) h[k][j] = Elem<T>::round(__fadd_rn(h[k][j], br[k][j]));
+        for (int j = 0; j < N; ++j) x[j] = __fadd_rn(x[j], y[j]);
+        h[k] = pack_raw(x);  // rounds each sum to T
       }
     }
     if (p.res_out != nullptr) {
+      Raw *ro = reinterpret_cast<Raw *>(static_cast<T *>(p.res_out) + base);
 #pragma unroll
       for (int k = 0; k < NV; ++k) {
         const int vi = lr + k * tpr;
-        if (active && vi < p.nvec) A::store(p.res_out, base + static_cast<int64_t>(vi) * N, h[k]);
+        if (active && vi < p.nvec) ro[vi] = h[k];
       }
     }
   }
@@ -128,18 +170,23 @@ __global__ void __launch_bounds__(kMaxBlock) norm_regs_kernel(const NormParams p
   if constexpr (kLN) {
     float s = 0.f;
 #pragma unroll
-    for (int k = 0; k < NV; ++k)
+    for (int k = 0; k < NV; ++k) {
+      float x[N];
+      unpack_raw(h[k], x);
 #pragma unroll
-      for (int j = 0; j < N; ++j) s = __fadd_rn(s, h[k][j]);
+      for (int j = 0; j < N; ++j) s = __fadd_rn(s, x[j]);
+    }
     s = group_sum(s, tpr, red);
     const float mean = __fdiv_rn(s, cols_f);
     float v = 0.f;
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
       if (lr + k * tpr < p.nvec) {
+        float x[N];
+        unpack_again(h[k], x);
 #pragma unroll
         for (int j = 0; j < N; ++j) {
-          const float d = __fsub_rn(h[k][j], mean);
+          const float d = __fsub_rn(x[j], mean);
           v = __fadd_rn(v, __fmul_rn(d, d));
         }
       }
@@ -151,9 +198,12 @@ __global__ void __launch_bounds__(kMaxBlock) norm_regs_kernel(const NormParams p
   } else {
     float s = 0.f;
 #pragma unroll
-    for (int k = 0; k < NV; ++k)
+    for (int k = 0; k < NV; ++k) {
+      float x[N];
+      unpack_raw(h[k], x);
 #pragma unroll
-      for (int j = 0; j < N; ++j) s = __fadd_rn(s, __fmul_rn(h[k][j], h[k][j]));
+      for (int j = 0; j < N; ++j) s = __fadd_rn(s, __fmul_rn(x[j], x[j]));
+    }
     s = group_sum(s, tpr, red);
     scale_a = __fsqrt_rn(__fadd_rn(__fdiv_rn(s, cols_f), p.eps));
     inv_m = __frcp_rn(scale_a);
@@ -161,14 +211,16 @@ __global__ void __launch_bounds__(kMaxBlock) norm_regs_kernel(const NormParams p
   }
 
   // 3) Epilogue: dst = T(norm(h) * w (+ b)).
+  Raw *dst = reinterpret_cast<Raw *>(static_cast<T *>(p.dst) + base);
 #pragma unroll
   for (int k = 0; k < NV; ++k) {
     const int vi = lr + k * tpr;
     if (active && vi < p.nvec) {
       const int64_t col = static_cast<int64_t>(vi) * N;
-      float wv[N], out[N];
+      float x[N], wv[N], out[N];
+      unpack_again(h[k], x);
       if (p.w != nullptr) {
-        A::load_cached(p.w, col, wv);
+        Acc<T, kVector>::load_cached(p.w, col, wv);
       } else {
 #pragma unroll
         for (int j = 0; j < N; ++j) wv[j] = 1.f;
@@ -176,22 +228,22 @@ __global__ void __launch_bounds__(kMaxBlock) norm_regs_kernel(const NormParams p
       if constexpr (kLN) {
         float bv[N];
         if (p.b != nullptr) {
-          A::load_cached(p.b, col, bv);
+          Acc<T, kVector>::load_cached(p.b, col, bv);
         } else {
 #pragma unroll
           for (int j = 0; j < N; ++j) bv[j] = 0.f;
         }
 #pragma unroll
         for (int j = 0; j < N; ++j) {
-          const float c = p.remove_mean ? __fsub_rn(h[k][j], shift_m) : h[k][j];
+          const float c = p.remove_mean ? __fsub_rn(x[j], shift_m) : x[j];
           out[j] = __fadd_rn(__fmul_rn(__fmul_rn(c, scale_a), wv[j]), bv[j]);
         }
       } else {
         // T(x / m * alpha): the IEEE quotient x / m via div_by, then * alpha.
 #pragma unroll
-        for (int j = 0; j < N; ++j) out[j] = __fmul_rn(div_by(h[k][j], scale_a, inv_m), wv[j]);
+        for (int j = 0; j < N; ++j) out[j] = __fmul_rn(div_by(x[j], scale_a, inv_m), wv[j]);
       }
-      A::store(p.dst, base + col, out);
+      dst[vi] = pack_raw(out);
     }
   }
 }
@@ -248,16 +300,17 @@ __global__ void __launch_bounds__(1024) norm_loop_kernel(const NormParams p) {
   }
 }
 
-// Per-thread register budget for row values: 32 without a branch, 16 with one
-// (the branch values are held too). Only shapes within it are instantiated.
-template <int N, bool kBranch>
-constexpr int kMaxNv = ((kBranch ? 16 : 32) / N) < 8 ? ((kBranch ? 16 : 32) / N) : 8;
+// Accesses per thread: up to 8 in 256-thread blocks (4 with a branch, whose
+// vectors are held too) and up to 4 in the 1024-thread shape used for the
+// widest rows. Only shapes within the cap are instantiated.
+template <int N, bool kBranch, int kMaxBlock>
+constexpr int kMaxNv = (kBranch || kMaxBlock > 256) ? 4 : 8;
 
 // Returns false when no instantiated kernel has this shape (a dispatcher bug).
 template <typename T, bool kVector, bool kLN, int kMaxBlock, bool kBranch>
 bool launch_regs_b(NormParams p, int nv, int block, int64_t grid, cudaStream_t st) {
   constexpr int N = Acc<T, kVector>::N;
-  constexpr int cap = kMaxNv<N, kBranch>;
+  constexpr int cap = kMaxNv<N, kBranch, kMaxBlock>;
   switch (nv) {
     case 1:
       norm_regs_kernel<T, kVector, 1, kLN, kMaxBlock, kBranch><<<grid, block, 0, st>>>(p);
@@ -310,14 +363,17 @@ int launch_norm(NormParams p, cudaStream_t st, const char *op) {
   const int64_t nvec = p.cols / n;
   // Up to 32 row values per thread (16 with a branch, which doubles the
   // loads held in registers): rows of up to 32768 (16384) elements.
-  const int per_thread = p.branch != nullptr ? 16 : 32;
-  const int nv_cap = (per_thread / n) < 8 ? (per_thread / n) : 8;  // a power of two
-  if (nvec <= 1024LL * nv_cap) {
-    // Aim for 4 accesses per thread (fewer if the budget is smaller); then
-    // nv <= nv_cap holds by construction.
-    const int target = nv_cap < 4 ? nv_cap : 4;
-    int64_t tpr = pow2_ceil(ceil_div(nvec, target));
-    if (tpr > 1024) tpr = 1024;
+  // Row-group shape: 256-thread blocks take up to 8 accesses per thread (4
+  // with a branch); wider rows use groups of up to 1024 threads with up to 4.
+  const int cap256 = p.branch != nullptr ? 4 : 8;
+  int64_t tpr = 0;
+  if (nvec <= 256LL * cap256) {
+    tpr = pow2_ceil(ceil_div(nvec, vec ? cap256 : 4));
+    if (tpr > 256) tpr = 256;
+  } else if (nvec <= 1024LL * 4) {
+    tpr = pow2_ceil(ceil_div(nvec, 4));
+  }
+  if (tpr > 0) {
     const int nv = static_cast<int>(pow2_ceil(ceil_div(nvec, tpr)));
     const int block = tpr < 256 ? 256 : static_cast<int>(tpr);
     const int64_t rpb = block / tpr;

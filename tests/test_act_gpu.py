@@ -75,3 +75,28 @@ def test_config_shapes(oracle, xn, cuda):
     x = to_storage(randn(r, (16, 4096), 0.02), "bf16")
     Y = xn.silu(to_device(x, "bf16", cuda))
     assert_close(from_device(Y, "bf16"), oracle.unary(x, "silu", "bf16"), "bf16", "config3 silu")
+
+
+@pytest.mark.parametrize("op", ["silu", "gelu_erf"])
+def test_unary_bf16_exhaustive(oracle, xn, cuda, op):
+    """Every finite bf16 input (the whole domain of the bf16 ops)."""
+    bits = np.arange(0x10000, dtype=np.uint32).astype(np.uint16)
+    exp = (bits >> 7) & 0xFF
+    x = bits[exp != 0xFF]  # drop inf / NaN
+    ref = oracle.unary(x, op, "bf16")
+    got = from_device(getattr(xn, op)(to_device(x, "bf16", cuda)), "bf16")
+    extra = gelu_erf_abs_bound(storage_to_f32(x, "bf16")) if op == "gelu_erf" else None
+    stats = assert_close(got, ref, "bf16", f"{op} bf16 exhaustive", extra_abs=extra)
+    # The only differences are from expf / erff implementations (CUDA vs glibc).
+    assert stats["exact_frac"] > 0.999, stats
+
+
+def test_swiglu_bf16_all_gates(oracle, xn, cuda):
+    """Every finite bf16 gate value against random up values."""
+    bits = np.arange(0x10000, dtype=np.uint32).astype(np.uint16)
+    g = bits[((bits >> 7) & 0xFF) != 0xFF]
+    u = to_storage(randn(rng(12), g.size, 2.0), "bf16")
+    ref = oracle.swiglu(g, u, "bf16")
+    got = from_device(xn.swiglu(to_device(g, "bf16", cuda), to_device(u, "bf16", cuda)), "bf16")
+    stats = assert_close(got, ref, "bf16", "swiglu bf16 all gates")
+    assert stats["exact_frac"] > 0.999, stats
