@@ -234,12 +234,12 @@ __device__ __forceinline__ float group_max(float v, int tpr, float *red) {
 // q0 = RN(x*r) is within one ulp of x/d, rem = x - d*q0 is exact with an FMA,
 // and RN(q0 + rem*r) is the correctly rounded quotient (Markstein's theorem;
 // no overflow is possible where it is used: |x/d| stays far inside the f32
-// range). A zero q0 is kept as is so the sign of zero matches x / d.
+// range). d > 0, so the quotient has the sign of x (and of q0): copysign keeps
+// -0 / d == -0, which the correction step alone would turn into +0.
 __device__ __forceinline__ float div_by(float x, float d, float r) {
   const float q0 = __fmul_rn(x, r);
   const float rem = __fmaf_rn(-d, q0, x);
-  const float q = __fmaf_rn(rem, r, q0);
-  return q0 == 0.f ? q0 : q;
+  return copysignf(__fmaf_rn(rem, r, q0), q0);
 }
 
 // s / d where s and d are bf16 values, d >= 1, and the quotient is then

@@ -6,8 +6,9 @@
 // (per codebook: gather rows, transpose to [B, dim, T], add in codebook order
 // with T rounding per add).
 //
-// Design: one warp per output row copies the row with 16-byte vector loads,
-// four loads in flight per lane before the stores. Ids are read on the device
+// Design: warps stride over (output row, 2 KB chunk) work items and copy each
+// chunk with 16-byte vector loads, four in flight per lane before the stores;
+// the grid is capped at 8 blocks per SM. Ids are read on the device
 // (no host round trip); an out-of-range id yields a zero row and raises a
 // device error flag instead of faulting. The RVQ kernel sums the n_q codebook
 // rows of a frame in registers and, for the [B, dim, T] layout, transposes a
@@ -36,27 +37,41 @@ __device__ __forceinline__ int64_t load_id(const void *ids, int64_t i, int ids_i
 }
 
 // U = access unit type (uint4 for 16-byte vectors, else the element type).
+// Work items are (output row, chunk of 32 x kUnroll units); warps stride over
+// them, so a grid of a few blocks per SM stays evenly loaded to the end (one
+// warp per whole row would leave the last wave of rows half empty).
+constexpr int kGatherUnroll = 4;
+
 template <typename U>
 __global__ void __launch_bounds__(256) gather_rows_kernel(const GatherParams p) {
-  constexpr int kUnroll = 4;
   const int lane = threadIdx.x & 31;
-  const int64_t orow = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (orow >= p.out_rows) return;
-  const int64_t l = orow / p.n_ids;
-  const int64_t i = orow - l * p.n_ids;
-  const int64_t id = load_id(p.ids, i, p.ids_i64);
-  U *d = static_cast<U *>(p.dst) + orow * p.row_units;
-  if (id < 0 || id >= p.src_dim) {
-    if (lane == 0 && p.err != nullptr) atomicOr(p.err, 1);
-    for (int64_t u = lane; u < p.row_units; u += 32) d[u] = U{};
-    return;
-  }
-  const U *s = static_cast<const U *>(p.src) + (l * p.src_dim + id) * p.row_units;
-  for (int64_t u0 = lane; u0 < p.row_units; u0 += 32 * kUnroll) {
-    U v[kUnroll];
+  const int64_t units_per_chunk = 32 * kGatherUnroll;
+  const int64_t chunks = (p.row_units + units_per_chunk - 1) / units_per_chunk;
+  const int64_t items = p.out_rows * chunks;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t item = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); item < items;
+       item += warps) {
+    const int64_t orow = item / chunks;
+    const int64_t c = item - orow * chunks;
+    const int64_t l = orow / p.n_ids;
+    const int64_t i = orow - l * p.n_ids;
+    const int64_t id = load_id(p.ids, i, p.ids_i64);
+    U *d = static_cast<U *>(p.dst) + orow * p.row_units;
+    const int64_t u_begin = c * units_per_chunk;
+    if (id < 0 || id >= p.src_dim) {
+      if (lane == 0 && p.err != nullptr) atomicOr(p.err, 1);
 #pragma unroll
-    for (int k = 0; k < kUnroll; ++k) {
-      const int64_t u = u0 + k * 32;
+      for (int k = 0; k < kGatherUnroll; ++k) {
+        const int64_t u = u_begin + lane + k * 32;
+        if (u < p.row_units) d[u] = U{};
+      }
+      continue;
+    }
+    const U *s = static_cast<const U *>(p.src) + (l * p.src_dim + id) * p.row_units;
+    U v[kGatherUnroll];
+#pragma unroll
+    for (int k = 0; k < kGatherUnroll; ++k) {
+      const int64_t u = u_begin + lane + k * 32;
       if (u < p.row_units) {
         if constexpr (sizeof(U) == 16) {
           v[k] = ld_stream(s + u);
@@ -66,8 +81,8 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const GatherParams p) 
       }
     }
 #pragma unroll
-    for (int k = 0; k < kUnroll; ++k) {
-      const int64_t u = u0 + k * 32;
+    for (int k = 0; k < kGatherUnroll; ++k) {
+      const int64_t u = u_begin + lane + k * 32;
       if (u < p.row_units) d[u] = v[k];
     }
   }
@@ -255,14 +270,17 @@ int xn_index_select(void *dst, const void *src, const void *ids, int ids_is_i64,
     return fail(XN_E_INVALID, "xn_index_select: null pointer");
   const int64_t row_bytes = right * eb;
   GatherParams p{dst, src, ids, err_flag, n_ids, out_rows, src_dim, 0, ids_is_i64 ? 1 : 0};
-  const int64_t grid = ceil_div(out_rows, 8);
-  if (grid > 0x7fffffffLL) return fail(XN_E_INVALID, "xn_index_select: too many rows");
   cudaStream_t st = as_stream(stream);
-  if (row_bytes % 16 == 0 && is_aligned16(dst) && is_aligned16(src)) {
-    p.row_units = row_bytes / 16;
+  const bool vec = row_bytes % 16 == 0 && is_aligned16(dst) && is_aligned16(src);
+  p.row_units = vec ? row_bytes / 16 : right;
+  // Enough warps for every work item, capped at 8 blocks of 8 warps per SM.
+  const int64_t items = out_rows * ceil_div(p.row_units, 32 * kGatherUnroll);
+  int64_t grid = ceil_div(items, 8);
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
+  if (grid > cap) grid = cap;
+  if (vec) {
     gather_rows_kernel<uint4><<<grid, 256, 0, st>>>(p);
   } else {
-    p.row_units = right;
     switch (eb) {
       case 1:
         gather_rows_kernel<uint8_t><<<grid, 256, 0, st>>>(p);

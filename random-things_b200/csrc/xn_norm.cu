@@ -187,7 +187,7 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? ((kLN && NV == 8
 #pragma unroll
         for (int j = 0; j < N; ++j) {
           const float d = __fsub_rn(x[j], mean);
-          v = __fadd_rn(v, __fmul_rn(d, d));
+          v = __fmaf_rn(d, d, v);
         }
       }
     }
@@ -202,7 +202,7 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? ((kLN && NV == 8
       float x[N];
       unpack_raw(h[k], x);
 #pragma unroll
-      for (int j = 0; j < N; ++j) s = __fadd_rn(s, __fmul_rn(x[j], x[j]));
+      for (int j = 0; j < N; ++j) s = __fmaf_rn(x[j], x[j], s);
     }
     s = group_sum(s, tpr, red);
     scale_a = __fsqrt_rn(__fadd_rn(__fdiv_rn(s, cols_f), p.eps));
