@@ -282,6 +282,140 @@ class LlamaPrefillOps:
 
 
 # ---------------------------------------------------------------------------
+# Mimi decode frames/s (benchmark config 2): RVQ decode + 8-layer decoder
+# transformer on the fused ops, replayed as one CUDA graph.
+# ---------------------------------------------------------------------------
+def mimi_rate(torch, device, steps: int, batch: int = 4, frames: int = 250) -> dict:
+    import mimi_chain as mc
+
+    cfg = mc.MimiChainConfig()
+    w = mc.synthetic_weights(cfg, torch.bfloat16, device, seed=7)
+    cos, sin = mc.rope_tables(cfg, torch.bfloat16, device)
+    chain = mc.MimiDecoderChain(cfg, w, cos, sin)
+    g = torch.Generator().manual_seed(8)
+    codes_h = torch.randint(0, cfg.bins, (batch, cfg.n_q, frames), generator=g, dtype=torch.int64).pin_memory()
+    codes = codes_h.to(device)
+    for _ in range(3):
+        out = chain.decode(codes)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = chain.decode(codes)
+    out_h = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    # End to end: codes H2D, decode, output D2H, every step.
+    e0.record()
+    for _ in range(steps):
+        codes.copy_(codes_h, non_blocking=True)
+        graph.replay()
+        out_h.copy_(out, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    ms_e2e = e0.elapsed_time(e1) / steps
+    del graph
+    n = batch * frames
+    return {"frames_per_s": round(n / (ms * 1e-3), 1), "ms_per_decode": round(ms, 4),
+            "e2e_frames_per_s": round(n / (ms_e2e * 1e-3), 1), "batch": batch, "frames": frames,
+            "dtype": "bf16", "layers": cfg.num_layers, "d_model": cfg.d_model, "codebooks": cfg.n_q,
+            "what": "RVQ decode (8 x 2048 x 256) + 8-layer decoder transformer (LN, RoPE, causal softmax, GELU "
+                    "fused ops; GEMMs on cuBLAS), one CUDA graph; seeded synthetic weights"}
+
+
+# ---------------------------------------------------------------------------
+# Bandwidth sweep (benchmark config 5): each op over row widths and row counts,
+# f32 and bf16, L2 flushed before every timed launch. Points whose tensors
+# exceed the memory cap are skipped (listed with the reason).
+# ---------------------------------------------------------------------------
+SWEEP_OPS = ["rms_norm_residual", "layer_norm", "rope", "swiglu", "softmax", "embedding_gather"]
+
+
+def sweep(torch, xn, device, widths, rows_list, dtypes, reps: int, mem_cap_gb: float) -> list[dict]:
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)  # 256 MB > L2
+    out = []
+    for dname in dtypes:
+        dt = {"f32": torch.float32, "bf16": torch.bfloat16}[dname]
+        s = 4 if dname == "f32" else 2
+        for op in SWEEP_OPS:
+            for cols in widths:
+                for rows in rows_list:
+                    n_tensors = {"rms_norm_residual": 4, "layer_norm": 2, "rope": 2, "swiglu": 3, "softmax": 2,
+                                 "embedding_gather": 1}[op]
+                    need = n_tensors * rows * cols * s + (32768 * cols * s if op == "embedding_gather" else 0)
+                    point = {"op": op, "dtype": dname, "rows": rows, "cols": cols}
+                    if need > mem_cap_gb * 1e9:
+                        point["skipped"] = f"needs {need / 1e9:.1f} GB > cap {mem_cap_gb} GB"
+                        out.append(point)
+                        continue
+                    g = torch.Generator(device=device)
+                    g.manual_seed(rows + cols)
+
+                    def rnd(*shape):
+                        t = torch.empty(shape, dtype=torch.float32, device=device)
+                        t.normal_(generator=g)
+                        return t.to(dt)
+
+                    w = rnd(cols) * 0.02 + 1
+                    if op == "rms_norm_residual":
+                        x, br, y, h = rnd(rows, cols), rnd(rows, cols), torch.empty(rows, cols, dtype=dt, device=device), \
+                            torch.empty(rows, cols, dtype=dt, device=device)
+                        fn = lambda: xn.rms_norm_(y, x, w, 1e-5, branch=br, residual_out=h)  # noqa: E731
+                        nbytes = 4 * rows * cols * s + cols * s
+                    elif op == "layer_norm":
+                        x, y, b = rnd(rows, cols), torch.empty(rows, cols, dtype=dt, device=device), rnd(cols)
+                        fn = lambda: xn.layer_norm_(y, x, w, b, 1e-5)  # noqa: E731
+                        nbytes = 2 * rows * cols * s + 2 * cols * s
+                    elif op == "rope":
+                        if cols % 128:
+                            point["skipped"] = "rope needs width = heads x 128"
+                            out.append(point)
+                            continue
+                        heads, d = cols // 128, 128
+                        x, y = rnd(1, rows, heads, d), torch.empty(1, rows, heads, d, dtype=dt, device=device)
+                        cos, sin = rnd(rows, d // 2), rnd(rows, d // 2)
+                        fn = lambda: xn.rope_(y, x, cos, sin, 0, layout="bthd")  # noqa: E731
+                        nbytes = 2 * rows * cols * s + 2 * rows * (d // 2) * s
+                    elif op == "swiglu":
+                        a, b2, y = rnd(rows, cols), rnd(rows, cols), torch.empty(rows, cols, dtype=dt, device=device)
+                        fn = lambda: xn.swiglu_(y, a, b2)  # noqa: E731
+                        nbytes = 3 * rows * cols * s
+                    elif op == "softmax":
+                        x, y = rnd(rows, cols), torch.empty(rows, cols, dtype=dt, device=device)
+                        fn = lambda: xn.softmax_(y, x)  # noqa: E731
+                        nbytes = 2 * rows * cols * s
+                    else:
+                        table = rnd(32768, cols)
+                        ids = torch.randint(0, 32768, (rows,), dtype=torch.int32, device=device, generator=g)
+                        y = torch.empty(rows, cols, dtype=dt, device=device)
+                        fn = lambda: xn.index_select(table, ids, 0, out=y)  # noqa: E731
+                        nbytes = rows * 4 + 2 * rows * cols * s
+                    fn()
+                    times = []
+                    for _ in range(reps):
+                        flush.zero_()
+                        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                        e0.record()
+                        fn()
+                        e1.record()
+                        torch.cuda.synchronize()
+                        times.append(e0.elapsed_time(e1))
+                    ms = statistics.median(times)
+                    point.update(ms=round(ms, 5), gbs=round(nbytes / (ms * 1e-3) / 1e9, 1))
+                    out.append(point)
+                    del fn
+                    torch.cuda.empty_cache()
+    return out
+
+
+# ---------------------------------------------------------------------------
 # CPU side: the oracle restatement of the reference CPU backend on a sample.
 # ---------------------------------------------------------------------------
 class CpuSample:
@@ -398,6 +532,12 @@ def main() -> int:
     ap.add_argument("--rows", type=int, default=CFG["batch"] * CFG["seq"],
                     help="token rows per GPU (a multiple of 4096; smaller values for profiling captures)")
     ap.add_argument("--ops", default=",".join(OPS), help="comma-separated subset of " + ",".join(OPS))
+    ap.add_argument("--mimi-steps", type=int, default=20, help="Mimi decode replays to time (0 skips it)")
+    ap.add_argument("--sweep", action="store_true", help="run the per-op bandwidth sweep instead (JSON per point)")
+    ap.add_argument("--sweep-widths", default="256,1024,4096,16384")
+    ap.add_argument("--sweep-rows", default="1024,16384,262144,1048576")
+    ap.add_argument("--sweep-dtypes", default="f32,bf16")
+    ap.add_argument("--sweep-mem-gb", type=float, default=48.0)
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -414,6 +554,17 @@ def main() -> int:
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
+    if args.sweep:
+        xn.lib()
+        peak, _ = measured_peak()
+        pts = sweep(torch, xn, dev, [int(v) for v in args.sweep_widths.split(",")],
+                    [int(v) for v in args.sweep_rows.split(",")], args.sweep_dtypes.split(","), max(3, args.steps),
+                    args.sweep_mem_gb)
+        for pt in pts:
+            if "gbs" in pt:
+                pt["frac"] = round(pt["gbs"] / peak, 3)
+            print(json.dumps(pt), flush=True)
+        return 0
     distributed = world > 1
     if distributed:
         from datetime import timedelta
@@ -481,10 +632,22 @@ def main() -> int:
         torch.cuda.synchronize()
         e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
 
+    mimi = None
+    if args.mimi_steps > 0:
+        mimi = mimi_rate(torch, dev, args.mimi_steps)
+
     if distributed:
-        t = torch.tensor([elapsed_ms, e2e_ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        vals = [elapsed_ms, e2e_ms, mimi["ms_per_decode"] if mimi else 0.0, mimi["e2e_frames_per_s"] if mimi else 0.0]
+        t = torch.tensor(vals, dtype=torch.float64, device=dev)
+        dist.all_reduce(t[:3], op=dist.ReduceOp.MAX)
+        dist.all_reduce(t[3:], op=dist.ReduceOp.MIN)
         elapsed_ms, e2e_ms = float(t[0]), float(t[1])
+        if mimi:
+            # Whole-job rate: every rank decodes its own batch; the slowest rank sets the time.
+            n = mimi["batch"] * mimi["frames"]
+            mimi["ms_per_decode"] = round(float(t[2]), 4)
+            mimi["frames_per_s"] = round(world * n / (float(t[2]) * 1e-3), 1)
+            mimi["e2e_frames_per_s"] = round(world * float(t[3]), 1)
 
     if rank == 0:
         step_bytes = sum(wl.bytes.values())
@@ -513,6 +676,7 @@ def main() -> int:
                 "ms_per_step": round(e2e_ms, 3),
                 "method": "per-sequence chunks; H2D, kernels and D2H on three streams"},
             "gpu_launches": len(ops) * args.steps,
+            "mimi_decode": mimi,
             "clocks": clocks,
         }
         if not args.no_cpu_baseline and world == 1:

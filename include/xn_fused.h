@@ -152,11 +152,37 @@ XN_API int xn_rope_qk(void *q_dst, const void *q_src, void *k_dst, const void *k
                int dtype, void *stream);
 
 /*
+ * Q and K rotated in place of the narrow + reshape + transpose + contiguous
+ * copies the reference makes from the packed QKV projection
+ * (mimi-rs/src/models/mimi.rs:1332-1351): both tensors are in [B, T, H, D]
+ * layout with `src_tok_stride` elements between consecutive (b, t) tokens
+ * (3 * H * D inside a packed [B, T, 3*H*D] projection, where k_src =
+ * q_src + H * D) and outputs written with `dst_tok_stride` (H * D for
+ * contiguous [B, T, H, D] outputs; equal to the source layout for in-place).
+ * Arithmetic as xn_rope.
+ */
+XN_API int xn_rope_qk_strided(void *q_dst, const void *q_src, void *k_dst, const void *k_src,
+                              const void *cos, const void *sin,
+                              int64_t b, int64_t hq, int64_t hk, int64_t t, int64_t d,
+                              int64_t pos, int64_t max_pos, int64_t src_tok_stride,
+                              int64_t dst_tok_stride, int interleaved, int dtype, void *stream);
+
+/*
  * Elementwise unary op on n elements (XN_UNARY_SILU or XN_UNARY_GELU_ERF).
  * Replaces Backend::unary for those ops (mimi-rs/src/backend.rs:57-62,
  * cuda_backend.rs:523-554, cpu_backend.rs:184-222). dst may alias src.
  */
 XN_API int xn_unary(void *dst, const void *src, int64_t n, int op, int dtype, void *stream);
+
+/*
+ * Residual add with optional layer scale on [rows, cols]:
+ *   dst = T(x + T(branch * layer_scale[col]))   (or T(x + branch))
+ * Replaces LayerScale::forward (broadcast_mul, cpu_backend.rs:1379-1387) +
+ * Tensor::add of mimi-rs/src/models/mimi.rs:1441-1444 where no norm follows
+ * (the last layer of a stack); elsewhere the norms fuse it. dst may alias x.
+ */
+XN_API int xn_residual_add(void *dst, const void *x, const void *branch, const void *layer_scale,
+                           int64_t rows, int64_t cols, int dtype, void *stream);
 
 /*
  * SwiGLU: dst[r, c] = T(T(silu(gate[r, c])) * up[r, c]), silu in T arithmetic.
@@ -179,6 +205,16 @@ XN_API int xn_swiglu(void *dst, const void *gate, const void *up, int64_t rows, 
  */
 XN_API int xn_softmax(void *dst, const void *src, int64_t rows, int64_t cols,
                int causal, int64_t t1, int64_t offset, int dtype, void *stream);
+
+/*
+ * xn_softmax preceded by the attention-score scale: x = T(x * scale), then
+ * the optional causal mask and the softmax. Replaces `scale` (Tensor::scale,
+ * mimi-rs/src/ops.rs:101-105, cpu_backend.rs:260-276) + mask + softmax of
+ * mimi-rs/src/models/mimi.rs:1361-1368 and llama.rs:192-202. `scale` is the
+ * T-typed value the caller uses (T::from_f32(1 / sqrt(head_dim))).
+ */
+XN_API int xn_softmax_scaled(void *dst, const void *src, int64_t rows, int64_t cols, float scale,
+                             int causal, int64_t t1, int64_t offset, int dtype, void *stream);
 
 /*
  * In-place causal mask on [bh, t1, t2]: x[b, i, j] = -inf where j > offset + i.

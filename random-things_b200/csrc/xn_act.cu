@@ -181,6 +181,78 @@ __global__ void __launch_bounds__(kBlock) swiglu_kernel(void *dst, const void *g
   }
 }
 
+// dst = T(x + T(branch * ls[col])) (or T(x + branch)) over [rows, cols]: the
+// reference's LayerScale::forward (broadcast_mul, cpu_backend.rs:1379-1387)
+// followed by `xs.add` (mimi.rs:1441-1444). grid.x covers a row's columns,
+// grid.y strides over rows.
+template <typename T, bool kVector>
+__global__ void __launch_bounds__(kBlock) residual_kernel(void *dst, const void *x, const void *branch,
+                                                           const void *ls, int64_t rows, int64_t cols) {
+  constexpr int N = kVector ? Elem<T>::kVec : 1;
+  const int64_t cacc = cols / N;
+  const int64_t c0 = static_cast<int64_t>(blockIdx.x) * kBlock * kUnroll + threadIdx.x;
+  for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
+    const T *xr = static_cast<const T *>(x) + r * cols;
+    const T *br = static_cast<const T *>(branch) + r * cols;
+    T *dr = static_cast<T *>(dst) + r * cols;
+    if constexpr (kVector) {
+      uint4 rx[kUnroll], rb[kUnroll];
+#pragma unroll
+      for (int k = 0; k < kUnroll; ++k) {
+        const int64_t i = c0 + k * kBlock;
+        if (i < cacc) {
+          rx[k] = ld_stream(xr + i * N);
+          rb[k] = ld_stream(br + i * N);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kUnroll; ++k) {
+        const int64_t i = c0 + k * kBlock;
+        if (i < cacc) {
+          float vx[N], vb[N];
+          unpack<T>(rx[k], vx);
+          unpack<T>(rb[k], vb);
+          if (ls != nullptr) {
+            float vs[N];
+            unpack<T>(ld_cached(static_cast<const T *>(ls) + i * N), vs);
+#pragma unroll
+            for (int j = 0; j < N; ++j) vb[j] = Elem<T>::round(__fmul_rn(vb[j], vs[j]));
+          }
+#pragma unroll
+          for (int j = 0; j < N; ++j) vx[j] = __fadd_rn(vx[j], vb[j]);
+          st_vec(dr + i * N, pack<T>(vx));
+        }
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < kUnroll; ++k) {
+        const int64_t i = c0 + k * kBlock;
+        if (i >= cols) break;
+        float b = Elem<T>::to_f32(br[i]);
+        if (ls != nullptr) b = Elem<T>::round(__fmul_rn(b, Elem<T>::to_f32(static_cast<const T *>(ls)[i])));
+        dr[i] = Elem<T>::from_f32(__fadd_rn(Elem<T>::to_f32(xr[i]), b));
+      }
+    }
+  }
+}
+
+template <typename T>
+int launch_residual(void *dst, const void *x, const void *branch, const void *ls, int64_t rows, int64_t cols,
+                    cudaStream_t st) {
+  constexpr int V = Elem<T>::kVec;
+  const bool vec = cols % V == 0 && is_aligned16(dst) && is_aligned16(x) && is_aligned16(branch) && is_aligned16(ls);
+  const int64_t cacc = vec ? cols / V : cols;
+  const int64_t gx = ceil_div(cacc, static_cast<int64_t>(kBlock) * kUnroll);
+  if (gx > 0x7fffffffLL) return fail(XN_E_INVALID, "xn_residual_add: row too long");
+  const int64_t gy = rows < 65535 ? rows : 65535;
+  dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy));
+  if (vec)
+    residual_kernel<T, true><<<grid, kBlock, 0, st>>>(dst, x, branch, ls, rows, cols);
+  else
+    residual_kernel<T, false><<<grid, kBlock, 0, st>>>(dst, x, branch, ls, rows, cols);
+  return check_launch("xn_residual_add");
+}
+
 template <typename T>
 int launch_unary(void *dst, const void *src, int64_t n, int op, cudaStream_t st) {
   constexpr int V = Elem<T>::kVec;
@@ -240,6 +312,17 @@ int xn_unary(void *dst, const void *src, int64_t n, int op, int dtype, void *str
   if (dst == nullptr || src == nullptr) return fail(XN_E_INVALID, "xn_unary: null dst or src");
   XN_DISPATCH_FLOAT(dtype, return launch_unary<T>(dst, src, n, op, as_stream(stream)));
   return fail(XN_E_DTYPE, "xn_unary: unsupported dtype %d", dtype);
+}
+
+int xn_residual_add(void *dst, const void *x, const void *branch, const void *layer_scale, int64_t rows,
+                    int64_t cols, int dtype, void *stream) {
+  using namespace xn;
+  if (!is_float_dtype(dtype)) return fail(XN_E_DTYPE, "xn_residual_add: unsupported dtype %d", dtype);
+  if (rows < 0 || cols < 0) return fail(XN_E_INVALID, "xn_residual_add: negative size");
+  if (rows == 0 || cols == 0) return ok();
+  if (dst == nullptr || x == nullptr || branch == nullptr) return fail(XN_E_INVALID, "xn_residual_add: null pointer");
+  XN_DISPATCH_FLOAT(dtype, return launch_residual<T>(dst, x, branch, layer_scale, rows, cols, as_stream(stream)));
+  return fail(XN_E_DTYPE, "xn_residual_add: unsupported dtype %d", dtype);
 }
 
 int xn_swiglu(void *dst, const void *gate, const void *up, int64_t rows, int64_t cols,

@@ -25,6 +25,8 @@ struct RopeTensor {
   const void *src;
   uint32_t heads;
   uint32_t items;  // work items of this tensor in this launch
+  int64_t src_ts;  // [B,T,H,D] layout: elements between consecutive tokens
+  int64_t dst_ts;  //   (H*D when contiguous; larger inside a packed QKV row)
 };
 
 struct RopeParams {
@@ -104,16 +106,21 @@ __global__ void __launch_bounds__(256) rope_kernel(const RopeParams p) {
   const int64_t d = p.d;
   const int64_t half = d / 2;
   const int64_t trow = (p.pos + ti) * half;  // first table entry of this time step
-  int64_t row0, head_stride;
-  if (p.layout == XN_LAYOUT_BHTD) {
-    row0 = ((static_cast<int64_t>(bi) * H) * p.t + ti) * d;
-    head_stride = static_cast<int64_t>(p.t) * d;
-  } else {
-    row0 = ((static_cast<int64_t>(bi) * p.t + ti) * H) * d;
-    head_stride = d;
-  }
+  int64_t head_stride;
   const T *src = static_cast<const T *>(tn.src);
   T *dst = static_cast<T *>(tn.dst);
+  if (p.layout == XN_LAYOUT_BHTD) {
+    const int64_t row0 = ((static_cast<int64_t>(bi) * H) * p.t + ti) * d;
+    src += row0;
+    dst += row0;
+    head_stride = static_cast<int64_t>(p.t) * d;
+  } else {
+    const int64_t tok = static_cast<int64_t>(bi) * p.t + ti;
+    src += tok * tn.src_ts;
+    dst += tok * tn.dst_ts;
+    head_stride = d;
+  }
+  // src and dst now point at head 0 of this (b, t) row.
   const T *cs = static_cast<const T *>(p.cos);
   const T *sn = static_cast<const T *>(p.sin);
 
@@ -124,7 +131,7 @@ __global__ void __launch_bounds__(256) rope_kernel(const RopeParams p) {
     for (int hh = 0; hh < kMaxHpt; ++hh) {
       const uint32_t h = hg * p.hpt + hh;
       if (hh < static_cast<int>(p.hpt) && h < H) {
-        const int64_t e1 = row0 + h * head_stride + c * V;
+        const int64_t e1 = h * head_stride + c * V;
         r1[hh] = ld_stream(src + e1);
         r2[hh] = ld_stream(src + e1 + half);
       }
@@ -135,7 +142,7 @@ __global__ void __launch_bounds__(256) rope_kernel(const RopeParams p) {
     for (int hh = 0; hh < kMaxHpt; ++hh) {
       const uint32_t h = hg * p.hpt + hh;
       if (hh < static_cast<int>(p.hpt) && h < H) {
-        const int64_t e1 = row0 + h * head_stride + c * V;
+        const int64_t e1 = h * head_stride + c * V;
         uint4 y1, y2;
         rotate_halfsplit<T>(r1[hh], r2[hh], cr, sr, y1, y2);
         st_vec(dst + e1, y1);
@@ -149,7 +156,7 @@ __global__ void __launch_bounds__(256) rope_kernel(const RopeParams p) {
 #pragma unroll
     for (int hh = 0; hh < kMaxHpt; ++hh) {
       const uint32_t h = hg * p.hpt + hh;
-      if (hh < static_cast<int>(p.hpt) && h < H) rx[hh] = ld_stream(src + row0 + h * head_stride + c * V);
+      if (hh < static_cast<int>(p.hpt) && h < H) rx[hh] = ld_stream(src + h * head_stride + c * V);
     }
     float cv[P], sv[P];
     unpack_half<T>(ld_cached8(cs + trow + c * P), cv);
@@ -168,7 +175,7 @@ __global__ void __launch_bounds__(256) rope_kernel(const RopeParams p) {
           y[2 * j + 1] = Elem<T>::round(__fadd_rn(Elem<T>::round(__fmul_rn(a, sv[j])),
                                                   Elem<T>::round(__fmul_rn(b, cv[j]))));
         }
-        st_vec(dst + row0 + h * head_stride + c * V, pack<T>(y));
+        st_vec(dst + h * head_stride + c * V, pack<T>(y));
       }
     }
   } else {
@@ -178,7 +185,7 @@ __global__ void __launch_bounds__(256) rope_kernel(const RopeParams p) {
     for (uint32_t hh = 0; hh < p.hpt; ++hh) {
       const uint32_t h = hg * p.hpt + hh;
       if (h >= H) break;
-      const int64_t r = row0 + h * head_stride;
+      const int64_t r = h * head_stride;
       const int64_t e1 = kInterleaved ? r + 2 * c : r + c;
       const int64_t e2 = kInterleaved ? e1 + 1 : e1 + half;
       const float a = Elem<T>::to_f32(src[e1]), b = Elem<T>::to_f32(src[e2]);
@@ -195,6 +202,8 @@ struct RopeJob {
   const void *src[2];
   int64_t heads[2];
   int n;
+  int64_t src_ts = 0;  // token strides for the [B,T,H,D] layout (0: contiguous)
+  int64_t dst_ts = 0;
 };
 
 template <typename T>
@@ -205,6 +214,12 @@ int launch_rope(const RopeJob &job, const void *cos, const void *sin, int64_t b,
   const int64_t half = d / 2;
   bool vec = is_aligned16(cos) && is_aligned16(sin);
   for (int i = 0; i < job.n; ++i) vec = vec && is_aligned16(job.dst[i]) && is_aligned16(job.src[i]);
+  // Token strides must keep every row start 16-byte aligned for the vector path.
+  for (int i = 0; i < job.n; ++i) {
+    const int64_t hd = job.heads[i] * d;
+    const int64_t sts = job.src_ts ? job.src_ts : hd, dts = job.dst_ts ? job.dst_ts : hd;
+    vec = vec && (sts * static_cast<int64_t>(sizeof(T))) % 16 == 0 && (dts * static_cast<int64_t>(sizeof(T))) % 16 == 0;
+  }
   vec = vec && (interleaved ? (d % V == 0) : (half % V == 0));
   const int64_t chunks = vec ? (interleaved ? d / V : half / V) : half;
   int64_t max_heads = 0;
@@ -225,13 +240,19 @@ int launch_rope(const RopeJob &job, const void *cos, const void *sin, int64_t b,
     int64_t total = 0;
     for (int i = 0; i < 2; ++i) {
       if (i < job.n) {
-        const int64_t bstride = job.heads[i] * t * d;  // elements per batch element
-        p.ten[i].dst = static_cast<T *>(job.dst[i]) + b0 * bstride;
-        p.ten[i].src = static_cast<const T *>(job.src[i]) + b0 * bstride;
+        const int64_t hd = job.heads[i] * d;
+        const int64_t sts = job.src_ts ? job.src_ts : hd, dts = job.dst_ts ? job.dst_ts : hd;
+        // Elements per batch element (BHTD is always contiguous).
+        const int64_t sb = layout == XN_LAYOUT_BHTD ? hd * t : sts * t;
+        const int64_t db = layout == XN_LAYOUT_BHTD ? hd * t : dts * t;
+        p.ten[i].dst = static_cast<T *>(job.dst[i]) + b0 * db;
+        p.ten[i].src = static_cast<const T *>(job.src[i]) + b0 * sb;
         p.ten[i].heads = static_cast<uint32_t>(job.heads[i]);
         p.ten[i].items = static_cast<uint32_t>(nb * ceil_div(job.heads[i], hpt) * t * chunks);
+        p.ten[i].src_ts = sts;
+        p.ten[i].dst_ts = dts;
       } else {
-        p.ten[i] = RopeTensor{nullptr, nullptr, 1, 0};
+        p.ten[i] = RopeTensor{nullptr, nullptr, 1, 0, 0, 0};
       }
       total += p.ten[i].items;
     }
@@ -308,6 +329,22 @@ int xn_rope_qk(void *q_dst, const void *q_src, void *k_dst, const void *k_src, c
   xn::RopeJob job{{q_dst, k_dst}, {q_src, k_src}, {hq, hk}, 2};
   return xn::rope_entry("xn_rope_qk", job, cos, sin, b, t, d, pos, max_pos, interleaved, layout,
                         dtype, stream);
+}
+
+int xn_rope_qk_strided(void *q_dst, const void *q_src, void *k_dst, const void *k_src, const void *cos,
+                       const void *sin, int64_t b, int64_t hq, int64_t hk, int64_t t, int64_t d, int64_t pos,
+                       int64_t max_pos, int64_t src_tok_stride, int64_t dst_tok_stride, int interleaved,
+                       int dtype, void *stream) {
+  using namespace xn;
+  const char *op = "xn_rope_qk_strided";
+  const int64_t hmax = hq > hk ? hq : hk;
+  if (src_tok_stride < hmax * d || dst_tok_stride < hmax * d)
+    return fail(XN_E_INVALID, "%s: token stride smaller than heads * d (src %lld, dst %lld, need %lld)", op,
+                (long long)src_tok_stride, (long long)dst_tok_stride, (long long)(hmax * d));
+  RopeJob job{{q_dst, k_dst}, {q_src, k_src}, {hq, hk}, 2};
+  job.src_ts = src_tok_stride;
+  job.dst_ts = dst_tok_stride;
+  return rope_entry(op, job, cos, sin, b, t, d, pos, max_pos, interleaved, XN_LAYOUT_BTHD, dtype, stream);
 }
 
 }  // extern "C"

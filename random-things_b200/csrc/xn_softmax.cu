@@ -30,6 +30,8 @@ struct SoftmaxParams {
   int causal;
   int tpr;
   int nvec;
+  int scaled;      // apply x = T(x * scale) first (the attention score scale)
+  float scale;
 };
 
 __device__ __forceinline__ int64_t row_limit(const SoftmaxParams &p, int64_t row) {
@@ -66,7 +68,11 @@ __global__ void __launch_bounds__(512) softmax_regs_kernel(const SoftmaxParams p
       }
 #pragma unroll
       for (int j = 0; j < N; ++j) {
-        if (e0 + j >= lim) x[k][j] = -INFINITY;
+        if (e0 + j >= lim) {
+          x[k][j] = -INFINITY;
+        } else if (p.scaled) {
+          x[k][j] = Elem<T>::round(__fmul_rn(x[k][j], p.scale));
+        }
         mx = fmaxf(mx, x[k][j]);
       }
     } else {
@@ -119,14 +125,18 @@ __global__ void __launch_bounds__(1024) softmax_loop_kernel(const SoftmaxParams 
   const T *src = static_cast<const T *>(p.src);
   T *dst = static_cast<T *>(p.dst);
   const int tpr = blockDim.x;
+  auto load = [&](int64_t c) -> float {
+    const float x = Elem<T>::to_f32(src[base + c]);
+    return p.scaled ? Elem<T>::round(__fmul_rn(x, p.scale)) : x;
+  };
   float mx = -INFINITY;
-  for (int64_t c = threadIdx.x; c < lim; c += tpr) mx = fmaxf(mx, Elem<T>::to_f32(src[base + c]));
+  for (int64_t c = threadIdx.x; c < lim; c += tpr) mx = fmaxf(mx, load(c));
   mx = group_max(mx, tpr, red);
   float s = 0.f;
   for (int64_t c = threadIdx.x; c < p.cols; c += tpr) {
     float e = 0.f;
     if (c < lim) {
-      e = Elem<T>::round(expf(Elem<T>::round(__fsub_rn(Elem<T>::to_f32(src[base + c]), mx))));
+      e = Elem<T>::round(expf(Elem<T>::round(__fsub_rn(load(c), mx))));
       s = __fadd_rn(s, e);
     }
     dst[base + c] = Elem<T>::from_f32(e);
@@ -204,11 +214,10 @@ __global__ void __launch_bounds__(256) causal_mask_kernel(void *dst, int64_t row
 }  // namespace
 }  // namespace xn
 
-extern "C" {
-
-int xn_softmax(void *dst, const void *src, int64_t rows, int64_t cols, int causal, int64_t t1,
-               int64_t offset, int dtype, void *stream) {
-  using namespace xn;
+namespace xn {
+namespace {
+int softmax_entry(void *dst, const void *src, int64_t rows, int64_t cols, int scaled, float scale, int causal,
+                  int64_t t1, int64_t offset, int dtype, void *stream) {
   if (!is_float_dtype(dtype)) return fail(XN_E_DTYPE, "xn_softmax: unsupported dtype %d", dtype);
   if (rows < 0 || cols < 0) return fail(XN_E_INVALID, "xn_softmax: negative size");
   if (causal && (t1 <= 0 || offset < 0 || rows % t1 != 0))
@@ -216,9 +225,24 @@ int xn_softmax(void *dst, const void *src, int64_t rows, int64_t cols, int causa
                 (long long)rows, (long long)t1, (long long)offset);
   if (rows == 0 || cols == 0) return ok();
   if (dst == nullptr || src == nullptr) return fail(XN_E_INVALID, "xn_softmax: null dst or src");
-  SoftmaxParams p{dst, src, rows, cols, causal ? t1 : 1, causal ? offset : 0, causal ? 1 : 0, 0, 0};
+  SoftmaxParams p{dst, src, rows, cols, causal ? t1 : 1, causal ? offset : 0, causal ? 1 : 0, 0, 0, scaled, scale};
   XN_DISPATCH_FLOAT(dtype, return launch_softmax<T>(p, as_stream(stream)));
   return fail(XN_E_DTYPE, "xn_softmax: unsupported dtype %d", dtype);
+}
+}  // namespace
+}  // namespace xn
+
+extern "C" {
+
+
+int xn_softmax(void *dst, const void *src, int64_t rows, int64_t cols, int causal, int64_t t1,
+               int64_t offset, int dtype, void *stream) {
+  return xn::softmax_entry(dst, src, rows, cols, 0, 1.f, causal, t1, offset, dtype, stream);
+}
+
+int xn_softmax_scaled(void *dst, const void *src, int64_t rows, int64_t cols, float scale, int causal, int64_t t1,
+                      int64_t offset, int dtype, void *stream) {
+  return xn::softmax_entry(dst, src, rows, cols, 1, scale, causal, t1, offset, dtype, stream);
 }
 
 int xn_causality_mask(void *dst, int64_t bh, int64_t t1, int64_t t2, int64_t offset, int dtype,

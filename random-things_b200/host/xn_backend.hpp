@@ -160,6 +160,29 @@ class CudaDevice {
     rope_impl(dst, src, cos, sin, b, h, t, d, pos, true, "rope-i");
   }
 
+  // Q and K of a packed [B, T, (hq + 2*hk) * d] QKV projection, rotated without
+  // the narrow / transpose / contiguous copies (mimi.rs:1332-1351); outputs are
+  // contiguous [B, T, h, d] (hq == hk).
+  template <typename T>
+  void rope_qk_packed(Storage<T> &q_dst, Storage<T> &k_dst, const Storage<T> &qkv, const Storage<T> &cos,
+                      const Storage<T> &sin, size_t b, size_t t, size_t heads, size_t d, size_t pos,
+                      bool interleaved) const {
+    const size_t row = 3 * heads * d;
+    expect_at_least(qkv, b * t * row, "rope_qk_packed qkv");
+    expect_at_least(q_dst, b * t * heads * d, "rope_qk_packed q");
+    expect_at_least(k_dst, b * t * heads * d, "rope_qk_packed k");
+    if (d % 2 != 0) throw Error("rope_qk_packed requires even d dimension, got d=" + std::to_string(d));
+    const size_t max_pos = d ? cos.len / (d / 2) : 0;
+    if (pos + t > max_pos)
+      throw Error("rope_qk_packed position out of range, pos=" + std::to_string(pos) + " + t=" + std::to_string(t) +
+                      " > max_pos=" + std::to_string(max_pos),
+                  XN_E_RANGE);
+    check(xn_rope_qk_strided(q_dst.data, qkv.data, k_dst.data, qkv.data + heads * d, cos.data, sin.data, (int64_t)b,
+                             (int64_t)heads, (int64_t)heads, (int64_t)t, (int64_t)d, (int64_t)pos, (int64_t)max_pos,
+                             (int64_t)row, (int64_t)(heads * d), interleaved ? 1 : 0, DTypeOf<T>::value, stream_),
+          "rope_qk_packed");
+  }
+
   // ---- Backend::unary for Silu / GeluErf (backend.rs:57-62)
   template <typename T>
   void unary(Storage<T> &dst, const Storage<T> &src, size_t len, UnaryOp op) const {
@@ -168,6 +191,18 @@ class CudaDevice {
     check(xn_unary(dst.data, src.data, (int64_t)len, op == UnaryOp::Silu ? XN_UNARY_SILU : XN_UNARY_GELU_ERF,
                    DTypeOf<T>::value, stream_),
           "unary");
+  }
+
+  // dst = x + layer_scale * branch (LayerScale + add, mimi.rs:1441-1444);
+  // layer_scale may be null.
+  template <typename T>
+  void residual_add(Storage<T> &dst, const Storage<T> &x, const Storage<T> &branch, const Storage<T> *layer_scale,
+                    size_t dim_m1, size_t d) const {
+    for (const Storage<T> *s : {&dst, &x, &branch}) expect_len(*s, dim_m1 * d, "residual_add");
+    if (layer_scale) expect_len(*layer_scale, dim_m1, "residual_add layer_scale");
+    check(xn_residual_add(dst.data, x.data, branch.data, layer_scale ? layer_scale->data : nullptr, (int64_t)d,
+                          (int64_t)dim_m1, DTypeOf<T>::value, stream_),
+          "residual_add");
   }
 
   // SwiGLU: dst = silu(gate) * up on [rows, cols] (llama.rs:256-263 composite).
@@ -201,6 +236,18 @@ class CudaDevice {
     check(xn_softmax(dst.data, src.data, (int64_t)(bh * t1), (int64_t)t2, 1, (int64_t)(t1 ? t1 : 1),
                      (int64_t)offset, DTypeOf<T>::value, stream_),
           "softmax_causal");
+  }
+
+  // T(scores * scale), optional causal mask, softmax in one launch
+  // (mimi.rs:1361-1368); `scale` is the T-typed value.
+  template <typename T>
+  void attn_softmax(Storage<T> &dst, const Storage<T> &src, size_t bh, size_t t1, size_t t2, float scale,
+                    bool causal, size_t offset) const {
+    expect_at_least(src, bh * t1 * t2, "attn_softmax src");
+    expect_at_least(dst, bh * t1 * t2, "attn_softmax dst");
+    check(xn_softmax_scaled(dst.data, src.data, (int64_t)(bh * t1), (int64_t)t2, scale, causal ? 1 : 0,
+                            (int64_t)(t1 ? t1 : 1), (int64_t)offset, DTypeOf<T>::value, stream_),
+          "attn_softmax");
   }
 
   // ---- Backend::apply_causality_mask (backend.rs:150-156)

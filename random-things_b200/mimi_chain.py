@@ -1,0 +1,168 @@
+"""Mimi decoder chain on the fused ops: RVQ decode + decoder transformer.
+
+This is the caller the fused layer ops were built for. It restates, for the
+ops on the path, the reference's
+  * SplitResidualVectorQuantizer::decode (mimi-rs/src/models/mimi.rs:1858-1868)
+    -> ResidualVectorQuantizer::decode (:1796-1806, 1x1-conv output projection)
+    -> ResidualVectorQuantization::decode (:1730-1744) -> codebook gathers,
+  * StreamingTransformer::forward (:1476-1483) over StreamingTransformerLayer
+    (:1423-1445) with StreamingMultiheadAttention (:1317-1384) and Mlp
+    (:1256-1269), norm_first, LayerNorm (eps 1e-5), LayerScale, interleaved
+    RoPE, causal softmax, GELU(erf),
+with every layer op on the sm_100a kernels and the layer-to-layer glue fused:
+  * the two RVQ codebook loops -> two xn_rvq_decode_sum launches,
+  * LayerScale + residual add + next LayerNorm -> one xn_layer_norm,
+  * narrow/transpose/contiguous + rope_i on Q and K -> one xn_rope_qk_strided
+    reading the packed QKV projection,
+  * scale + causal mask + softmax -> one xn_softmax_scaled,
+  * the final LayerScale + add -> one xn_residual_add.
+GEMMs (projections, attention products, MLP) run on cuBLAS through
+torch.matmul, as the reference runs them on cuBLAS. The SEANet decoder and the
+upsampling transposed convolution are outside this path; the chain runs the
+decoder transformer at the codes' frame rate on [B, T, D] (the reference's
+conv_layout transposes, :1528-1548, become layout choices).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+import xn_fused as xn
+
+
+@dataclass
+class MimiChainConfig:
+    """The Mimi v0.1 values used on this path (mimi.rs:1908-1963)."""
+
+    d_model: int = 512
+    num_heads: int = 8
+    num_layers: int = 8
+    dim_feedforward: int = 2048
+    max_period: float = 10000.0
+    max_seq_len: int = 8192
+    context: int = 250
+    n_q: int = 8
+    bins: int = 2048
+    q_dim: int = 256
+    eps: float = 1e-5
+
+    @property
+    def head_dim(self) -> int:
+        return self.d_model // self.num_heads
+
+
+def rope_tables(cfg: MimiChainConfig, dtype: torch.dtype, device) -> tuple[torch.Tensor, torch.Tensor]:
+    """RotaryEmbedding::new (mimi.rs:1162-1185): inv_freq = 1 / theta^(i / half),
+    angle = pos * inv_freq, evaluated in f32 and rounded to T."""
+    half = cfg.head_dim // 2
+    i = torch.arange(half, dtype=torch.float32)
+    inv = 1.0 / torch.pow(torch.tensor(cfg.max_period, dtype=torch.float32), i / half)
+    ang = torch.arange(cfg.max_seq_len, dtype=torch.float32)[:, None] * inv[None, :]
+    return ang.cos().to(dtype).to(device), ang.sin().to(dtype).to(device)
+
+
+def synthetic_weights(cfg: MimiChainConfig, dtype: torch.dtype, device, seed: int = 0) -> dict[str, torch.Tensor]:
+    """Seeded random weights with the reference's tensor names and shapes.
+    Codebook entries ~ N(0, 1), layer scales ~ U(0, 0.1), norm gains ~ N(1, 0.02),
+    projections ~ N(0, 1/fan_in) so activations stay O(1)."""
+    g = torch.Generator(device="cpu")
+    g.manual_seed(seed)
+    D, F, Q = cfg.d_model, cfg.dim_feedforward, cfg.q_dim
+
+    def n(shape, std=1.0, mean=0.0):
+        return (torch.randn(shape, generator=g) * std + mean).to(dtype).to(device)
+
+    def u(shape, hi):
+        return (torch.rand(shape, generator=g) * hi).to(dtype).to(device)
+
+    w: dict[str, torch.Tensor] = {}
+    for i in range(cfg.n_q):
+        w[f"quantizer.codebook.{i}"] = n((cfg.bins, Q))
+    w["quantizer.rvq_first.output_proj"] = n((D, Q), 1 / math.sqrt(Q))
+    w["quantizer.rvq_rest.output_proj"] = n((D, Q), 1 / math.sqrt(Q))
+    for l in range(cfg.num_layers):
+        p = f"layers.{l}."
+        w[p + "norm1.weight"] = n(D, 0.02, 1.0)
+        w[p + "norm1.bias"] = n(D, 0.02)
+        w[p + "self_attn.in_proj_weight"] = n((3 * D, D), 1 / math.sqrt(D))
+        w[p + "self_attn.out_proj.weight"] = n((D, D), 1 / math.sqrt(D))
+        w[p + "layer_scale_1.scale"] = u(D, 0.1)
+        w[p + "norm2.weight"] = n(D, 0.02, 1.0)
+        w[p + "norm2.bias"] = n(D, 0.02)
+        w[p + "linear1.weight"] = n((F, D), 1 / math.sqrt(D))
+        w[p + "linear2.weight"] = n((D, F), 1 / math.sqrt(F))
+        w[p + "layer_scale_2.scale"] = u(D, 0.1)
+    return w
+
+
+class MimiDecoderChain:
+    """RVQ decode + decoder transformer over whole sequences (offset 0)."""
+
+    def __init__(self, cfg: MimiChainConfig, weights: dict[str, torch.Tensor], cos: torch.Tensor,
+                 sin: torch.Tensor):
+        self.cfg, self.w, self.cos, self.sin = cfg, weights, cos, sin
+        dtype = weights["quantizer.codebook.0"].dtype
+        # StreamingMultiheadAttention: T::from_f32(1 / sqrt(head_dim)) (mimi.rs:1361).
+        self.scale = float(torch.tensor(1.0 / math.sqrt(cfg.head_dim), dtype=torch.float32).to(dtype).float())
+        self.books = [weights[f"quantizer.codebook.{i}"] for i in range(cfg.n_q)]
+
+    # -- RVQ ---------------------------------------------------------------
+    def rvq_decode(self, codes: torch.Tensor) -> torch.Tensor:
+        """codes [B, n_q, T] (int64) -> embeddings [B, T, D]: rvq_first on
+        codebook 0 plus rvq_rest on codebooks 1.., each a gather-sum and a 1x1
+        projection, then added in T."""
+        w = self.w
+        first = xn.rvq_decode_sum(self.books[:1], codes[:, :1].contiguous(), out_layout="btd")
+        x = torch.matmul(first, w["quantizer.rvq_first.output_proj"].t())
+        if self.cfg.n_q > 1:
+            rest = xn.rvq_decode_sum(self.books[1:], codes[:, 1:].contiguous(), out_layout="btd")
+            x = x + torch.matmul(rest, w["quantizer.rvq_rest.output_proj"].t())
+        return x
+
+    # -- transformer -------------------------------------------------------
+    def attention(self, l: int, y: torch.Tensor, offset: int = 0) -> torch.Tensor:
+        cfg, w = self.cfg, self.w
+        B, T, D = y.shape
+        H, hd = cfg.num_heads, cfg.head_dim
+        qkv = torch.matmul(y, w[f"layers.{l}.self_attn.in_proj_weight"].t())  # [B, T, 3D]
+        q, k = xn.rope_qk_packed(qkv, H, self.cos, self.sin, offset, interleaved=True)  # [B, T, H, hd]
+        v = qkv[..., 2 * D:].view(B, T, H, hd)
+        scores = torch.matmul(q.transpose(1, 2), k.permute(0, 2, 3, 1))  # [B, H, T, T]
+        probs = xn.attn_softmax(scores, self.scale, offset)
+        ctx = torch.matmul(probs, v.transpose(1, 2))  # [B, H, T, hd]
+        return torch.matmul(ctx.transpose(1, 2).reshape(B, T, D), w[f"layers.{l}.self_attn.out_proj.weight"].t())
+
+    def mlp(self, l: int, y: torch.Tensor) -> torch.Tensor:
+        w = self.w
+        h = torch.matmul(y, w[f"layers.{l}.linear1.weight"].t())
+        xn.unary_(h, h, "gelu_erf")
+        return torch.matmul(h, w[f"layers.{l}.linear2.weight"].t())
+
+    def transformer(self, x: torch.Tensor, offset: int = 0) -> torch.Tensor:
+        """StreamingTransformer::forward over [B, T, D] with the norm / residual
+        chain fused across layer boundaries."""
+        cfg, w = self.cfg, self.w
+        eps = cfg.eps
+        resid = x
+        y = xn.layer_norm(resid, w["layers.0.norm1.weight"], w["layers.0.norm1.bias"], eps)
+        for l in range(cfg.num_layers):
+            p = f"layers.{l}."
+            attn = self.attention(l, y, offset)
+            # xs = xs + ls1 * attn ; norm2(xs)
+            y2, resid = xn.layer_norm_residual(resid, attn, w[p + "norm2.weight"], w[p + "norm2.bias"], eps,
+                                               layer_scale=w[p + "layer_scale_1.scale"])
+            m = self.mlp(l, y2)
+            if l + 1 < cfg.num_layers:
+                # xs = xs + ls2 * mlp ; next layer's norm1(xs)
+                q = f"layers.{l + 1}."
+                y, resid = xn.layer_norm_residual(resid, m, w[q + "norm1.weight"], w[q + "norm1.bias"], eps,
+                                                  layer_scale=w[p + "layer_scale_2.scale"])
+            else:
+                resid = xn.residual_add(resid, m, w[p + "layer_scale_2.scale"])
+        return resid
+
+    def decode(self, codes: torch.Tensor) -> torch.Tensor:
+        """codes [B, n_q, T] -> decoder-transformer output [B, T, D]."""
+        return self.transformer(self.rvq_decode(codes))

@@ -58,7 +58,11 @@ SIGNATURES = {
     "xn_rope": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _int, _int, _int, _vp],
     "xn_rope_qk": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _int, _int,
                    _int, _vp],
+    "xn_rope_qk_strided": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+                           _int, _int, _vp],
     "xn_unary": [_vp, _vp, _i64, _int, _int, _vp],
+    "xn_residual_add": [_vp, _vp, _vp, _vp, _i64, _i64, _int, _vp],
+    "xn_softmax_scaled": [_vp, _vp, _i64, _i64, _f32, _int, _i64, _i64, _int, _vp],
     "xn_swiglu": [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp],
     "xn_softmax": [_vp, _vp, _i64, _i64, _int, _i64, _i64, _int, _vp],
     "xn_causality_mask": [_vp, _i64, _i64, _i64, _i64, _int, _vp],
@@ -302,6 +306,39 @@ def rope_qk(q: torch.Tensor, k: torch.Tensor, cos, sin, pos: int, *, interleaved
     return qo, ko
 
 
+def rope_qk_packed(qkv: torch.Tensor, heads: int, cos, sin, pos: int, *, kv_heads: int | None = None,
+                   interleaved: bool = True, out: tuple[torch.Tensor, torch.Tensor] | None = None):
+    """RoPE on the Q and K parts of a packed [B, T, (H + 2*Hkv) * D] projection
+    (mimi.rs:1326-1351: narrow, reshape, transpose, contiguous, then rope_i),
+    read in place. Returns rotated (q, k) as contiguous [B, T, H, D] / [B, T, Hkv, D]."""
+    op = "rope_qk_packed"
+    if qkv.dim() != 3 or not qkv.is_contiguous():
+        raise XnError(f"{op}: expected a contiguous [B, T, C] projection, got {tuple(qkv.shape)}")
+    kv_heads = heads if kv_heads is None else kv_heads
+    b, t, c = qkv.shape
+    if c % (heads + 2 * kv_heads):
+        raise XnError(f"{op}: width {c} is not (heads + 2 * kv_heads) * d")
+    d = c // (heads + 2 * kv_heads)
+    _check_same_shape(cos.shape, sin.shape, f"{op} cos/sin")
+    max_pos, d_over_2 = cos.shape
+    if d_over_2 * 2 != d:
+        raise XnError(f"{op} requires even d dimension, got d={d}")
+    if pos + t > max_pos:
+        raise XnError(f"{op} position out of range, pos={pos} + t={t} > max_pos={max_pos}", XN_E_RANGE)
+    qo, ko = out if out is not None else (
+        torch.empty((b, t, heads, d), dtype=qkv.dtype, device=qkv.device),
+        torch.empty((b, t, kv_heads, d), dtype=qkv.dtype, device=qkv.device))
+    if heads != kv_heads:
+        raise XnError(f"{op}: outputs share one token stride; use heads == kv_heads")
+    _dev(qkv, cos, sin, qo, ko)
+    _same_dtype(qkv, cos, sin, qo, ko)
+    esz = qkv.element_size()
+    k_src = qkv.data_ptr() + heads * d * esz
+    _call("xn_rope_qk_strided", _p(qo), _p(qkv), _p(ko), k_src, _p(cos), _p(sin), b, heads, kv_heads, t, d,
+          int(pos), max_pos, c, heads * d, int(interleaved), _dtype_code(qkv), _stream(qkv))
+    return qo, ko
+
+
 # ---------------------------------------------------------------------------
 # Activations (inplace_ops.rs unary_, ops.rs:178-182,458-464)
 # ---------------------------------------------------------------------------
@@ -325,6 +362,26 @@ def silu(x: torch.Tensor) -> torch.Tensor:
 def gelu_erf(x: torch.Tensor) -> torch.Tensor:
     out = torch.empty_like(x)
     unary_(out, x, "gelu_erf")
+    return out
+
+
+def residual_add_(dst: torch.Tensor, x: torch.Tensor, branch: torch.Tensor,
+                  layer_scale: torch.Tensor | None = None) -> None:
+    """dst = x + layer_scale * branch (LayerScale then add, mimi.rs:1441-1444)."""
+    _check_same_shape(x.shape, branch.shape, "residual_add_ branch")
+    _check_same_shape(dst.shape, x.shape, "residual_add_ dst")
+    rows, cols = _rows_cols(dst)
+    if layer_scale is not None:
+        _check_same_shape(layer_scale.shape, (cols,), "residual_add_ layer_scale")
+    _dev(dst, x, branch, layer_scale)
+    _same_dtype(dst, x, branch, layer_scale)
+    _call("xn_residual_add", _p(dst), _p(x), _p(branch), _p(layer_scale), rows, cols, _dtype_code(dst),
+          _stream(dst))
+
+
+def residual_add(x: torch.Tensor, branch: torch.Tensor, layer_scale: torch.Tensor | None = None) -> torch.Tensor:
+    out = torch.empty_like(x)
+    residual_add_(out, x, branch, layer_scale)
     return out
 
 
@@ -407,6 +464,29 @@ def softmax_causal_(dst: torch.Tensor, src: torch.Tensor, offset: int) -> None:
 def softmax_causal(x: torch.Tensor, offset: int) -> torch.Tensor:
     out = torch.empty_like(x)
     softmax_causal_(out, x, offset)
+    return out
+
+
+def attn_softmax_(dst: torch.Tensor, scores: torch.Tensor, scale: float, offset: int | None = None) -> None:
+    """softmax(mask(T(scores * scale))) over the last dimension: the score
+    scale, optional causal mask (offset given) and softmax of mimi.rs:1361-1368
+    in one pass. `scale` is the T-typed scale value."""
+    _check_same_shape(dst.shape, scores.shape, "attn_softmax_")
+    _dev(dst, scores)
+    _same_dtype(dst, scores)
+    if offset is None:
+        rows, cols = _rows_cols(dst)
+        _call("xn_softmax_scaled", _p(dst), _p(scores), rows, cols, float(scale), 0, 1, 0, _dtype_code(dst),
+              _stream(dst))
+    else:
+        bh, t1, t2 = _mask_dims(scores, "attn_softmax_")
+        _call("xn_softmax_scaled", _p(dst), _p(scores), bh * t1, t2, float(scale), 1, max(t1, 1), int(offset),
+              _dtype_code(dst), _stream(dst))
+
+
+def attn_softmax(scores: torch.Tensor, scale: float, offset: int | None = None) -> torch.Tensor:
+    out = torch.empty_like(scores)
+    attn_softmax_(out, scores, scale, offset)
     return out
 
 

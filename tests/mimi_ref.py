@@ -1,0 +1,64 @@
+"""CPU reference of the Mimi decoder chain (test infrastructure).
+
+The reference's own op sequence (mimi-rs/src/models/mimi.rs:1317-1445,
+1476-1483, 1730-1868), unfused, on the oracle's restatement of the CPU backend
+ops. GEMMs are f32 matrix products of the T-typed operands, rounded to T, as
+the reference's GEMM returns T values (their summation order is the one thing
+no two GEMM libraries share, so the chain is compared with a tolerance).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from helpers import storage_to_f32, to_storage
+
+
+def _mm(a: np.ndarray, b_t: np.ndarray, dtype: str) -> np.ndarray:
+    """a [..., K] @ b_t[N, K]^T in f32, rounded to T."""
+    af, bf = storage_to_f32(a, dtype), storage_to_f32(b_t, dtype)
+    return to_storage(np.matmul(af, bf.T), dtype)
+
+
+def _bmm(a: np.ndarray, b: np.ndarray, dtype: str) -> np.ndarray:
+    return to_storage(np.matmul(storage_to_f32(a, dtype), storage_to_f32(b, dtype)), dtype)
+
+
+def chain_ref(oracle, cfg, w: dict, cos: np.ndarray, sin: np.ndarray, codes: np.ndarray, dtype: str,
+              scale: float) -> np.ndarray:
+    """codes [B, n_q, T] -> [B, T, D]. `w` holds numpy storage arrays keyed as
+    mimi_chain.synthetic_weights; `scale` is the T-typed 1/sqrt(head_dim)."""
+    B, _, T = codes.shape
+    D, H = cfg.d_model, cfg.num_heads
+    hd = D // H
+    # SplitResidualVectorQuantizer::decode: rvq_first + rvq_rest, each with its projection.
+    books = [w[f"quantizer.codebook.{i}"] for i in range(cfg.n_q)]
+    first = oracle.rvq_decode(books[:1], np.ascontiguousarray(codes[:, :1]), dtype, "btd")
+    x = _mm(first, w["quantizer.rvq_first.output_proj"], dtype)
+    if cfg.n_q > 1:
+        rest = oracle.rvq_decode(books[1:], np.ascontiguousarray(codes[:, 1:]), dtype, "btd")
+        x = oracle.binary(x, _mm(rest, w["quantizer.rvq_rest.output_proj"], dtype), "add", dtype)
+    scale_row = to_storage(np.full(T, scale, dtype=np.float32), dtype)
+    for l in range(cfg.num_layers):
+        p = f"layers.{l}."
+        y = oracle.layer_norm(x, w[p + "norm1.weight"], w[p + "norm1.bias"], cfg.eps, dtype)
+        qkv = _mm(y, w[p + "self_attn.in_proj_weight"], dtype)
+        heads = []
+        for part in range(3):
+            t = qkv[..., part * D:(part + 1) * D].reshape(B, T, H, hd)
+            heads.append(np.ascontiguousarray(np.swapaxes(t, 1, 2)))  # [B, H, T, hd]
+        q = oracle.rope(heads[0], cos, sin, 0, dtype, interleaved=True)
+        k = oracle.rope(heads[1], cos, sin, 0, dtype, interleaved=True)
+        v = heads[2]
+        scores = _bmm(q, np.ascontiguousarray(np.swapaxes(k, 2, 3)), dtype)
+        scores = oracle.broadcast_rows(scores, scale_row, "mul", dtype)
+        probs = oracle.softmax_causal(scores, 0, dtype)
+        ctx = _bmm(probs, v, dtype)
+        attn = _mm(np.ascontiguousarray(np.swapaxes(ctx, 1, 2)).reshape(B, T, D), w[p + "self_attn.out_proj.weight"],
+                   dtype)
+        x = oracle.residual_prologue(x, attn, w[p + "layer_scale_1.scale"], dtype)
+        y2 = oracle.layer_norm(x, w[p + "norm2.weight"], w[p + "norm2.bias"], cfg.eps, dtype)
+        h = _mm(y2, w[p + "linear1.weight"], dtype)
+        h = oracle.unary(h, "gelu_erf", dtype)
+        m = _mm(h, w[p + "linear2.weight"], dtype)
+        x = oracle.residual_prologue(x, m, w[p + "layer_scale_2.scale"], dtype)
+    return x

@@ -1,0 +1,76 @@
+"""End-to-end parity of the Mimi decoder chain (benchmark config 2 shapes:
+batch 4, 250 frames, d_model 512, 8 heads of 64, 8 layers, FFN 2048, 8
+codebooks of 2048 x 256) against the reference op sequence on the CPU oracle,
+with seeded synthetic weights (no checkpoint is available offline)."""
+import numpy as np
+import pytest
+import torch
+
+from helpers import from_device
+from mimi_ref import chain_ref
+
+pytestmark = pytest.mark.gpu
+
+
+def _setup(dtype_name, cfg_kwargs, B, T, seed=0):
+    import mimi_chain as mc
+
+    tdt = {"f32": torch.float32, "bf16": torch.bfloat16}[dtype_name]
+    cfg = mc.MimiChainConfig(**cfg_kwargs)
+    dev = torch.device("cuda:0")
+    w = mc.synthetic_weights(cfg, tdt, dev, seed)
+    cos, sin = mc.rope_tables(cfg, tdt, dev)
+    chain = mc.MimiDecoderChain(cfg, w, cos, sin)
+    g = torch.Generator().manual_seed(seed + 1)
+    codes = torch.randint(0, cfg.bins, (B, cfg.n_q, T), generator=g, dtype=torch.int64)
+    return mc, cfg, w, cos, sin, chain, codes, dev
+
+
+def _np(w, dtype_name):
+    return {k: from_device(v, dtype_name) for k, v in w.items()}
+
+
+@pytest.mark.parametrize("dtype,tol", [("f32", 2e-4), ("bf16", 5e-2)])
+def test_mimi_chain_matches_reference_sequence(oracle, xn, cuda, dtype, tol):
+    """Full config-2 chain. f32: max |error| <= 2e-4 * rms(output); the GEMM
+    libraries' summation orders differ (cuBLAS vs numpy), nothing else does.
+    bf16: the same, at bf16 resolution (one-ulp GEMM differences propagate
+    through 8 layers), checked as a relative RMS error."""
+    mc, cfg, w, cos, sin, chain, codes, dev = _setup(dtype, {}, 4, 250)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    got = from_device(chain.decode(codes.to(dev)), dtype)
+    ref = chain_ref(oracle, cfg, _np(w, dtype), from_device(cos, dtype), from_device(sin, dtype), codes.numpy(),
+                    dtype, chain.scale)
+    from helpers import storage_to_f32
+
+    g, r = storage_to_f32(got, dtype).astype(np.float64), storage_to_f32(ref, dtype).astype(np.float64)
+    rms = np.sqrt(np.mean(r ** 2))
+    if dtype == "f32":
+        err = np.max(np.abs(g - r)) / rms
+    else:
+        err = np.sqrt(np.mean((g - r) ** 2)) / rms
+    print(f"mimi chain {dtype}: error {err:.3e} of rms {rms:.3f}")
+    assert err <= tol
+
+
+def test_mimi_rvq_stage_exact(oracle, xn, cuda):
+    """The RVQ gather-sums are bit-exact; only the projection GEMM differs."""
+    mc, cfg, w, cos, sin, chain, codes, dev = _setup("f32", {}, 2, 37)
+    books = [from_device(w[f"quantizer.codebook.{i}"], "f32") for i in range(cfg.n_q)]
+    c = codes.numpy()
+    ref_rest = oracle.rvq_decode(books[1:], np.ascontiguousarray(c[:, 1:]), "f32", "btd")
+    got_rest = xn.rvq_decode_sum([w[f"quantizer.codebook.{i}"] for i in range(1, cfg.n_q)],
+                                 codes[:, 1:].contiguous().to(dev), out_layout="btd")
+    assert np.array_equal(from_device(got_rest, "f32"), ref_rest)
+
+
+def test_mimi_chain_small_config_f32(oracle, xn, cuda):
+    """A 2-layer, 4-head variant with ragged frame count."""
+    kw = dict(d_model=64, num_heads=4, num_layers=2, dim_feedforward=128, n_q=3, bins=64, q_dim=32)
+    mc, cfg, w, cos, sin, chain, codes, dev = _setup("f32", kw, 3, 17)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    got = from_device(chain.decode(codes.to(dev)), "f32")
+    ref = chain_ref(oracle, cfg, _np(w, "f32"), from_device(cos, "f32"), from_device(sin, "f32"), codes.numpy(),
+                    "f32", chain.scale)
+    rms = np.sqrt(np.mean(ref.astype(np.float64) ** 2))
+    assert np.max(np.abs(got.astype(np.float64) - ref)) <= 2e-4 * rms

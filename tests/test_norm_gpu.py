@@ -115,3 +115,15 @@ def test_norm_deterministic(xn, cuda):
     a = xn.rms_norm(X, W, 1e-5)
     b = xn.rms_norm(X, W, 1e-5)
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("rows,cols", [(1000, 512), (7, 100), (3, 1)])
+@pytest.mark.parametrize("with_ls", [True, False])
+def test_residual_add(oracle, xn, cuda, dtype, rows, cols, with_ls):
+    """x + LayerScale(branch), bit-exact (mimi.rs:1441-1444)."""
+    x, br, _, _, ls = _inputs(rows + cols, rows, cols, dtype)
+    ref = oracle.residual_prologue(x, br, ls if with_ls else None, dtype)
+    Y = xn.residual_add(to_device(x, dtype, cuda), to_device(br, dtype, cuda),
+                        to_device(ls, dtype, cuda) if with_ls else None)
+    assert np.array_equal(from_device(Y, dtype), ref)

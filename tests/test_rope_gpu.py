@@ -85,3 +85,23 @@ def test_rope_inplace_and_errors(oracle, xn, cuda):
     with pytest.raises(xn.XnError, match="even d"):
         xn.rope(torch.zeros(1, 1, 2, 3, device=cuda), torch.zeros(4, 1, device=cuda),
                 torch.zeros(4, 1, device=cuda), 0)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("interleaved", [True, False])
+@pytest.mark.parametrize("b,t,h,d,pos", [(4, 250, 8, 64, 0), (16, 1, 16, 64, 77), (2, 9, 3, 6, 1)])
+def test_rope_qk_packed_projection(oracle, xn, cuda, dtype, interleaved, b, t, h, d, pos):
+    """Q and K read in place from the packed QKV projection equal the reference's
+    narrow -> reshape -> transpose -> contiguous -> rope_i (mimi.rs:1332-1351)."""
+    r = rng(b * t + h * d + pos)
+    qkv = to_storage(randn(r, (b, t, 3 * h * d)), dtype)
+    cos, sin = oracle.rope_tables(d, pos + t + 3, 10000.0, dtype, "mimi")
+    ref = []
+    for part in range(2):
+        x = np.ascontiguousarray(qkv[..., part * h * d:(part + 1) * h * d].reshape(b, t, h, d).swapaxes(1, 2))
+        y = oracle.rope(x, cos, sin, pos, dtype, interleaved=interleaved)
+        ref.append(np.ascontiguousarray(y.swapaxes(1, 2)))
+    Q, K = xn.rope_qk_packed(to_device(qkv, dtype, cuda), h, to_device(cos, dtype, cuda), to_device(sin, dtype, cuda),
+                             pos, interleaved=interleaved)
+    assert np.array_equal(from_device(Q, dtype), ref[0])
+    assert np.array_equal(from_device(K, dtype), ref[1])

@@ -57,3 +57,20 @@ def test_softmax_decode_steps(oracle, xn, cuda):
         x = to_storage(randn(r, (16, 16, 1, t), 1.0), "bf16")
         Y = xn.softmax(to_device(x, "bf16", cuda))
         assert_close(from_device(Y, "bf16"), oracle.softmax(x, "bf16"), "bf16", f"decode t={t}")
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("shape,offset,scale", [((4, 8, 250, 250), 0, 0.125), ((16, 16, 1, 200), 199, 0.125),
+                                                ((2, 3, 7, 7), None, 0.3), ((1, 2, 5, 20000), 19995, 0.125)])
+def test_attn_softmax_scaled(oracle, xn, cuda, dtype, shape, offset, scale):
+    """T(scores * scale), causal mask, softmax in one pass == the reference's
+    `scale` (cpu_backend.rs:260-276), apply_causality_mask and softmax."""
+    r = rng(sum(shape) + int(scale * 100))
+    s = to_storage(randn(r, shape, 4.0), dtype)
+    sc = to_storage(np.full(shape[-1], scale, dtype=np.float32), dtype)  # the T-typed scale
+    scaled = oracle.broadcast_rows(s, sc, "mul", dtype)
+    ref = oracle.softmax(scaled, dtype) if offset is None else oracle.softmax_causal(scaled, offset, dtype)
+    scale_t = float(np.asarray(sc[:1]).view(np.float32)[0]) if dtype == "f32" else float(
+        np.frombuffer(np.array([int(sc[0]) << 16], dtype=np.uint32).tobytes(), dtype=np.float32)[0])
+    Y = xn.attn_softmax(to_device(s, dtype, cuda), scale_t, offset)
+    assert_close(from_device(Y, dtype), ref, dtype, f"attn_softmax {dtype} {shape}")
