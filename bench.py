@@ -338,13 +338,13 @@ def mimi_rate(torch, device, steps: int, batch: int = 4, frames: int = 250) -> d
 SWEEP_OPS = ["rms_norm_residual", "layer_norm", "rope", "swiglu", "softmax", "embedding_gather"]
 
 
-def sweep(torch, xn, device, widths, rows_list, dtypes, reps: int, mem_cap_gb: float) -> list[dict]:
+def sweep(torch, xn, device, widths, rows_list, dtypes, reps: int, mem_cap_gb: float, ops=SWEEP_OPS) -> list[dict]:
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)  # 256 MB > L2
     out = []
     for dname in dtypes:
         dt = {"f32": torch.float32, "bf16": torch.bfloat16}[dname]
         s = 4 if dname == "f32" else 2
-        for op in SWEEP_OPS:
+        for op in ops:
             for cols in widths:
                 for rows in rows_list:
                     n_tensors = {"rms_norm_residual": 4, "layer_norm": 2, "rope": 2, "swiglu": 3, "softmax": 2,
@@ -473,6 +473,30 @@ class CpuSample:
         return sum(self.bytes.values())
 
 
+def cpu_mimi_rate(batch: int = 1, frames: int = 250) -> dict:
+    """The reference op sequence of the Mimi decoder chain on the CPU oracle
+    (numpy f32 GEMMs rounded to bf16), one decode timed after a warm-up."""
+    import numpy as np
+    import torch
+
+    import mimi_chain as mc
+    import mimi_oracle
+    import xn_oracle
+
+    cfg = mc.MimiChainConfig()
+    w = {k: mimi_oracle.to_storage(v.float().numpy(), "bf16")
+         for k, v in mc.synthetic_weights(cfg, torch.float32, "cpu", seed=7).items()}
+    cos, sin = (mimi_oracle.to_storage(t.float().numpy(), "bf16") for t in mc.rope_tables(cfg, torch.float32, "cpu"))
+    codes = np.random.default_rng(8).integers(0, cfg.bins, size=(batch, cfg.n_q, frames), dtype=np.int64)
+    scale = 0.125
+    mimi_oracle.chain_ref(xn_oracle, cfg, w, cos, sin, codes[:, :, :8], "bf16", scale)
+    t0 = time.perf_counter()
+    mimi_oracle.chain_ref(xn_oracle, cfg, w, cos, sin, codes, "bf16", scale)
+    dt = time.perf_counter() - t0
+    return {"frames_per_s": round(batch * frames / dt, 1),
+            "sample": f"{batch} x {frames} frames, bf16, oracle ops + numpy f32 GEMMs, {os.cpu_count()} threads"}
+
+
 def cpu_rate(rows: int, steps: int, warmup: int) -> dict:
     import xn_oracle
 
@@ -538,6 +562,7 @@ def main() -> int:
     ap.add_argument("--sweep-rows", default="1024,16384,262144,1048576")
     ap.add_argument("--sweep-dtypes", default="f32,bf16")
     ap.add_argument("--sweep-mem-gb", type=float, default=48.0)
+    ap.add_argument("--sweep-ops", default=",".join(SWEEP_OPS))
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -559,7 +584,7 @@ def main() -> int:
         peak, _ = measured_peak()
         pts = sweep(torch, xn, dev, [int(v) for v in args.sweep_widths.split(",")],
                     [int(v) for v in args.sweep_rows.split(",")], args.sweep_dtypes.split(","), max(3, args.steps),
-                    args.sweep_mem_gb)
+                    args.sweep_mem_gb, [o for o in args.sweep_ops.split(",") if o])
         for pt in pts:
             if "gbs" in pt:
                 pt["frac"] = round(pt["gbs"] / peak, 3)
@@ -682,6 +707,8 @@ def main() -> int:
         if not args.no_cpu_baseline and world == 1:
             cb = cpu_rate(args.cpu_rows, 3, 1)
             line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+            if mimi is not None:
+                line["cpu_baseline"]["mimi_decode"] = cpu_mimi_rate()
         print(json.dumps(line), flush=True)
     if distributed:
         dist.barrier()

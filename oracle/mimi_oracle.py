@@ -1,4 +1,6 @@
-"""CPU reference of the Mimi decoder chain (test infrastructure).
+"""CPU restatement of the Mimi decoder chain (test infrastructure).
+
+TEST INFRASTRUCTURE ONLY: used by tests/ and by bench.py's CPU-baseline leg.
 
 The reference's own op sequence (mimi-rs/src/models/mimi.rs:1317-1445,
 1476-1483, 1730-1868), unfused, on the oracle's restatement of the CPU backend
@@ -10,7 +12,30 @@ from __future__ import annotations
 
 import numpy as np
 
-from helpers import storage_to_f32, to_storage
+import xn_oracle as oracle_mod
+
+
+def storage_to_f32(a: np.ndarray, dtype: str) -> np.ndarray:
+    """T storage (f32, or uint16 bits of bf16 / f16) widened to f32."""
+    a = np.ascontiguousarray(a)
+    if dtype == "f32":
+        return a.astype(np.float32)
+    if dtype == "bf16":
+        return (a.astype(np.uint32) << 16).view(np.float32)
+    return a.view(np.float16).astype(np.float32)
+
+
+def to_storage(a: np.ndarray, dtype: str) -> np.ndarray:
+    """f32 values rounded to T (round-to-nearest-even), as storage."""
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    if dtype == "f32":
+        return a
+    if dtype == "f16":
+        return a.astype(np.float16).view(np.uint16)
+    u = a.view(np.uint32)
+    nan = (u & 0x7FFFFFFF) > 0x7F800000
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    return np.where(nan, ((u >> 16) | 0x40).astype(np.uint16), r)
 
 
 def _mm(a: np.ndarray, b_t: np.ndarray, dtype: str) -> np.ndarray:
@@ -25,6 +50,7 @@ def _bmm(a: np.ndarray, b: np.ndarray, dtype: str) -> np.ndarray:
 
 def chain_ref(oracle, cfg, w: dict, cos: np.ndarray, sin: np.ndarray, codes: np.ndarray, dtype: str,
               scale: float) -> np.ndarray:
+    # `oracle` is the xn_oracle module (passed explicitly so callers control its build).
     """codes [B, n_q, T] -> [B, T, D]. `w` holds numpy storage arrays keyed as
     mimi_chain.synthetic_weights; `scale` is the T-typed 1/sqrt(head_dim)."""
     B, _, T = codes.shape

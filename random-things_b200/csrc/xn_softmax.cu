@@ -14,6 +14,8 @@
 // group reductions. Rows wider than 16384 elements use a three-pass kernel.
 #include <math.h>
 
+#include <type_traits>
+
 #include "xn_common.cuh"
 #include "xn_internal.h"
 
@@ -40,7 +42,41 @@ __device__ __forceinline__ int64_t row_limit(const SoftmaxParams &p, int64_t row
   return lim < p.cols ? lim : p.cols;
 }
 
-template <typename T, bool kVector, int NV>
+// Paired 16-bit types for the packed (vector) path.
+template <typename T>
+struct Pair;
+template <>
+struct Pair<__nv_bfloat16> {
+  using T2 = __nv_bfloat162;
+  __device__ __forceinline__ static T2 splat(float v) { return __float2bfloat162_rn(v); }
+  __device__ __forceinline__ static float2 to_f2(T2 v) { return __bfloat1622float2(v); }
+  __device__ __forceinline__ static T2 from_f2(float a, float b) { return __floats2bfloat162_rn(a, b); }
+  __device__ __forceinline__ static T2 neg_inf() { return splat(-INFINITY); }
+  // Keeps the low element, sets the high one to -inf.
+  __device__ __forceinline__ static T2 mask_high(T2 v) {
+    return __halves2bfloat162(__low2bfloat16(v), __float2bfloat16(-INFINITY));
+  }
+};
+template <>
+struct Pair<__half> {
+  using T2 = __half2;
+  __device__ __forceinline__ static T2 splat(float v) { return __float2half2_rn(v); }
+  __device__ __forceinline__ static float2 to_f2(T2 v) { return __half22float2(v); }
+  __device__ __forceinline__ static T2 from_f2(float a, float b) { return __floats2half2_rn(a, b); }
+  __device__ __forceinline__ static T2 neg_inf() { return splat(-INFINITY); }
+  __device__ __forceinline__ static T2 mask_high(T2 v) {
+    return __halves2half2(__low2half(v), __float2half(-INFINITY));
+  }
+};
+
+// One row per row group, held in registers. Steps, in the reference's T
+// arithmetic (cpu_backend.rs:667-689): [x = T(x * scale)], max, e = T(exp(T(x -
+// max))), sum of f32(e), y = T(e / sum). For 16-bit T the row stays packed and
+// the max, the subtraction and the scale run as paired bf16x2 / f16x2
+// instructions, which round exactly once as the reference's T operations do;
+// exp and the division run in f32. Causal rows (kCausal) treat columns past
+// offset + (row % t1) as -inf, i.e. they are neither read nor exp'd and give 0.
+template <typename T, bool kVector, int NV, bool kCausal>
 __global__ void __launch_bounds__(512) softmax_regs_kernel(const SoftmaxParams p) {
   constexpr int N = kVector ? Elem<T>::kVec : 1;
   __shared__ float red[32];
@@ -50,67 +86,266 @@ __global__ void __launch_bounds__(512) softmax_regs_kernel(const SoftmaxParams p
   const int rpb = blockDim.x / tpr;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * rpb + g;
   const bool active = row < p.rows;
-  const int64_t base = row * p.cols;
-  const int64_t lim = active ? row_limit(p, row) : 0;
-  const T *src = static_cast<const T *>(p.src);
-  T *dst = static_cast<T *>(p.dst);
+  const int cols = static_cast<int>(p.cols);
+  int lim = active ? cols : 0;
+  if constexpr (kCausal) {
+    if (active) {
+      const int64_t l = p.offset + (row % p.t1) + 1;
+      lim = l < cols ? static_cast<int>(l) : cols;
+    }
+  }
+  const T *src = static_cast<const T *>(p.src) + row * p.cols;
+  T *dst = static_cast<T *>(p.dst) + row * p.cols;
 
-  float x[NV][N];
-  float mx = -INFINITY;
+  if constexpr (kVector && !std::is_same_v<T, float>) {
+    using P = Pair<T>;
+    using T2 = typename P::T2;
+    constexpr int W = N / 2;  // pairs per vector
+    uint4 raw[NV];
+    T2 mx2 = P::neg_inf();
+    const T2 sc2 = P::splat(p.scale);
 #pragma unroll
-  for (int k = 0; k < NV; ++k) {
-    const int64_t e0 = static_cast<int64_t>(lr + k * tpr) * N;
-    if (active && lr + k * tpr < p.nvec && e0 < lim) {
-      if constexpr (kVector) {
-        unpack<T>(ld_stream(src + base + e0), x[k]);
+    for (int k = 0; k < NV; ++k) {
+      const int e0 = (lr + k * tpr) * N;
+      if (e0 < lim) {
+        raw[k] = ld_stream(src + e0);
+        T2 *w = reinterpret_cast<T2 *>(&raw[k]);
+#pragma unroll
+        for (int j = 0; j < W; ++j) {
+          if (p.scaled) w[j] = __hmul2(w[j], sc2);
+          if constexpr (kCausal) {
+            if (e0 + 2 * j >= lim) w[j] = P::neg_inf();
+            else if (e0 + 2 * j + 1 >= lim) w[j] = P::mask_high(w[j]);
+          }
+          mx2 = __hmax2(mx2, w[j]);
+        }
       } else {
-        x[k][0] = Elem<T>::to_f32(src[base + e0]);
+#pragma unroll
+        for (int j = 0; j < W; ++j) reinterpret_cast<T2 *>(&raw[k])[j] = P::neg_inf();
       }
+    }
+    const float2 mf = P::to_f2(mx2);
+    const float mx = group_max(fmaxf(mf.x, mf.y), tpr, red);
+    const T2 m2 = P::splat(mx);  // exact: mx is a T value
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      T2 *w = reinterpret_cast<T2 *>(&raw[k]);
+#pragma unroll
+      for (int j = 0; j < W; ++j) {
+        const float2 d = P::to_f2(__hsub2(w[j], m2));  // T(x - max); -inf stays -inf
+        const T2 e = P::from_f2(expf(d.x), expf(d.y));  // T(exp(...)); exp(-inf) = 0
+        const float2 ef = P::to_f2(e);
+        s = __fadd_rn(__fadd_rn(s, ef.x), ef.y);
+        w[j] = e;
+      }
+    }
+    s = group_sum(s, tpr, red);
+    const float rs = __frcp_rn(s);  // s >= 1: the row maximum contributes exp(0)
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int e0 = (lr + k * tpr) * N;
+      if (active && lr + k * tpr < p.nvec) {
+        T2 *w = reinterpret_cast<T2 *>(&raw[k]);
+#pragma unroll
+        for (int j = 0; j < W; ++j) {
+          const float2 e = P::to_f2(w[j]);
+          w[j] = P::from_f2(div_by(e.x, s, rs), div_by(e.y, s, rs));
+        }
+        st_vec(dst + e0, raw[k]);
+      }
+    }
+  } else {
+    float x[NV][N];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int e0 = (lr + k * tpr) * N;
+      if (e0 < lim) {
+        if constexpr (kVector) {
+          unpack<T>(ld_stream(src + e0), x[k]);
+        } else {
+          x[k][0] = Elem<T>::to_f32(src[e0]);
+        }
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+          if (p.scaled) x[k][j] = Elem<T>::round(__fmul_rn(x[k][j], Elem<T>::round(p.scale)));
+          if constexpr (kCausal) {
+            if (e0 + j >= lim) x[k][j] = -INFINITY;
+          }
+          mx = fmaxf(mx, x[k][j]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < N; ++j) x[k][j] = -INFINITY;
+      }
+    }
+    mx = group_max(mx, tpr, red);
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
 #pragma unroll
       for (int j = 0; j < N; ++j) {
-        if (e0 + j >= lim) {
-          x[k][j] = -INFINITY;
-        } else if (p.scaled) {
-          x[k][j] = Elem<T>::round(__fmul_rn(x[k][j], p.scale));
-        }
-        mx = fmaxf(mx, x[k][j]);
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < N; ++j) x[k][j] = -INFINITY;
-    }
-  }
-  mx = group_max(mx, tpr, red);
-  float s = 0.f;
-#pragma unroll
-  for (int k = 0; k < NV; ++k) {
-    const int64_t e0 = static_cast<int64_t>(lr + k * tpr) * N;
-#pragma unroll
-    for (int j = 0; j < N; ++j) {
-      if (e0 + j < lim) {
+        // exp(-inf - max) = 0 for masked and padding entries.
         x[k][j] = Elem<T>::round(expf(Elem<T>::round(__fsub_rn(x[k][j], mx))));
         s = __fadd_rn(s, x[k][j]);
-      } else {
-        x[k][j] = 0.f;
+      }
+    }
+    s = group_sum(s, tpr, red);
+    const float rs = __frcp_rn(s);
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int vi = lr + k * tpr;
+      if (active && vi < p.nvec) {
+        const int e0 = vi * N;
+        float y[N];
+#pragma unroll
+        for (int j = 0; j < N; ++j) y[j] = div_by(x[k][j], s, rs);
+        if constexpr (kVector) {
+          st_vec(dst + e0, pack<T>(y));
+        } else {
+          dst[e0] = Elem<T>::from_f32(y[0]);
+        }
       }
     }
   }
-  s = group_sum(s, tpr, red);
-  const float rs = __frcp_rn(s);  // s >= 1: the row maximum contributes exp(0)
+}
+
+// Vector rows, persistent and prefetching: each row group walks rows
+// row, row + step, ... (step = all groups of the grid) and issues the loads of
+// its next row before computing the current one, so HBM reads stay in flight
+// through the reductions and the exp / divide work. Arithmetic as
+// softmax_regs_kernel. The loop bound depends only on the block, so blocks
+// whose row groups span several warps keep their __syncthreads uniform.
+template <typename T, int NV, bool kCausal>
+__global__ void __launch_bounds__(512, NV >= 8 ? 1 : 2) softmax_pipe_kernel(const SoftmaxParams p) {
+  constexpr int N = Elem<T>::kVec;
+  __shared__ float red[32];
+  const int tpr = p.tpr;
+  const int g = threadIdx.x / tpr;
+  const int lr = threadIdx.x - g * tpr;
+  const int rpb = blockDim.x / tpr;
+  const int64_t step = static_cast<int64_t>(gridDim.x) * rpb;
+  const int cols = static_cast<int>(p.cols);
+  const T *src = static_cast<const T *>(p.src);
+  T *dst = static_cast<T *>(p.dst);
+  auto row_lim = [&](int64_t r) -> int {
+    if (r >= p.rows) return 0;
+    if constexpr (kCausal) {
+      const int64_t l = p.offset + (r % p.t1) + 1;
+      return l < cols ? static_cast<int>(l) : cols;
+    } else {
+      return cols;
+    }
+  };
+  auto load_row = [&](int64_t r, uint4 (&buf)[NV]) {
+    const int lim = row_lim(r);
 #pragma unroll
-  for (int k = 0; k < NV; ++k) {
-    const int vi = lr + k * tpr;
-    if (active && vi < p.nvec) {
-      const int64_t e0 = static_cast<int64_t>(vi) * N;
-      float y[N];
+    for (int k = 0; k < NV; ++k) {
+      const int e0 = (lr + k * tpr) * N;
+      if (e0 < lim) buf[k] = ld_stream(src + r * p.cols + e0);
+    }
+  };
+  uint4 cur[NV], nxt[NV];
+  int64_t row = static_cast<int64_t>(blockIdx.x) * rpb + g;
+  load_row(row, cur);
+  for (int64_t base = static_cast<int64_t>(blockIdx.x) * rpb; base < p.rows; base += step, row += step) {
+    load_row(row + step, nxt);  // prefetch the next row of this group
+    const int lim = row_lim(row);
+    float s = 0.f, mx;
+    if constexpr (std::is_same_v<T, float>) {
+      float m = -INFINITY;
+      const float sc = p.scale;
 #pragma unroll
-      for (int j = 0; j < N; ++j) y[j] = e0 + j < lim ? div_by(x[k][j], s, rs) : 0.f;
-      if constexpr (kVector) {
-        st_vec(dst + base + e0, pack<T>(y));
-      } else {
-        dst[base + e0] = Elem<T>::from_f32(y[0]);
+      for (int k = 0; k < NV; ++k) {
+        const int e0 = (lr + k * tpr) * N;
+        float *x = reinterpret_cast<float *>(&cur[k]);
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+          if (e0 + j < lim) {
+            if (p.scaled) x[j] = __fmul_rn(x[j], sc);
+          } else {
+            x[j] = -INFINITY;
+          }
+          m = fmaxf(m, x[j]);
+        }
+      }
+      mx = group_max(m, tpr, red);
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        float *x = reinterpret_cast<float *>(&cur[k]);
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+          x[j] = expf(__fsub_rn(x[j], mx));  // exp(-inf - max) = 0 for masked / padding
+          s = __fadd_rn(s, x[j]);
+        }
+      }
+    } else {
+      using P = Pair<T>;
+      using T2 = typename P::T2;
+      constexpr int W = N / 2;
+      T2 mx2 = P::neg_inf();
+      const T2 sc2 = P::splat(p.scale);
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        const int e0 = (lr + k * tpr) * N;
+        T2 *w = reinterpret_cast<T2 *>(&cur[k]);
+#pragma unroll
+        for (int j = 0; j < W; ++j) {
+          if (e0 + 2 * j + 1 < lim) {
+            if (p.scaled) w[j] = __hmul2(w[j], sc2);
+          } else if (e0 + 2 * j < lim) {
+            if (p.scaled) w[j] = __hmul2(w[j], sc2);
+            w[j] = P::mask_high(w[j]);
+          } else {
+            w[j] = P::neg_inf();
+          }
+          mx2 = __hmax2(mx2, w[j]);
+        }
+      }
+      const float2 mf = P::to_f2(mx2);
+      mx = group_max(fmaxf(mf.x, mf.y), tpr, red);
+      const T2 m2 = P::splat(mx);  // exact: mx is a T value
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        T2 *w = reinterpret_cast<T2 *>(&cur[k]);
+#pragma unroll
+        for (int j = 0; j < W; ++j) {
+          const float2 d = P::to_f2(__hsub2(w[j], m2));  // T(x - max)
+          const T2 e = P::from_f2(expf(d.x), expf(d.y));  // T(exp(...))
+          const float2 ef = P::to_f2(e);
+          s = __fadd_rn(__fadd_rn(s, ef.x), ef.y);
+          w[j] = e;
+        }
       }
     }
+    s = group_sum(s, tpr, red);
+    const float rs = __frcp_rn(s);  // s >= 1 for a live row: its maximum contributes exp(0)
+    if (row < p.rows) {
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        const int vi = lr + k * tpr;
+        if (vi < p.nvec) {
+          if constexpr (std::is_same_v<T, float>) {
+            float *x = reinterpret_cast<float *>(&cur[k]);
+#pragma unroll
+            for (int j = 0; j < N; ++j) x[j] = div_by(x[j], s, rs);
+          } else {
+            using P = Pair<T>;
+            using T2 = typename P::T2;
+            T2 *w = reinterpret_cast<T2 *>(&cur[k]);
+#pragma unroll
+            for (int j = 0; j < N / 2; ++j) {
+              const float2 e = P::to_f2(w[j]);
+              w[j] = P::from_f2(div_by(e.x, s, rs), div_by(e.y, s, rs));
+            }
+          }
+          st_vec(dst + row * p.cols + vi * N, cur[k]);
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < NV; ++k) cur[k] = nxt[k];
   }
 }
 
@@ -127,7 +362,7 @@ __global__ void __launch_bounds__(1024) softmax_loop_kernel(const SoftmaxParams 
   const int tpr = blockDim.x;
   auto load = [&](int64_t c) -> float {
     const float x = Elem<T>::to_f32(src[base + c]);
-    return p.scaled ? Elem<T>::round(__fmul_rn(x, p.scale)) : x;
+    return p.scaled ? Elem<T>::round(__fmul_rn(x, Elem<T>::round(p.scale))) : x;
   };
   float mx = -INFINITY;
   for (int64_t c = threadIdx.x; c < lim; c += tpr) mx = fmaxf(mx, load(c));
@@ -146,29 +381,75 @@ __global__ void __launch_bounds__(1024) softmax_loop_kernel(const SoftmaxParams 
     dst[base + c] = Elem<T>::from_f32(__fdiv_rn(Elem<T>::to_f32(dst[base + c]), s));
 }
 
+// Persistent grid for the prefetching kernel: as many blocks as fit on the GPU
+// at once (never more than there are row-group rows).
+template <typename K>
+int64_t persistent_grid(K kernel, int block, int64_t needed) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, block, 0) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  const int64_t g = static_cast<int64_t>(per_sm) * sm_count();
+  return g < needed ? g : needed;
+}
+
+template <typename T, bool kCausal>
+bool launch_softmax_pipe(const SoftmaxParams &p, int nv, int block, int64_t grid, cudaStream_t st) {
+  switch (nv) {
+    case 1: {
+      auto k = softmax_pipe_kernel<T, 1, kCausal>;
+      k<<<persistent_grid(k, block, grid), block, 0, st>>>(p);
+      return true;
+    }
+    case 2: {
+      auto k = softmax_pipe_kernel<T, 2, kCausal>;
+      k<<<persistent_grid(k, block, grid), block, 0, st>>>(p);
+      return true;
+    }
+    case 4: {
+      auto k = softmax_pipe_kernel<T, 4, kCausal>;
+      k<<<persistent_grid(k, block, grid), block, 0, st>>>(p);
+      return true;
+    }
+    case 8: {
+      auto k = softmax_pipe_kernel<T, 8, kCausal>;
+      k<<<persistent_grid(k, block, grid), block, 0, st>>>(p);
+      return true;
+    }
+    default:
+      return false;
+  }
+}
+
 // Returns false when no instantiated kernel has this shape (a dispatcher bug).
-template <typename T, bool kVector>
-bool launch_softmax_regs(const SoftmaxParams &p, int nv, int block, int64_t grid, cudaStream_t st) {
+template <typename T, bool kVector, bool kCausal>
+bool launch_softmax_regs_c(const SoftmaxParams &p, int nv, int block, int64_t grid, cudaStream_t st) {
+  if constexpr (kVector) return launch_softmax_pipe<T, kCausal>(p, nv, block, grid, st);
   constexpr int N = kVector ? Elem<T>::kVec : 1;
   switch (nv) {
     case 1:
-      softmax_regs_kernel<T, kVector, 1><<<grid, block, 0, st>>>(p);
+      softmax_regs_kernel<T, kVector, 1, kCausal><<<grid, block, 0, st>>>(p);
       return true;
     case 2:
-      softmax_regs_kernel<T, kVector, 2><<<grid, block, 0, st>>>(p);
+      softmax_regs_kernel<T, kVector, 2, kCausal><<<grid, block, 0, st>>>(p);
       return true;
     case 4:
-      softmax_regs_kernel<T, kVector, 4><<<grid, block, 0, st>>>(p);
+      softmax_regs_kernel<T, kVector, 4, kCausal><<<grid, block, 0, st>>>(p);
       return true;
     case 8:
       if constexpr (8 * N <= 32) {
-        softmax_regs_kernel<T, kVector, 8><<<grid, block, 0, st>>>(p);
+        softmax_regs_kernel<T, kVector, 8, kCausal><<<grid, block, 0, st>>>(p);
         return true;
       }
       return false;
     default:
       return false;
   }
+}
+
+template <typename T, bool kVector>
+bool launch_softmax_regs(const SoftmaxParams &p, int nv, int block, int64_t grid, cudaStream_t st) {
+  return p.causal ? launch_softmax_regs_c<T, kVector, true>(p, nv, block, grid, st)
+                  : launch_softmax_regs_c<T, kVector, false>(p, nv, block, grid, st);
 }
 
 template <typename T>

@@ -77,3 +77,23 @@ def test_rvq_bad_code_flag(xn, cuda):
     Y = xn.rvq_decode_sum(books, codes, out_layout="btd", err_flag=err)
     assert int(err.item()) == 1
     assert torch.all(Y[0, 0] == 3) and torch.all(Y[0, 1] == 1) and torch.all(Y[0, 2] == 3)
+
+
+@pytest.mark.parametrize("dtype,row", [("bf16", 1024), ("bf16", 4096), ("f32", 4096), ("bf16", 24576)])
+def test_index_select_bulk_path_with_bad_ids(oracle, xn, cuda, dtype, row):
+    """Rows of 2-48 KB take the bulk-copy path; bad ids interleaved with good
+    ones give zero rows and bit 1 of the flag, the other rows stay exact."""
+    r = rng(row)
+    table = to_storage(randn(r, (300, row)), dtype)
+    ids = r.integers(0, 300, size=777)
+    ids[::50] = -3
+    ids[7::61] = 300
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    Y = from_device(xn.index_select(to_device(table, dtype, cuda), torch.from_numpy(ids).to(cuda), 0,
+                                    err_flag=err), dtype)
+    assert int(err.item()) == 1
+    bad = (ids < 0) | (ids >= 300)
+    good_ids = np.where(bad, 0, ids).astype(np.uint32)
+    ref = oracle.index_select(table, good_ids, 0)
+    assert np.array_equal(Y[~bad], ref[~bad])
+    assert np.all(Y[bad] == 0)

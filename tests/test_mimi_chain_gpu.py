@@ -7,7 +7,7 @@ import pytest
 import torch
 
 from helpers import from_device
-from mimi_ref import chain_ref
+from mimi_oracle import chain_ref
 
 pytestmark = pytest.mark.gpu
 
