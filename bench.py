@@ -339,7 +339,11 @@ SWEEP_OPS = ["rms_norm_residual", "layer_norm", "rope", "swiglu", "softmax", "em
 
 
 def sweep(torch, xn, device, widths, rows_list, dtypes, reps: int, mem_cap_gb: float, ops=SWEEP_OPS) -> list[dict]:
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)  # 256 MB > L2
+    # L2 flush before every timed launch: write 256 MB (> the 126 MB L2), then
+    # read another 256 MB buffer, so the L2 holds only clean lines of the
+    # second buffer and the timed launch pays for no write-back of the flush.
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+    flush_clean = torch.zeros(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
     out = []
     for dname in dtypes:
         dt = {"f32": torch.float32, "bf16": torch.bfloat16}[dname]
@@ -401,6 +405,7 @@ def sweep(torch, xn, device, widths, rows_list, dtypes, reps: int, mem_cap_gb: f
                     times = []
                     for _ in range(reps):
                         flush.zero_()
+                        flush_clean.sum()
                         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                         e0.record()
                         fn()

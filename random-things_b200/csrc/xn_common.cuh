@@ -14,6 +14,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 namespace xn {
 
 // ---------------------------------------------------------------------------
@@ -101,9 +103,10 @@ __device__ __forceinline__ void unpack<float>(const uint4 &v, float (&f)[4]) {
   f[3] = __uint_as_float(v.w);
 }
 
+// bf16 is the high half of an f32: widening is a shift (low element) and a
+// mask (high element), one integer operation each.
 __device__ __forceinline__ float2 bf2_to_f2(uint32_t w) {
-  __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162 *>(&w);
-  return __bfloat1622float2(h);
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
 }
 
 __device__ __forceinline__ float2 h2_to_f2(uint32_t w) {
@@ -154,6 +157,121 @@ template <>
 __device__ __forceinline__ uint4 pack<__half>(const float (&f)[8]) {
   return make_uint4(f2_to_h2(f[0], f[1]), f2_to_h2(f[2], f[3]), f2_to_h2(f[4], f[5]),
                     f2_to_h2(f[6], f[7]));
+}
+
+// ---------------------------------------------------------------------------
+// A 16-byte vector as adjacent element pairs in f32, for the sm_100 paired f32
+// instructions (__fadd2_rn / __fmul2_rn / __ffma2_rn: two IEEE f32 operations
+// per instruction, each rounded exactly like its scalar form). bf16 widens by
+// bit placement (one shift or mask per element); packing rounds a pair with
+// one cvt.rn.{bf16x2,f16x2}.f32.
+// ---------------------------------------------------------------------------
+template <typename T>
+struct Pairs;
+
+template <>
+struct Pairs<float> {
+  static constexpr int kP = 2;  // pairs per 16-byte vector
+  __device__ __forceinline__ static void unpack(const uint4 &v, float2 (&p)[2]) {
+    p[0] = make_float2(__uint_as_float(v.x), __uint_as_float(v.y));
+    p[1] = make_float2(__uint_as_float(v.z), __uint_as_float(v.w));
+  }
+  __device__ __forceinline__ static uint4 pack(const float2 (&p)[2]) {
+    return make_uint4(__float_as_uint(p[0].x), __float_as_uint(p[0].y), __float_as_uint(p[1].x),
+                      __float_as_uint(p[1].y));
+  }
+};
+
+template <>
+struct Pairs<__nv_bfloat16> {
+  static constexpr int kP = 4;
+  __device__ __forceinline__ static void unpack(const uint4 &v, float2 (&p)[4]) {
+    p[0] = bf2_to_f2(v.x);
+    p[1] = bf2_to_f2(v.y);
+    p[2] = bf2_to_f2(v.z);
+    p[3] = bf2_to_f2(v.w);
+  }
+  __device__ __forceinline__ static uint4 pack(const float2 (&p)[4]) {
+    return make_uint4(f2_to_bf2(p[0].x, p[0].y), f2_to_bf2(p[1].x, p[1].y), f2_to_bf2(p[2].x, p[2].y),
+                      f2_to_bf2(p[3].x, p[3].y));
+  }
+};
+
+template <>
+struct Pairs<__half> {
+  static constexpr int kP = 4;
+  __device__ __forceinline__ static void unpack(const uint4 &v, float2 (&p)[4]) {
+    p[0] = h2_to_f2(v.x);
+    p[1] = h2_to_f2(v.y);
+    p[2] = h2_to_f2(v.z);
+    p[3] = h2_to_f2(v.w);
+  }
+  __device__ __forceinline__ static uint4 pack(const float2 (&p)[4]) {
+    return make_uint4(f2_to_h2(p[0].x, p[0].y), f2_to_h2(p[1].x, p[1].y), f2_to_h2(p[2].x, p[2].y),
+                      f2_to_h2(p[3].x, p[3].y));
+  }
+};
+
+__device__ __forceinline__ float2 splat2(float v) { return make_float2(v, v); }
+
+// h = T(x + T(b * s)) (with s) or T(x + b) (without) on a 16-byte vector: the
+// reference's LayerScale multiply and residual add, each a T operation that
+// rounds its f32 result to T. For bf16 / f16 the paired instructions round
+// the exact result once, which gives the same T value:
+//   * the product of two 8- or 11-bit significands is exact in f32 (a bf16
+//     product in the subnormal range has at most 16 significant bits, so f32
+//     rounding cannot move it onto a bf16 midpoint either);
+//   * an f32 sum of two T values is inexact only when the smaller term is
+//     below 2^-15 of the larger, far inside half a T ulp, so both roundings
+//     return the larger term's neighbourhood value.
+template <typename T>
+__device__ __forceinline__ uint32_t t2_add(uint32_t a, uint32_t b);
+template <typename T>
+__device__ __forceinline__ uint32_t t2_mul(uint32_t a, uint32_t b);
+
+template <>
+__device__ __forceinline__ uint32_t t2_add<__nv_bfloat16>(uint32_t a, uint32_t b) {
+  __nv_bfloat162 r = __hadd2(*reinterpret_cast<__nv_bfloat162 *>(&a), *reinterpret_cast<__nv_bfloat162 *>(&b));
+  return *reinterpret_cast<uint32_t *>(&r);
+}
+template <>
+__device__ __forceinline__ uint32_t t2_mul<__nv_bfloat16>(uint32_t a, uint32_t b) {
+  __nv_bfloat162 r = __hmul2(*reinterpret_cast<__nv_bfloat162 *>(&a), *reinterpret_cast<__nv_bfloat162 *>(&b));
+  return *reinterpret_cast<uint32_t *>(&r);
+}
+template <>
+__device__ __forceinline__ uint32_t t2_add<__half>(uint32_t a, uint32_t b) {
+  __half2 r = __hadd2(*reinterpret_cast<__half2 *>(&a), *reinterpret_cast<__half2 *>(&b));
+  return *reinterpret_cast<uint32_t *>(&r);
+}
+template <>
+__device__ __forceinline__ uint32_t t2_mul<__half>(uint32_t a, uint32_t b) {
+  __half2 r = __hmul2(*reinterpret_cast<__half2 *>(&a), *reinterpret_cast<__half2 *>(&b));
+  return *reinterpret_cast<uint32_t *>(&r);
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 residual_vec(uint4 x, uint4 b, const void *s) {
+  if constexpr (std::is_same<T, float>::value) {
+    float2 bp[2], xp[2];
+    Pairs<float>::unpack(b, bp);
+    Pairs<float>::unpack(x, xp);
+    if (s != nullptr) {
+      float2 sp[2];
+      Pairs<float>::unpack(ld_cached(s), sp);
+      bp[0] = __fmul2_rn(bp[0], sp[0]);
+      bp[1] = __fmul2_rn(bp[1], sp[1]);
+    }
+    xp[0] = __fadd2_rn(xp[0], bp[0]);
+    xp[1] = __fadd2_rn(xp[1], bp[1]);
+    return Pairs<float>::pack(xp);
+  } else {
+    if (s != nullptr) {
+      const uint4 sv = ld_cached(s);
+      b = make_uint4(t2_mul<T>(b.x, sv.x), t2_mul<T>(b.y, sv.y), t2_mul<T>(b.z, sv.z), t2_mul<T>(b.w, sv.w));
+    }
+    return make_uint4(t2_add<T>(x.x, b.x), t2_add<T>(x.y, b.y), t2_add<T>(x.z, b.z), t2_add<T>(x.w, b.w));
+  }
 }
 
 // Half a vector (8 bytes): kVec/2 values, used for the interleaved-RoPE tables.
@@ -240,6 +358,15 @@ __device__ __forceinline__ float div_by(float x, float d, float r) {
   const float q0 = __fmul_rn(x, r);
   const float rem = __fmaf_rn(-d, q0, x);
   return copysignf(__fmaf_rn(rem, r, q0), q0);
+}
+
+// div_by on an element pair, for dividends that are never -0 (exp results):
+// with x = +0 every step is +0, so the sign fix-up is not needed. nd = -d,
+// r = __frcp_rn(d) in both lanes.
+__device__ __forceinline__ float2 div_nonneg2(float2 x, float2 nd, float2 r) {
+  const float2 q0 = __fmul2_rn(x, r);
+  const float2 rem = __ffma2_rn(nd, q0, x);
+  return __ffma2_rn(rem, r, q0);
 }
 
 // s / d where s and d are bf16 values, d >= 1, and the quotient is then

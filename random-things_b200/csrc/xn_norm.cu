@@ -248,6 +248,161 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? ((kLN && NV == 8
   }
 }
 
+// The 16-byte vector path. Same row-group structure as norm_regs_kernel, with
+// every f32 step on adjacent element pairs through the sm_100 paired
+// instructions (two IEEE f32 operations per instruction, so per pair: LN one
+// add for the sum, two for the centred squares, four in the epilogue; RMS one
+// FMA for the sum of squares, four in the epilogue), bf16 widened by shift
+// and mask, and the residual prologue on packed T pairs (residual_vec). The
+// results per element are the same as the scalar forms: only the grouping of
+// the row sums differs (two interleaved partial sums per thread).
+template <typename T, int NV, bool kLN, int kMaxBlock, bool kBranch>
+__global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : (kMaxBlock == 512 ? 2 : 1))
+    norm_vec_kernel(const NormParams p) {
+  using P = Pairs<T>;
+  constexpr int KP = P::kP;
+  constexpr int N = Elem<T>::kVec;
+  __shared__ float red[32];
+  const int tpr = p.tpr;
+  const int g = threadIdx.x / tpr;
+  const int lr = threadIdx.x - g * tpr;
+  const int rpb = blockDim.x / tpr;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * rpb + g;
+  const bool active = row < p.rows;
+  const int64_t base = row * p.cols;
+  const uint4 *src = reinterpret_cast<const uint4 *>(static_cast<const T *>(p.src) + base);
+
+  // 1) h = src (+ T(branch * ls)), packed; invalid slots hold +0.
+  uint4 h[NV];
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int vi = lr + k * tpr;
+    h[k] = make_uint4(0u, 0u, 0u, 0u);
+    if (active && vi < p.nvec) h[k] = ld_stream(src + vi);
+  }
+  if constexpr (kBranch) {
+    const uint4 *br = reinterpret_cast<const uint4 *>(static_cast<const T *>(p.branch) + base);
+    uint4 b[NV];
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int vi = lr + k * tpr;
+      if (active && vi < p.nvec) b[k] = ld_stream(br + vi);
+    }
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int vi = lr + k * tpr;
+      if (active && vi < p.nvec)
+        h[k] = residual_vec<T>(h[k], b[k], p.ls != nullptr ? static_cast<const T *>(p.ls) + vi * N : nullptr);
+    }
+    if (p.res_out != nullptr) {
+      uint4 *ro = reinterpret_cast<uint4 *>(static_cast<T *>(p.res_out) + base);
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        const int vi = lr + k * tpr;
+        if (active && vi < p.nvec) st_vec(ro + vi, h[k]);
+      }
+    }
+  }
+
+  // 2) Row statistics in f32, then 3) the epilogue dst = T(norm(h) * w (+ b)).
+  const float cols_f = __ll2float_rn(p.cols);
+  uint4 *dst = reinterpret_cast<uint4 *>(static_cast<T *>(p.dst) + base);
+  const T *wp = static_cast<const T *>(p.w);
+  if constexpr (kLN) {
+    float2 s2 = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      float2 x[KP];
+      P::unpack(h[k], x);
+#pragma unroll
+      for (int j = 0; j < KP; ++j) s2 = __fadd2_rn(s2, x[j]);
+    }
+    const float mean = __fdiv_rn(group_sum(__fadd_rn(s2.x, s2.y), tpr, red), cols_f);
+    const float2 nmean = splat2(-mean);
+    float2 v2 = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      if (lr + k * tpr < p.nvec) {
+        float2 x[KP];
+        P::unpack(opaque(h[k]), x);
+#pragma unroll
+        for (int j = 0; j < KP; ++j) {
+          const float2 d = __fadd2_rn(x[j], nmean);
+          v2 = __ffma2_rn(d, d, v2);
+        }
+      }
+    }
+    const float var = __fdiv_rn(group_sum(__fadd_rn(v2.x, v2.y), tpr, red), cols_f);
+    const float2 inv = splat2(__fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(var, p.eps))));
+    // x + (-0) == x exactly (signed zeros included), so "no centring" is the
+    // same instruction with a -0 shift.
+    const float2 nshift = splat2(p.remove_mean ? -mean : -0.f);
+    const T *bp = static_cast<const T *>(p.b);
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int vi = lr + k * tpr;
+      if (active && vi < p.nvec) {
+        float2 x[KP], w[KP], b[KP];
+        P::unpack(opaque(h[k]), x);
+        if (wp != nullptr) {
+          P::unpack(ld_cached(wp + vi * N), w);
+        } else {
+#pragma unroll
+          for (int j = 0; j < KP; ++j) w[j] = splat2(1.f);
+        }
+        if (bp != nullptr) {
+          P::unpack(ld_cached(bp + vi * N), b);
+        } else {
+#pragma unroll
+          for (int j = 0; j < KP; ++j) b[j] = splat2(0.f);
+        }
+#pragma unroll
+        for (int j = 0; j < KP; ++j)
+          x[j] = __fadd2_rn(__fmul2_rn(__fmul2_rn(__fadd2_rn(x[j], nshift), inv), w[j]), b[j]);
+        st_vec(dst + vi, P::pack(x));
+      }
+    }
+  } else {
+    float2 s2 = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      float2 x[KP];
+      P::unpack(h[k], x);
+#pragma unroll
+      for (int j = 0; j < KP; ++j) s2 = __ffma2_rn(x[j], x[j], s2);
+    }
+    const float s = group_sum(__fadd_rn(s2.x, s2.y), tpr, red);
+    const float m = __fsqrt_rn(__fadd_rn(__fdiv_rn(s, cols_f), p.eps));
+    const float r = __frcp_rn(m);
+    const float2 nm2 = splat2(-m), r2 = splat2(r);
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int vi = lr + k * tpr;
+      if (active && vi < p.nvec) {
+        float2 x[KP], w[KP];
+        P::unpack(opaque(h[k]), x);
+        if (wp != nullptr) {
+          P::unpack(ld_cached(wp + vi * N), w);
+        } else {
+#pragma unroll
+          for (int j = 0; j < KP; ++j) w[j] = splat2(1.f);
+        }
+#pragma unroll
+        for (int j = 0; j < KP; ++j) {
+          // T(x / m * alpha), the quotient by div_by's steps on a pair.
+          const float2 q0 = __fmul2_rn(x[j], r2);
+          const float2 rem = __ffma2_rn(nm2, q0, x[j]);
+          float2 q = __ffma2_rn(rem, r2, q0);
+          q.x = copysignf(q.x, q0.x);
+          q.y = copysignf(q.y, q0.y);
+          x[j] = __fmul2_rn(q, w[j]);
+        }
+        st_vec(dst + vi, P::pack(x));
+      }
+    }
+  }
+}
+
 // Rows wider than the register budget: one block per row, several passes.
 template <typename T, bool kLN>
 __global__ void __launch_bounds__(1024) norm_loop_kernel(const NormParams p) {
@@ -300,11 +455,22 @@ __global__ void __launch_bounds__(1024) norm_loop_kernel(const NormParams p) {
   }
 }
 
-// Accesses per thread: up to 8 in 256-thread blocks (4 with a branch, whose
-// vectors are held too) and up to 4 in the 1024-thread shape used for the
-// widest rows. Only shapes within the cap are instantiated.
+// Accesses per thread: up to 8 in 256- and 512-thread blocks (4 with a
+// branch, whose vectors are held too) and up to 4 in the 1024-thread shape
+// used for the widest rows. Only shapes within the cap are instantiated.
 template <int N, bool kBranch, int kMaxBlock>
-constexpr int kMaxNv = (kBranch || kMaxBlock > 256) ? 4 : 8;
+constexpr int kMaxNv = (kBranch || kMaxBlock > 512) ? 4 : 8;
+
+// One launch of the row-group kernel with NV accesses per thread: the paired
+// f32 kernel for 16-byte vectors, the scalar one otherwise.
+template <typename T, bool kVector, int NV, bool kLN, int kMaxBlock, bool kBranch>
+void launch_nv(const NormParams &p, int block, int64_t grid, cudaStream_t st) {
+  if constexpr (kVector) {
+    norm_vec_kernel<T, NV, kLN, kMaxBlock, kBranch><<<grid, block, 0, st>>>(p);
+  } else {
+    norm_regs_kernel<T, false, NV, kLN, kMaxBlock, kBranch><<<grid, block, 0, st>>>(p);
+  }
+}
 
 // Returns false when no instantiated kernel has this shape (a dispatcher bug).
 template <typename T, bool kVector, bool kLN, int kMaxBlock, bool kBranch>
@@ -313,23 +479,23 @@ bool launch_regs_b(NormParams p, int nv, int block, int64_t grid, cudaStream_t s
   constexpr int cap = kMaxNv<N, kBranch, kMaxBlock>;
   switch (nv) {
     case 1:
-      norm_regs_kernel<T, kVector, 1, kLN, kMaxBlock, kBranch><<<grid, block, 0, st>>>(p);
+      launch_nv<T, kVector, 1, kLN, kMaxBlock, kBranch>(p, block, grid, st);
       return true;
     case 2:
       if constexpr (cap >= 2) {
-        norm_regs_kernel<T, kVector, 2, kLN, kMaxBlock, kBranch><<<grid, block, 0, st>>>(p);
+        launch_nv<T, kVector, 2, kLN, kMaxBlock, kBranch>(p, block, grid, st);
         return true;
       }
       return false;
     case 4:
       if constexpr (cap >= 4) {
-        norm_regs_kernel<T, kVector, 4, kLN, kMaxBlock, kBranch><<<grid, block, 0, st>>>(p);
+        launch_nv<T, kVector, 4, kLN, kMaxBlock, kBranch>(p, block, grid, st);
         return true;
       }
       return false;
     case 8:
       if constexpr (cap >= 8) {
-        norm_regs_kernel<T, kVector, 8, kLN, kMaxBlock, kBranch><<<grid, block, 0, st>>>(p);
+        launch_nv<T, kVector, 8, kLN, kMaxBlock, kBranch>(p, block, grid, st);
         return true;
       }
       return false;
@@ -338,14 +504,19 @@ bool launch_regs_b(NormParams p, int nv, int block, int64_t grid, cudaStream_t s
   }
 }
 
-// Blocks of 256 threads (row groups up to 256) may use more registers per
-// thread than the 1024-thread shape needed by the widest rows.
+// Register budgets per block size: 256-thread blocks run four per SM, the
+// 512-thread vector shape two (so one row's loads overlap another's
+// reductions), the 1024-thread shape one.
 template <typename T, bool kVector, bool kLN>
 bool launch_regs(NormParams p, int nv, int block, int64_t grid, cudaStream_t st) {
   const bool branch = p.branch != nullptr;
   if (block <= 256) {
     return branch ? launch_regs_b<T, kVector, kLN, 256, true>(p, nv, block, grid, st)
                   : launch_regs_b<T, kVector, kLN, 256, false>(p, nv, block, grid, st);
+  }
+  if constexpr (kVector) {
+    if (block == 512 && nv > 4)
+      return branch ? false : launch_regs_b<T, kVector, kLN, 512, false>(p, nv, block, grid, st);
   }
   return branch ? launch_regs_b<T, kVector, kLN, 1024, true>(p, nv, block, grid, st)
                 : launch_regs_b<T, kVector, kLN, 1024, false>(p, nv, block, grid, st);
@@ -364,12 +535,15 @@ int launch_norm(NormParams p, cudaStream_t st, const char *op) {
   // Up to 32 row values per thread (16 with a branch, which doubles the
   // loads held in registers): rows of up to 32768 (16384) elements.
   // Row-group shape: 256-thread blocks take up to 8 accesses per thread (4
-  // with a branch); wider rows use groups of up to 1024 threads with up to 4.
+  // with a branch); wider vector rows without a branch use 512-thread groups
+  // with 8; the rest groups of up to 1024 threads with up to 4.
   const int cap256 = p.branch != nullptr ? 4 : 8;
   int64_t tpr = 0;
   if (nvec <= 256LL * cap256) {
     tpr = pow2_ceil(ceil_div(nvec, vec ? cap256 : 4));
     if (tpr > 256) tpr = 256;
+  } else if (vec && p.branch == nullptr && nvec > 512LL * 4 && nvec <= 512LL * 8) {
+    tpr = 512;
   } else if (nvec <= 1024LL * 4) {
     tpr = pow2_ceil(ceil_div(nvec, 4));
   }

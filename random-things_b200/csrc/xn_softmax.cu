@@ -49,7 +49,7 @@ template <>
 struct Pair<__nv_bfloat16> {
   using T2 = __nv_bfloat162;
   __device__ __forceinline__ static T2 splat(float v) { return __float2bfloat162_rn(v); }
-  __device__ __forceinline__ static float2 to_f2(T2 v) { return __bfloat1622float2(v); }
+  __device__ __forceinline__ static float2 to_f2(T2 v) { return bf2_to_f2(*reinterpret_cast<uint32_t *>(&v)); }
   __device__ __forceinline__ static T2 from_f2(float a, float b) { return __floats2bfloat162_rn(a, b); }
   __device__ __forceinline__ static T2 neg_inf() { return splat(-INFINITY); }
   // Keeps the low element, sets the high one to -inf.
@@ -229,17 +229,23 @@ __global__ void __launch_bounds__(512, NV >= 8 ? 1 : 2) softmax_pipe_kernel(cons
   const int cols = static_cast<int>(p.cols);
   const T *src = static_cast<const T *>(p.src);
   T *dst = static_cast<T *>(p.dst);
-  auto row_lim = [&](int64_t r) -> int {
+  // Causal rows: the query index q = row % t1 is carried along the walk
+  // (row += step means q += step % t1, wrapped), not divided per row.
+  // In 32 bits: t1 <= 2^30 (checked on the host) and an offset at or past the
+  // row width leaves every row whole, so off + q + 1 and q + q_step stay below 2^31.
+  const int t1 = kCausal ? static_cast<int>(p.t1) : 1;
+  const int q_step = kCausal ? static_cast<int>(step % t1) : 0;
+  const int off = kCausal ? static_cast<int>(p.offset < p.cols ? p.offset : p.cols) : 0;
+  auto row_lim = [&](int64_t r, int q) -> int {
     if (r >= p.rows) return 0;
     if constexpr (kCausal) {
-      const int64_t l = p.offset + (r % p.t1) + 1;
-      return l < cols ? static_cast<int>(l) : cols;
+      const int l = off + q + 1;
+      return l < cols ? l : cols;
     } else {
       return cols;
     }
   };
-  auto load_row = [&](int64_t r, uint4 (&buf)[NV]) {
-    const int lim = row_lim(r);
+  auto load_row = [&](int64_t r, int lim, uint4 (&buf)[NV]) {
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
       const int e0 = (lr + k * tpr) * N;
@@ -248,36 +254,49 @@ __global__ void __launch_bounds__(512, NV >= 8 ? 1 : 2) softmax_pipe_kernel(cons
   };
   uint4 cur[NV], nxt[NV];
   int64_t row = static_cast<int64_t>(blockIdx.x) * rpb + g;
-  load_row(row, cur);
+  int q = kCausal ? static_cast<int>(row % t1) : 0;
+  int lim = row_lim(row, q);
+  load_row(row, lim, cur);
   for (int64_t base = static_cast<int64_t>(blockIdx.x) * rpb; base < p.rows; base += step, row += step) {
-    load_row(row + step, nxt);  // prefetch the next row of this group
-    const int lim = row_lim(row);
-    float s = 0.f, mx;
+    int qn = q + q_step;
+    if (qn >= t1) qn -= t1;
+    const int lim_next = row_lim(row + step, qn);
+    load_row(row + step, lim_next, nxt);  // prefetch the next row of this group
+    float2 s2 = make_float2(0.f, 0.f);  // two interleaved partial sums
     if constexpr (std::is_same_v<T, float>) {
       float m = -INFINITY;
-      const float sc = p.scale;
+      const float2 sc = splat2(p.scale);
 #pragma unroll
       for (int k = 0; k < NV; ++k) {
         const int e0 = (lr + k * tpr) * N;
+        float2 *x2 = reinterpret_cast<float2 *>(&cur[k]);
         float *x = reinterpret_cast<float *>(&cur[k]);
-#pragma unroll
-        for (int j = 0; j < N; ++j) {
-          if (e0 + j < lim) {
-            if (p.scaled) x[j] = __fmul_rn(x[j], sc);
-          } else {
-            x[j] = -INFINITY;
+        if (e0 + N <= lim) {
+          if (p.scaled) {
+            x2[0] = __fmul2_rn(x2[0], sc);
+            x2[1] = __fmul2_rn(x2[1], sc);
           }
-          m = fmaxf(m, x[j]);
+        } else {  // the vector holding the row end, or padding: -inf past it
+#pragma unroll
+          for (int j = 0; j < N; ++j) {
+            if (e0 + j < lim) {
+              if (p.scaled) x[j] = __fmul_rn(x[j], p.scale);
+            } else {
+              x[j] = -INFINITY;
+            }
+          }
         }
+        m = fmaxf(m, fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3])));
       }
-      mx = group_max(m, tpr, red);
+      const float2 nmx = splat2(-group_max(m, tpr, red));
 #pragma unroll
       for (int k = 0; k < NV; ++k) {
-        float *x = reinterpret_cast<float *>(&cur[k]);
+        float2 *x2 = reinterpret_cast<float2 *>(&cur[k]);
 #pragma unroll
-        for (int j = 0; j < N; ++j) {
-          x[j] = expf(__fsub_rn(x[j], mx));  // exp(-inf - max) = 0 for masked / padding
-          s = __fadd_rn(s, x[j]);
+        for (int j = 0; j < 2; ++j) {
+          const float2 d = __fadd2_rn(x2[j], nmx);  // x - max; exp(-inf) = 0 for masked / padding
+          x2[j] = make_float2(expf(d.x), expf(d.y));
+          s2 = __fadd2_rn(s2, x2[j]);
         }
       }
     } else {
@@ -290,22 +309,29 @@ __global__ void __launch_bounds__(512, NV >= 8 ? 1 : 2) softmax_pipe_kernel(cons
       for (int k = 0; k < NV; ++k) {
         const int e0 = (lr + k * tpr) * N;
         T2 *w = reinterpret_cast<T2 *>(&cur[k]);
+        if (e0 + N <= lim) {
+          if (p.scaled) {
 #pragma unroll
-        for (int j = 0; j < W; ++j) {
-          if (e0 + 2 * j + 1 < lim) {
-            if (p.scaled) w[j] = __hmul2(w[j], sc2);
-          } else if (e0 + 2 * j < lim) {
-            if (p.scaled) w[j] = __hmul2(w[j], sc2);
-            w[j] = P::mask_high(w[j]);
-          } else {
-            w[j] = P::neg_inf();
+            for (int j = 0; j < W; ++j) w[j] = __hmul2(w[j], sc2);
           }
-          mx2 = __hmax2(mx2, w[j]);
+        } else {  // the vector holding the row end, or padding: -inf past it
+#pragma unroll
+          for (int j = 0; j < W; ++j) {
+            if (e0 + 2 * j + 1 < lim) {
+              if (p.scaled) w[j] = __hmul2(w[j], sc2);
+            } else if (e0 + 2 * j < lim) {
+              if (p.scaled) w[j] = __hmul2(w[j], sc2);
+              w[j] = P::mask_high(w[j]);
+            } else {
+              w[j] = P::neg_inf();
+            }
+          }
         }
+#pragma unroll
+        for (int j = 0; j < W; ++j) mx2 = __hmax2(mx2, w[j]);
       }
       const float2 mf = P::to_f2(mx2);
-      mx = group_max(fmaxf(mf.x, mf.y), tpr, red);
-      const T2 m2 = P::splat(mx);  // exact: mx is a T value
+      const T2 m2 = P::splat(group_max(fmaxf(mf.x, mf.y), tpr, red));  // exact: the max is a T value
 #pragma unroll
       for (int k = 0; k < NV; ++k) {
         T2 *w = reinterpret_cast<T2 *>(&cur[k]);
@@ -313,31 +339,31 @@ __global__ void __launch_bounds__(512, NV >= 8 ? 1 : 2) softmax_pipe_kernel(cons
         for (int j = 0; j < W; ++j) {
           const float2 d = P::to_f2(__hsub2(w[j], m2));  // T(x - max)
           const T2 e = P::from_f2(expf(d.x), expf(d.y));  // T(exp(...))
-          const float2 ef = P::to_f2(e);
-          s = __fadd_rn(__fadd_rn(s, ef.x), ef.y);
+          s2 = __fadd2_rn(s2, P::to_f2(e));
           w[j] = e;
         }
       }
     }
-    s = group_sum(s, tpr, red);
-    const float rs = __frcp_rn(s);  // s >= 1 for a live row: its maximum contributes exp(0)
+    const float s = group_sum(__fadd_rn(s2.x, s2.y), tpr, red);
+    // s >= 1 for a live row: its maximum contributes exp(0).
+    const float2 rs = splat2(__frcp_rn(s)), ns = splat2(-s);
     if (row < p.rows) {
 #pragma unroll
       for (int k = 0; k < NV; ++k) {
         const int vi = lr + k * tpr;
         if (vi < p.nvec) {
           if constexpr (std::is_same_v<T, float>) {
-            float *x = reinterpret_cast<float *>(&cur[k]);
-#pragma unroll
-            for (int j = 0; j < N; ++j) x[j] = div_by(x[j], s, rs);
+            float2 *x2 = reinterpret_cast<float2 *>(&cur[k]);
+            x2[0] = div_nonneg2(x2[0], ns, rs);
+            x2[1] = div_nonneg2(x2[1], ns, rs);
           } else {
             using P = Pair<T>;
             using T2 = typename P::T2;
             T2 *w = reinterpret_cast<T2 *>(&cur[k]);
 #pragma unroll
             for (int j = 0; j < N / 2; ++j) {
-              const float2 e = P::to_f2(w[j]);
-              w[j] = P::from_f2(div_by(e.x, s, rs), div_by(e.y, s, rs));
+              const float2 q = div_nonneg2(P::to_f2(w[j]), ns, rs);
+              w[j] = P::from_f2(q.x, q.y);
             }
           }
           st_vec(dst + row * p.cols + vi * N, cur[k]);
@@ -346,6 +372,8 @@ __global__ void __launch_bounds__(512, NV >= 8 ? 1 : 2) softmax_pipe_kernel(cons
     }
 #pragma unroll
     for (int k = 0; k < NV; ++k) cur[k] = nxt[k];
+    q = qn;
+    lim = lim_next;
   }
 }
 
@@ -504,6 +532,8 @@ int softmax_entry(void *dst, const void *src, int64_t rows, int64_t cols, int sc
   if (causal && (t1 <= 0 || offset < 0 || rows % t1 != 0))
     return fail(XN_E_INVALID, "xn_softmax: causal mask needs t1 > 0 dividing rows and offset >= 0 (rows=%lld t1=%lld offset=%lld)",
                 (long long)rows, (long long)t1, (long long)offset);
+  if (causal && t1 > (int64_t{1} << 30))
+    return fail(XN_E_INVALID, "xn_softmax: t1 = %lld query rows per slice exceeds 2^30", (long long)t1);
   if (rows == 0 || cols == 0) return ok();
   if (dst == nullptr || src == nullptr) return fail(XN_E_INVALID, "xn_softmax: null dst or src");
   SoftmaxParams p{dst, src, rows, cols, causal ? t1 : 1, causal ? offset : 0, causal ? 1 : 0, 0, 0, scaled, scale};
