@@ -257,6 +257,67 @@ XN_API int xn_rvq_decode_sum(void *dst, const void *const *tables, int64_t n_q,
                       int *err_flag, void *stream);
 
 /*
+ * Streaming decode, KV cache (next-step rows of the hot path).
+ *
+ * A layer's cache is a ring buffer per (batch, head): k_cache and v_cache are
+ * [b, h, cap, d]. `total` counts the positions appended before the call; the
+ * t new positions go to slots (total + i) % cap. After the append the cache
+ * holds the n = total + t positions seen, of which the last
+ * kv_len = min(n, context) (context <= cap) are attended, oldest first
+ * (logical key j at slot (n - kv_len + j) % cap). This is the state of the
+ * reference's cat-then-trim caches (mimi-rs/src/models/mimi.rs:1122-1153,
+ * pocket_tts/src/mimi_transformer.rs:32-61; with context = cap = the
+ * preallocated length it is the slice_set cache of
+ * pocket_tts/src/transformer.rs:16-33) without their per-step copies.
+ *
+ * When total_dev is not NULL it points at the device copy of `total` (an
+ * int64) and `total` is ignored, so one captured CUDA graph serves every step;
+ * xn_position_advance then adds t on the device at the end of a step.
+ */
+enum {
+  XN_MASK_RELATIVE = 0,  /* key j visible to query i iff j <= i + kv_len - t
+                            (pocket_tts/src/transformer.rs:35-52) */
+  XN_MASK_ABSOLUTE = 1   /* iff j <= total + i: apply_causality_mask(offset) on
+                            the trimmed cache (mimi-rs/src/models/mimi.rs:1364) */
+};
+
+/*
+ * KV-cache append fused with RoPE, reading the packed QKV projection
+ * qkv [b, t, 3, h, d] (q | k | v, the in_proj output):
+ *   q_out [b, h, t, d] = rope(q) at positions total + i
+ *   k_cache slot (total + i) % cap = rope(k) ; v_cache slot = v
+ * Replaces narrow/reshape/transpose/contiguous + rope_i on q and k +
+ * KvCache::append (mimi-rs/src/models/mimi.rs:1330-1354;
+ * pocket_tts/src/mimi_transformer.rs:122-137). RoPE arithmetic as xn_rope
+ * (interleaved or half-split; cos/sin [max_pos, d/2]); requires
+ * total + t <= max_pos and t <= cap. With total_dev, a position outside the
+ * tables skips that step's writes and sets *err_flag (when not NULL) to 1.
+ */
+XN_API int xn_kv_append_rope(void *q_out, void *k_cache, void *v_cache, const void *qkv,
+                      const void *cos, const void *sin, int64_t b, int64_t h, int64_t t,
+                      int64_t d, int64_t total, const int64_t *total_dev, int64_t max_pos,
+                      int64_t cap, int interleaved, int dtype, int *err_flag, void *stream);
+
+/*
+ * Decode attention over the ring cache, one launch for
+ *   scores = T(T(q . k_j) * T(scale)), causal mask (mask_mode), softmax as
+ *   xn_softmax, out = T(sum_j p_j v_j)
+ * i.e. q.matmul_t(k).scale(scale), apply_causality_mask / mask add, softmax,
+ * matmul(v) (mimi-rs/src/models/mimi.rs:1356-1371,
+ * pocket_tts/src/transformer.rs:134-145). q [b, h, t, d] (xn_kv_append_rope's
+ * q_out); out [b, t, h, d] = the [b, t, h*d] out_proj input (the reference's
+ * transpose + reshape). The dot products and the weighted sum accumulate in
+ * f32 in key order. d must be 32, 64 or 128; context <= 8192.
+ */
+XN_API int xn_attention_decode(void *out, const void *q, const void *k_cache, const void *v_cache,
+                        int64_t b, int64_t h, int64_t t, int64_t d, int64_t total,
+                        const int64_t *total_dev, int64_t cap, int64_t context, int mask_mode,
+                        float scale, int dtype, void *stream);
+
+/* *total_dev += t on the device, ordered on `stream` (end of a decode step). */
+XN_API int xn_position_advance(int64_t *total_dev, int64_t t, void *stream);
+
+/*
  * Row-shard plan for splitting `rows` over `world` GPUs: contiguous blocks of
  * ceil(rows / world) rows; writes this rank's first row and row count (host
  * pointers). No reference counterpart: the reference is single-GPU.

@@ -234,6 +234,33 @@ static const float kFrac1Sqrt2 = (float)0.707106781186547524400844362104849039;
     }                                                                                  \
   }
 
+/* Batched matmul with the reference's gemm contract (cpu_backend.rs:45-88,
+ * 425-540): T inputs widened to f32, products accumulated in f32, the sum
+ * rounded to T once. The gemm crate's blocked summation order is not
+ * reproducible outside it; here the accumulation is sequential in k with
+ * fused multiply-adds (its x86-64 microkernels use FMA). */
+#define XO_DEFINE_MATMUL(SUF, ST, TO, FROM)                                            \
+  static void matmul_##SUF(ST *dst, const ST *lhs, const ST *rhs, int64_t batch,       \
+                           int64_t m, int64_t n, int64_t k, int trans_rhs) {           \
+    _Pragma("omp parallel for schedule(static)") for (int64_t bm = 0; bm < batch * m; bm++) { \
+      const int64_t bi = bm / m;                                                       \
+      const ST *a = lhs + bm * k;                                                      \
+      const ST *bb = rhs + bi * n * k;                                                 \
+      for (int64_t j = 0; j < n; j++) {                                                \
+        float acc = 0.0f;                                                              \
+        for (int64_t x = 0; x < k; x++) {                                              \
+          const float rv = trans_rhs ? TO(bb[j * k + x]) : TO(bb[x * n + j]);          \
+          acc = fmaf(TO(a[x]), rv, acc);                                               \
+        }                                                                              \
+        dst[bm * n + j] = FROM(acc);                                                   \
+      }                                                                                \
+    }                                                                                  \
+  }
+
+XO_DEFINE_MATMUL(f32, float, F32_TO, F32_FROM)
+XO_DEFINE_MATMUL(bf16, uint16_t, BF16_TO, BF16_FROM)
+XO_DEFINE_MATMUL(f16, uint16_t, F16_TO, F16_FROM)
+
 XO_DEFINE(f32, float, F32_TO, F32_FROM)
 XO_DEFINE(bf16, uint16_t, BF16_TO, BF16_FROM)
 XO_DEFINE(f16, uint16_t, F16_TO, F16_FROM)
@@ -259,6 +286,13 @@ void xo_layer_norm(int dt, void *dst, const void *src, const void *w, const void
   XO_DISPATCH(dt, layer_norm_f16(dst, src, w, b, dim_m1, d, eps, remove_mean),
               layer_norm_bf16(dst, src, w, b, dim_m1, d, eps, remove_mean),
               layer_norm_f32(dst, src, w, b, dim_m1, d, eps, remove_mean));
+}
+
+void xo_matmul(int dt, void *dst, const void *lhs, const void *rhs, int64_t batch, int64_t m,
+               int64_t n, int64_t k, int trans_rhs) {
+  XO_DISPATCH(dt, matmul_f16(dst, lhs, rhs, batch, m, n, k, trans_rhs),
+              matmul_bf16(dst, lhs, rhs, batch, m, n, k, trans_rhs),
+              matmul_f32(dst, lhs, rhs, batch, m, n, k, trans_rhs));
 }
 
 void xo_softmax(int dt, void *dst, const void *src, int64_t dim_m1, int64_t d) {

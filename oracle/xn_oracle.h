@@ -41,6 +41,12 @@ void xo_rms_norm(int dtype, void *dst, const void *src, const void *alpha,
 void xo_layer_norm(int dtype, void *dst, const void *src, const void *weight,
                    const void *bias, int64_t dim_m1, int64_t d, float eps,
                    int remove_mean);
+/* Batched matmul (cpu_backend.rs:45-88, 425-540, the gemm crate): lhs
+ * [batch, m, k] times rhs [batch, k, n] (trans_rhs = 0) or the transpose of
+ * rhs [batch, n, k] (trans_rhs = 1, matmul_t); f32 accumulation, sequential
+ * in k with FMA, result rounded to T. */
+void xo_matmul(int dtype, void *dst, const void *lhs, const void *rhs, int64_t batch,
+               int64_t m, int64_t n, int64_t k, int trans_rhs);
 /* cpu_backend.rs:667-689 */
 void xo_softmax(int dtype, void *dst, const void *src, int64_t dim_m1, int64_t d);
 /* cpu_backend.rs:647-665 */

@@ -47,6 +47,7 @@ def lib() -> ctypes.CDLL:
             "xo_layer_norm": ([ctypes.c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, ctypes.c_float,
                                ctypes.c_int], None),
             "xo_softmax": ([ctypes.c_int, _c_vp, _c_vp, _c_i64, _c_i64], None),
+            "xo_matmul": ([ctypes.c_int, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int], None),
             "xo_apply_causality_mask": ([ctypes.c_int, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64], None),
             "xo_rope": ([ctypes.c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64,
                          _c_i64], None),
@@ -246,3 +247,80 @@ def rvq_decode(codebooks, codes: np.ndarray, dtype: str, out_layout: str = "bct"
     if out_layout == "btd":
         return np.ascontiguousarray(np.swapaxes(quantized, 1, 2))
     return quantized
+
+
+# ---------------------------------------------------------------------------
+# Streaming decode: the reference's KV cache and attention op sequence.
+# ---------------------------------------------------------------------------
+def matmul(lhs, rhs, dtype: str, trans_rhs: bool = False):
+    """Batched matmul (cpu_backend.rs:45-88 / the gemm crate): lhs [.., m, k]
+    times rhs [.., k, n] (or rhs [.., n, k] transposed when trans_rhs, i.e.
+    matmul_t); f32 accumulation (sequential in k, FMA), T result."""
+    lhs, rhs = _chk(lhs, dtype), _chk(rhs, dtype)
+    m, k = lhs.shape[-2:]
+    n = rhs.shape[-2] if trans_rhs else rhs.shape[-1]
+    assert (rhs.shape[-1] if trans_rhs else rhs.shape[-2]) == k
+    batch = int(np.prod(lhs.shape[:-2], dtype=np.int64)) if lhs.ndim > 2 else 1
+    assert rhs.shape[:-2] == lhs.shape[:-2]
+    out = np.empty(lhs.shape[:-2] + (m, n), dtype=lhs.dtype)
+    lib().xo_matmul(DTYPES[dtype], _ptr(out), _ptr(lhs), _ptr(rhs), batch, m, n, k, int(trans_rhs))
+    return out
+
+
+def scale(x, s: float, dtype: str):
+    """Tensor::scale (ops.rs:101-105 -> cpu_backend.rs:260-272): T(x * T(s))."""
+    x = _chk(x, dtype)
+    sv = np.full(x.shape, 0, dtype=x.dtype)
+    sv[...] = to_storage_scalar(s, dtype)
+    return binary(x, sv, "mul", dtype)
+
+
+def to_storage_scalar(v: float, dtype: str):
+    if dtype == "f32":
+        return np.float32(v)
+    if dtype == "bf16":
+        return np.uint16(lib().xo_f32_to_bf16(float(np.float32(v))))
+    return np.float16(np.float32(v)).view(np.uint16)
+
+
+class KvCacheRef:
+    """KvCache::append (mimi-rs/src/models/mimi.rs:1122-1153,
+    pocket_tts/src/mimi_transformer.rs:32-61): cat along the sequence axis,
+    then keep the last max_seq_len positions. Arrays are [b, h, seq, d]."""
+
+    def __init__(self, max_seq_len: int):
+        self.k = self.v = None
+        self.max_seq_len = max_seq_len
+
+    def append(self, k, v):
+        if self.k is None:
+            nk, nv = k, v
+        else:
+            nk, nv = np.concatenate([self.k, k], axis=2), np.concatenate([self.v, v], axis=2)
+        if nk.shape[2] > self.max_seq_len:
+            trim = nk.shape[2] - self.max_seq_len
+            nk, nv = nk[:, :, trim:], nv[:, :, trim:]
+        self.k, self.v = np.ascontiguousarray(nk), np.ascontiguousarray(nv)
+        return self.k, self.v
+
+
+def split_qkv(qkv, heads: int):
+    """The narrow / reshape / transpose / contiguous split of the packed
+    in_proj output [b, t, 3*h*d] into q, k, v [b, h, t, d]
+    (mimi-rs/src/models/mimi.rs:1330-1346)."""
+    b, t, three_hd = qkv.shape
+    d = three_hd // (3 * heads)
+    parts = qkv.reshape(b, t, 3, heads, d)
+    return [np.ascontiguousarray(np.transpose(parts[:, :, i], (0, 2, 1, 3))) for i in range(3)]
+
+
+def attention_step(q, k, v, scale_value: float, mask_offset: int, dtype: str):
+    """The reference attention op sequence on q [b, h, t, d] and the cached
+    k, v [b, h, kv, d] (mimi-rs/src/models/mimi.rs:1356-1371): matmul_t,
+    scale, apply_causality_mask(mask_offset) (the additive 0 / -inf mask of
+    pocket_tts/src/transformer.rs:35-52,138-139 gives the same values with
+    mask_offset = kv - t), softmax, matmul; returned as [b, t, h, d]."""
+    scores = scale(matmul(q, k, dtype, trans_rhs=True), scale_value, dtype)
+    probs = softmax(apply_causality_mask(scores, mask_offset, dtype), dtype)
+    out = matmul(probs, v, dtype)
+    return np.ascontiguousarray(np.transpose(out, (0, 2, 1, 3)))

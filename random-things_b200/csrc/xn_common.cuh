@@ -307,6 +307,84 @@ __device__ __forceinline__ void st_elem(void *base, int64_t i, float v) {
   reinterpret_cast<T *>(base)[i] = Elem<T>::from_f32(v);
 }
 
+// Half-split rotation of one 16-byte chunk of each half:
+//   y1 = T(T(x1*c) - T(x2*s)),  y2 = T(T(x1*s) + T(x2*c)).
+// bf16 / f16 use the native paired instructions, which round each product and
+// sum once, exactly as the reference's T arithmetic does (the product of two
+// 8- or 11-bit significands is exact in f32; see residual_vec for the sum).
+template <typename T>
+__device__ __forceinline__ void rotate_halfsplit(const uint4 &x1, const uint4 &x2, const uint4 &c, const uint4 &s,
+                                                 uint4 &y1, uint4 &y2) {
+  if constexpr (std::is_same_v<T, float>) {
+    float a[4], b[4], cv[4], sv[4], o1[4], o2[4];
+    unpack<T>(x1, a);
+    unpack<T>(x2, b);
+    unpack<T>(c, cv);
+    unpack<T>(s, sv);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      o1[j] = __fsub_rn(__fmul_rn(a[j], cv[j]), __fmul_rn(b[j], sv[j]));
+      o2[j] = __fadd_rn(__fmul_rn(a[j], sv[j]), __fmul_rn(b[j], cv[j]));
+    }
+    y1 = pack<T>(o1);
+    y2 = pack<T>(o2);
+  } else {
+    using T2 = std::conditional_t<std::is_same_v<T, __half>, __half2, __nv_bfloat162>;
+    const uint32_t *pa = &x1.x, *pb = &x2.x, *pc = &c.x, *ps = &s.x;
+    uint32_t o1[4], o2[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const T2 a = *reinterpret_cast<const T2 *>(pa + j), b = *reinterpret_cast<const T2 *>(pb + j);
+      const T2 cv = *reinterpret_cast<const T2 *>(pc + j), sv = *reinterpret_cast<const T2 *>(ps + j);
+      const T2 r1 = __hsub2(__hmul2(a, cv), __hmul2(b, sv));
+      const T2 r2 = __hadd2(__hmul2(a, sv), __hmul2(b, cv));
+      o1[j] = *reinterpret_cast<const uint32_t *>(&r1);
+      o2[j] = *reinterpret_cast<const uint32_t *>(&r2);
+    }
+    y1 = make_uint4(o1[0], o1[1], o1[2], o1[3]);
+    y2 = make_uint4(o2[0], o2[1], o2[2], o2[3]);
+  }
+}
+
+// Interleaved rotation of one 16-byte vector: pairs (x[2j], x[2j+1]) with
+// c_j, s_j from the kVec/2 table values in c / s:
+//   y[2j] = T(T(x[2j]*c) - T(x[2j+1]*s)),  y[2j+1] = T(T(x[2j]*s) + T(x[2j+1]*c)).
+// For bf16 / f16 a pair is one 32-bit word w = (a, b): m1 = w*(c,c) = (ac, bc)
+// and m2 = w*(s,s) = (as, bs) are paired products; swapping m2's halves and
+// negating the low one gives (-bs, as), and one paired add gives
+// (ac - bs, bc + as). Negation is exact and x - y is x + (-y) in IEEE
+// arithmetic, so every result is the reference's T value.
+template <typename T>
+__device__ __forceinline__ uint4 rotate_interleaved(const uint4 &x, const uint2 &c, const uint2 &s) {
+  if constexpr (std::is_same_v<T, float>) {
+    const float cv[2] = {__uint_as_float(c.x), __uint_as_float(c.y)};
+    const float sv[2] = {__uint_as_float(s.x), __uint_as_float(s.y)};
+    const float xv[4] = {__uint_as_float(x.x), __uint_as_float(x.y), __uint_as_float(x.z), __uint_as_float(x.w)};
+    float y[4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const float a = xv[2 * j], b = xv[2 * j + 1];
+      y[2 * j] = __fsub_rn(__fmul_rn(a, cv[j]), __fmul_rn(b, sv[j]));
+      y[2 * j + 1] = __fadd_rn(__fmul_rn(a, sv[j]), __fmul_rn(b, cv[j]));
+    }
+    return make_uint4(__float_as_uint(y[0]), __float_as_uint(y[1]), __float_as_uint(y[2]), __float_as_uint(y[3]));
+  } else {
+    const uint32_t xw[4] = {x.x, x.y, x.z, x.w};
+    const uint32_t cw[2] = {c.x, c.y}, sw[2] = {s.x, s.y};
+    uint32_t y[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t sel = (j & 1) ? 0x3232u : 0x1010u;  // splat the low or high half
+      const uint32_t cc = __byte_perm(cw[j >> 1], 0u, sel), ss = __byte_perm(sw[j >> 1], 0u, sel);
+      const uint32_t m1 = t2_mul<T>(xw[j], cc);
+      const uint32_t m2 = t2_mul<T>(xw[j], ss);
+      const uint32_t neg_swapped = __byte_perm(m2, 0u, 0x1032u) ^ 0x00008000u;  // (-bs, as)
+      y[j] = t2_add<T>(m1, neg_swapped);
+    }
+    return make_uint4(y[0], y[1], y[2], y[3]);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Reductions inside a row group of `tpr` threads (power of two, 1..1024).
 // Groups smaller than a warp use xor-shuffles that stay inside the group;

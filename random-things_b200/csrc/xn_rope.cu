@@ -43,45 +43,6 @@ struct RopeParams {
 
 constexpr int kMaxHpt = 4;  // heads per thread (cos/sin reuse, loads in flight)
 
-// Half-split rotation of one 16-byte chunk of each half:
-//   y1 = T(T(x1*c) - T(x2*s)),  y2 = T(T(x1*s) + T(x2*c)).
-// bf16 / f16 use the native paired instructions, which round each product and
-// sum once, exactly as the reference's T arithmetic does (the product of two
-// 8- or 11-bit significands is exact in f32; see xn_act.cu for the sum).
-template <typename T>
-__device__ __forceinline__ void rotate_halfsplit(const uint4 &x1, const uint4 &x2, const uint4 &c, const uint4 &s,
-                                                 uint4 &y1, uint4 &y2) {
-  if constexpr (std::is_same_v<T, float>) {
-    float a[4], b[4], cv[4], sv[4], o1[4], o2[4];
-    unpack<T>(x1, a);
-    unpack<T>(x2, b);
-    unpack<T>(c, cv);
-    unpack<T>(s, sv);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      o1[j] = __fsub_rn(__fmul_rn(a[j], cv[j]), __fmul_rn(b[j], sv[j]));
-      o2[j] = __fadd_rn(__fmul_rn(a[j], sv[j]), __fmul_rn(b[j], cv[j]));
-    }
-    y1 = pack<T>(o1);
-    y2 = pack<T>(o2);
-  } else {
-    using T2 = std::conditional_t<std::is_same_v<T, __half>, __half2, __nv_bfloat162>;
-    const uint32_t *pa = &x1.x, *pb = &x2.x, *pc = &c.x, *ps = &s.x;
-    uint32_t o1[4], o2[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const T2 a = *reinterpret_cast<const T2 *>(pa + j), b = *reinterpret_cast<const T2 *>(pb + j);
-      const T2 cv = *reinterpret_cast<const T2 *>(pc + j), sv = *reinterpret_cast<const T2 *>(ps + j);
-      const T2 r1 = __hsub2(__hmul2(a, cv), __hmul2(b, sv));
-      const T2 r2 = __hadd2(__hmul2(a, sv), __hmul2(b, cv));
-      o1[j] = *reinterpret_cast<const uint32_t *>(&r1);
-      o2[j] = *reinterpret_cast<const uint32_t *>(&r2);
-    }
-    y1 = make_uint4(o1[0], o1[1], o1[2], o1[3]);
-    y2 = make_uint4(o2[0], o2[1], o2[2], o2[3]);
-  }
-}
-
 template <typename T, bool kInterleaved, bool kVector>
 __global__ void __launch_bounds__(256) rope_kernel(const RopeParams p) {
   constexpr int V = Elem<T>::kVec;
@@ -158,25 +119,12 @@ __global__ void __launch_bounds__(256) rope_kernel(const RopeParams p) {
       const uint32_t h = hg * p.hpt + hh;
       if (hh < static_cast<int>(p.hpt) && h < H) rx[hh] = ld_stream(src + h * head_stride + c * V);
     }
-    float cv[P], sv[P];
-    unpack_half<T>(ld_cached8(cs + trow + c * P), cv);
-    unpack_half<T>(ld_cached8(sn + trow + c * P), sv);
+    const uint2 cr = ld_cached8(cs + trow + c * P), sr = ld_cached8(sn + trow + c * P);
 #pragma unroll
     for (int hh = 0; hh < kMaxHpt; ++hh) {
       const uint32_t h = hg * p.hpt + hh;
-      if (hh < static_cast<int>(p.hpt) && h < H) {
-        float x[V], y[V];
-        unpack<T>(rx[hh], x);
-#pragma unroll
-        for (int j = 0; j < P; ++j) {
-          const float a = x[2 * j], b = x[2 * j + 1];
-          y[2 * j] = Elem<T>::round(__fsub_rn(Elem<T>::round(__fmul_rn(a, cv[j])),
-                                              Elem<T>::round(__fmul_rn(b, sv[j]))));
-          y[2 * j + 1] = Elem<T>::round(__fadd_rn(Elem<T>::round(__fmul_rn(a, sv[j])),
-                                                  Elem<T>::round(__fmul_rn(b, cv[j]))));
-        }
-        st_vec(dst + h * head_stride + c * V, pack<T>(y));
-      }
+      if (hh < static_cast<int>(p.hpt) && h < H)
+        st_vec(dst + h * head_stride + c * V, rotate_interleaved<T>(rx[hh], cr, sr));
     }
   } else {
     // Scalar fallback: chunk c is one pair (element c of each half, or pair c).

@@ -26,6 +26,7 @@ XN_OK, XN_E_INVALID, XN_E_DTYPE, XN_E_RANGE, XN_E_CUDA = 0, 1, 2, 3, 4
 XN_UNARY_SILU, XN_UNARY_GELU_ERF = 0, 1
 XN_LAYOUT_BHTD, XN_LAYOUT_BTHD = 0, 1
 XN_RVQ_MAX_CODEBOOKS = 32
+XN_MASK_RELATIVE, XN_MASK_ABSOLUTE = 0, 1
 
 # Same codes as `enum DType` (mimi-rs/src/dtype.rs:4-10).
 DTYPE_CODES = {
@@ -70,6 +71,11 @@ SIGNATURES = {
     "xn_rvq_decode_sum": [_vp, ctypes.POINTER(_vp), _i64, _vp, _i64, _i64, _i64, _i64, _int, _int, _vp,
                           _vp],
     "xn_shard_rows": [_i64, _int, _int, ctypes.POINTER(_i64), ctypes.POINTER(_i64)],
+    "xn_kv_append_rope": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _int,
+                          _int, _vp, _vp],
+    "xn_attention_decode": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _int, _f32,
+                            _int, _vp],
+    "xn_position_advance": [_vp, _i64, _vp],
 }
 _RESTYPE = {"xn_last_error": ctypes.c_char_p}
 
@@ -597,6 +603,103 @@ def rvq_decode_sum(codebooks: Sequence[torch.Tensor], codes: torch.Tensor, *, ou
     _call("xn_rvq_decode_sum", _p(out), tables, q, _p(codes), b, t, dim, bins, int(out_layout == "bct"),
           _dtype_code(out), _p(err_flag), _stream(out))
     return out
+
+
+# ---------------------------------------------------------------------------
+# Streaming decode: ring-buffer KV cache (mimi.rs:1099-1153, 1317-1384;
+# pocket_tts/src/transformer.rs, mimi_transformer.rs)
+# ---------------------------------------------------------------------------
+
+def _total_args(total: int | None, total_dev: torch.Tensor | None, op: str) -> tuple[int, int | None]:
+    if total_dev is not None:
+        if total_dev.dtype != torch.int64 or total_dev.numel() != 1 or not total_dev.is_cuda:
+            raise XnError(f"{op}: total_dev must be a one-element int64 CUDA tensor")
+        return 0, total_dev.data_ptr()
+    if total is None or total < 0:
+        raise XnError(f"{op}: need total >= 0 or total_dev")
+    return int(total), None
+
+
+def kv_append_rope(qkv: torch.Tensor, heads: int, cos: torch.Tensor, sin: torch.Tensor, k_cache: torch.Tensor,
+                   v_cache: torch.Tensor, total: int | None = None, *, interleaved: bool = True,
+                   total_dev: torch.Tensor | None = None, err_flag: torch.Tensor | None = None,
+                   q_out: torch.Tensor | None = None) -> torch.Tensor:
+    """Splits the packed projection qkv [B, T, 3*H*D], applies RoPE (rope_i when
+    interleaved, as mimi.rs:1350-1351 and pocket_tts/src/rope.rs) to q and k at
+    positions total + i, writes k and v into the ring caches [B, H, cap, D] at
+    slots (total + i) % cap, and returns q as [B, H, T, D]. With total_dev
+    (int64 [1] on the device) the position is read on the device."""
+    op = "kv_append_rope"
+    if qkv.dim() != 3 or not qkv.is_contiguous():
+        raise XnError(f"{op}: expected a contiguous [B, T, 3*H*D] projection, got {tuple(qkv.shape)}")
+    b, t, c = qkv.shape
+    if c % (3 * heads):
+        raise XnError(f"{op}: width {c} is not 3 * heads * d")
+    d = c // (3 * heads)
+    if k_cache.dim() != 4 or tuple(k_cache.shape) != (b, heads, k_cache.shape[2], d):
+        raise XnError(f"{op}: k_cache must be [B, H, cap, D] = [{b}, {heads}, cap, {d}], got {tuple(k_cache.shape)}")
+    _check_same_shape(k_cache.shape, v_cache.shape, f"{op} caches")
+    if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise XnError(f"{op}: caches must be contiguous")
+    _check_same_shape(cos.shape, sin.shape, f"{op} cos/sin")
+    max_pos, d_over_2 = cos.shape
+    if d_over_2 * 2 != d:
+        raise XnError(f"{op} requires even d dimension, got d={d}")
+    tot, tdev = _total_args(total, total_dev, op)
+    if tdev is None and tot + t > max_pos:
+        raise XnError(f"{op} position out of range, pos={tot} + t={t} > max_pos={max_pos}", XN_E_RANGE)
+    if q_out is None:
+        q_out = torch.empty((b, heads, t, d), dtype=qkv.dtype, device=qkv.device)
+    else:
+        _check_same_shape(q_out.shape, (b, heads, t, d), f"{op} q_out")
+    _dev(qkv, cos, sin, k_cache, v_cache, q_out)
+    _same_dtype(qkv, cos, sin, k_cache, v_cache, q_out)
+    if err_flag is not None:
+        _dev(err_flag)
+        if err_flag.dtype != torch.int32:
+            raise XnError(f"{op}: err_flag must be an int32 CUDA tensor")
+    _call("xn_kv_append_rope", _p(q_out), _p(k_cache), _p(v_cache), _p(qkv), _p(cos), _p(sin), b, heads, t, d,
+          tot, tdev, max_pos, k_cache.shape[2], int(interleaved), _dtype_code(qkv), _p(err_flag), _stream(qkv))
+    return q_out
+
+
+def attention_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, total: int | None,
+                     context: int, scale: float, *, mask: str = "relative", total_dev: torch.Tensor | None = None,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+    """Attention of q [B, H, T, D] over the last min(total + T, context) cached
+    positions: scale, causal mask ("relative": key j <= i + kv_len - T as
+    pocket_tts/src/transformer.rs:35-52; "absolute": j <= total + i as
+    apply_causality_mask(offset) in mimi.rs:1364), softmax and the weighted sum
+    of V, as the reference's op sequence (mimi.rs:1356-1371). Returns
+    [B, T, H*D] (the out_proj input)."""
+    op = "attention_decode"
+    if q.dim() != 4 or not q.is_contiguous():
+        raise XnError(f"{op}: q must be a contiguous [B, H, T, D] tensor")
+    b, h, t, d = q.shape
+    if k_cache.dim() != 4 or tuple(k_cache.shape[:2]) != (b, h) or k_cache.shape[3] != d:
+        raise XnError(f"{op}: k_cache must be [B, H, cap, D] = [{b}, {h}, cap, {d}], got {tuple(k_cache.shape)}")
+    _check_same_shape(k_cache.shape, v_cache.shape, f"{op} caches")
+    if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise XnError(f"{op}: caches must be contiguous")
+    modes = {"relative": XN_MASK_RELATIVE, "absolute": XN_MASK_ABSOLUTE}
+    if mask not in modes:
+        raise XnError(f"{op}: unknown mask mode {mask!r}")
+    tot, tdev = _total_args(total, total_dev, op)
+    if out is None:
+        out = torch.empty((b, t, h * d), dtype=q.dtype, device=q.device)
+    elif out.numel() != b * t * h * d or not out.is_contiguous():
+        raise XnError(f"{op}: out must be a contiguous [B, T, H*D] tensor")
+    _dev(q, k_cache, v_cache, out)
+    _same_dtype(q, k_cache, v_cache, out)
+    _call("xn_attention_decode", _p(out), _p(q), _p(k_cache), _p(v_cache), b, h, t, d, tot, tdev,
+          k_cache.shape[2], int(context), modes[mask], float(scale), _dtype_code(q), _stream(q))
+    return out
+
+
+def position_advance(total_dev: torch.Tensor, t: int) -> None:
+    """total_dev += t on the device (the end of a captured decode step)."""
+    _total_args(None, total_dev, "position_advance")
+    _call("xn_position_advance", _p(total_dev), int(t), _stream(total_dev))
 
 
 # ---------------------------------------------------------------------------

@@ -61,6 +61,18 @@ def test_argument_errors_without_gpu(xn):
     tables = (ctypes.c_void_p * 1)(1)
     assert _rc(xn, "xn_rvq_decode_sum", 1, tables, 0, 1, 1, 1, 8, 4, 1, 2, None, None) == xn.XN_E_INVALID
     assert _rc(xn, "xn_rvq_decode_sum", 1, tables, 33, 1, 1, 1, 8, 4, 1, 2, None, None) == xn.XN_E_INVALID
+    # decode: position past the tables, t > cap, odd head dim
+    ap = "xn_kv_append_rope"
+    assert _rc(xn, ap, 1, 1, 1, 1, 1, 1, 2, 4, 3, 64, 8, None, 10, 16, 1, 1, None, None) == xn.XN_E_RANGE
+    assert _rc(xn, ap, 1, 1, 1, 1, 1, 1, 2, 4, 9, 64, 0, None, 100, 8, 1, 1, None, None) == xn.XN_E_INVALID
+    assert _rc(xn, ap, 1, 1, 1, 1, 1, 1, 2, 4, 1, 63, 0, None, 100, 8, 1, 1, None, None) == xn.XN_E_INVALID
+    at = "xn_attention_decode"
+    # head dim outside {32, 64, 128}; context > cap; unknown mask mode; context above the shared-memory bound
+    assert _rc(xn, at, 1, 1, 1, 1, 2, 4, 1, 48, 0, None, 16, 16, 0, 0.125, 1, None) == xn.XN_E_INVALID
+    assert _rc(xn, at, 1, 1, 1, 1, 2, 4, 1, 64, 0, None, 16, 17, 0, 0.125, 1, None) == xn.XN_E_INVALID
+    assert _rc(xn, at, 1, 1, 1, 1, 2, 4, 1, 64, 0, None, 16, 16, 2, 0.125, 1, None) == xn.XN_E_INVALID
+    assert _rc(xn, at, 1, 1, 1, 1, 2, 4, 1, 64, 0, None, 9000, 8193, 0, 0.125, 1, None) == xn.XN_E_INVALID
+    assert _rc(xn, "xn_position_advance", None, 1, None) == xn.XN_E_INVALID
     assert L.xn_abi_version() == 1
 
 

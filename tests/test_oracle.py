@@ -137,3 +137,49 @@ def test_thread_count_does_not_change_results(oracle):
         oracle.set_num_threads(n)
     assert np.array_equal(y1, y2)
     assert torch.get_num_threads() >= 1
+
+
+def test_matmul_oracle_matches_float64(oracle):
+    """xo_matmul (the reference's gemm contract: f32 accumulation, one T
+    rounding) against a float64 product, f32 and bf16, plain and transposed."""
+    r = rng(9)
+    a, bt = randn(r, (3, 5, 64)), randn(r, (3, 7, 64))
+    exact = np.einsum("bmk,bnk->bmn", a.astype(np.float64), bt.astype(np.float64))
+    got = oracle.matmul(a, bt, "f32", trans_rhs=True)
+    assert np.max(np.abs(got - exact)) <= 64 * 2.0 ** -24 * np.max(np.abs(a)) * np.max(np.abs(bt)) * 8
+    got2 = oracle.matmul(a, np.ascontiguousarray(np.swapaxes(bt, 1, 2)), "f32")
+    assert np.array_equal(got, got2)
+    ah, bh = to_storage(a, "bf16"), to_storage(bt, "bf16")
+    gh = storage_to_f32(oracle.matmul(ah, bh, "bf16", trans_rhs=True), "bf16")
+    ex = np.einsum("bmk,bnk->bmn", storage_to_f32(ah, "bf16").astype(np.float64),
+                   storage_to_f32(bh, "bf16").astype(np.float64))
+    assert np.all(np.abs(gh - ex) <= np.abs(ex) * 2.0 ** -8 + 1e-6)
+
+
+def test_kv_cache_ref_is_cat_then_trim(oracle):
+    """KvCacheRef keeps the last max_seq_len positions in order
+    (mimi.rs:1122-1153)."""
+    cache = oracle.KvCacheRef(5)
+    seen = []
+    for step, t in enumerate([2, 1, 3, 1, 4]):
+        k = np.arange(t, dtype=np.float32).reshape(1, 1, t, 1) + 10 * step
+        kk, vv = cache.append(k, k + 0.5)
+        seen.extend(k.ravel().tolist())
+        assert kk.ravel().tolist() == seen[-5:]
+        assert np.array_equal(vv, kk + 0.5)
+
+
+def test_attention_step_rows_are_distributions(oracle):
+    """The reference attention sequence on f32: with v = identity rows the
+    output rows are the softmax probabilities (non-negative, summing to 1,
+    zero past the causal limit)."""
+    r = rng(10)
+    b, h, t, kv, d = 1, 2, 3, 6, 6
+    q, k = randn(r, (b, h, t, d)), randn(r, (b, h, kv, d))
+    v = np.broadcast_to(np.eye(kv, d, dtype=np.float32), (b, h, kv, d)).copy()
+    out = oracle.attention_step(q, k, v, 0.5, kv - t, "f32")  # [b, t, h, d]
+    p = np.transpose(out, (0, 2, 1, 3))
+    assert np.all(p >= 0)
+    assert np.allclose(p.sum(-1), 1.0, atol=1e-6)
+    for i in range(t):
+        assert np.all(p[:, :, i, kv - t + i + 1:] == 0)
