@@ -330,6 +330,91 @@ def mimi_rate(torch, device, steps: int, batch: int = 4, frames: int = 250) -> d
                     "fused ops; GEMMs on cuBLAS), one CUDA graph; seeded synthetic weights"}
 
 
+DECODE_CFG = dict(d_model=1024, num_heads=16, num_layers=6, dim_feedforward=4096)
+
+
+def decode_rate(torch, device, steps: int, act: str, batch: int = 16) -> dict:
+    """Benchmark config 3: streaming decode, B=16, D=1024, 16 heads of 64, 6
+    layers, MLP 4096, one frame per step for steps t = 1..`steps` (the cache
+    grows to `steps` positions). One captured CUDA graph per step (all
+    layers, the position read from device memory) replayed for every step.
+    Reports the mean time per step over the whole stream, inputs resident in
+    HBM, and end to end with each step's input copied from pinned host memory
+    and its output read back."""
+    import mimi_chain as mc
+
+    cfg = mc.MimiChainConfig(**DECODE_CFG)
+    w = mc.synthetic_weights(cfg, torch.bfloat16, device, seed=9)
+    cos, sin = mc.rope_tables(cfg, torch.bfloat16, device)
+    chain = mc.StreamingDecoderChain(cfg, w, cos, sin, batch, act=act, context=steps)
+    g = torch.Generator(device=device).manual_seed(10)
+    xs = torch.randn((steps, batch, 1, cfg.d_model), device=device, generator=g).to(torch.bfloat16)
+    chain.capture(1)
+    for s in range(3):
+        chain.step_graph(xs[s])
+    torch.cuda.synchronize()
+    chain.reset()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for s in range(steps):
+        chain.step_graph(xs[s])
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / steps
+    xs_h = xs.cpu().pin_memory()
+    out_h = torch.empty(chain.out_static.shape, dtype=torch.bfloat16, pin_memory=True)
+    chain.reset()
+    torch.cuda.synchronize()
+    e0.record()
+    for s in range(steps):
+        chain.x_static.copy_(xs_h[s], non_blocking=True)
+        chain.graph.replay()
+        out_h.copy_(chain.out_static, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    us_e2e = e0.elapsed_time(e1) * 1e3 / steps
+    weight_bytes = sum(v.numel() * v.element_size() for k, v in w.items() if k.startswith("layers."))
+    del chain
+    return {"us_per_step": round(us, 2), "frames_per_s": round(batch / (us * 1e-6), 1),
+            "e2e_us_per_step": round(us_e2e, 2), "e2e_frames_per_s": round(batch / (us_e2e * 1e-6), 1),
+            "weight_gbs": round(weight_bytes / (us * 1e-6) / 1e9, 1),
+            "batch": batch, "steps": steps, "dtype": "bf16", "mlp_activation": act, **DECODE_CFG,
+            "h2d_bytes_per_step": batch * cfg.d_model * 2, "d2h_bytes_per_step": batch * cfg.d_model * 2,
+            "what": "streaming decoder transformer, one frame per step (benchmark config 3): fused LN/residual, "
+                    "KV-cache append + RoPE, decode attention, activation; GEMMs on cuBLAS; one CUDA graph "
+                    "per step; seeded synthetic weights"}
+
+
+def cpu_decode_rate(act: str, steps: int = 3, batch: int = 16) -> dict:
+    """The reference streaming op sequence (oracle ops, numpy f32 GEMMs rounded
+    to bf16) at config 3, mean time per step over the first steps after one
+    warm-up step."""
+    import numpy as np
+    import torch
+
+    import mimi_chain as mc
+    import mimi_oracle
+    import xn_oracle
+
+    cfg = mc.MimiChainConfig(**DECODE_CFG)
+    w = {k: mimi_oracle.to_storage(v.float().numpy(), "bf16")
+         for k, v in mc.synthetic_weights(cfg, torch.float32, "cpu", seed=9).items() if k.startswith("layers.")}
+    cos, sin = (mimi_oracle.to_storage(t.float().numpy(), "bf16") for t in mc.rope_tables(cfg, torch.float32, "cpu"))
+    r = np.random.default_rng(10)
+    xs = [mimi_oracle.to_storage(r.standard_normal((batch, 1, cfg.d_model), dtype=np.float32), "bf16")
+          for _ in range(steps + 1)]
+    with _oracle_threads(xn_oracle, 1):
+        t0 = time.perf_counter()
+        mimi_oracle.stream_ref(xn_oracle, cfg, w, cos, sin, xs[:1], "bf16", 0.125, 256, act=act)
+        t1 = time.perf_counter()
+        mimi_oracle.stream_ref(xn_oracle, cfg, w, cos, sin, xs, "bf16", 0.125, 256, act=act)
+        t2 = time.perf_counter()
+    us = ((t2 - t1) - (t1 - t0)) / steps * 1e6
+    return {"us_per_step": round(us, 1), "frames_per_s": round(batch / (us * 1e-6), 1),
+            "sample": f"steps 2..{steps + 1} of a stream at batch {batch}, bf16, oracle ops single-threaded + "
+                      f"numpy f32 GEMMs on {os.cpu_count()} BLAS threads"}
+
+
 # ---------------------------------------------------------------------------
 # Bandwidth sweep (benchmark config 5): each op over row widths and row counts,
 # f32 and bf16, L2 flushed before every timed launch. Points whose tensors
@@ -494,12 +579,28 @@ def cpu_mimi_rate(batch: int = 1, frames: int = 250) -> dict:
     cos, sin = (mimi_oracle.to_storage(t.float().numpy(), "bf16") for t in mc.rope_tables(cfg, torch.float32, "cpu"))
     codes = np.random.default_rng(8).integers(0, cfg.bins, size=(batch, cfg.n_q, frames), dtype=np.int64)
     scale = 0.125
-    mimi_oracle.chain_ref(xn_oracle, cfg, w, cos, sin, codes[:, :, :8], "bf16", scale)
-    t0 = time.perf_counter()
-    mimi_oracle.chain_ref(xn_oracle, cfg, w, cos, sin, codes, "bf16", scale)
-    dt = time.perf_counter() - t0
+    with _oracle_threads(xn_oracle, 1):
+        mimi_oracle.chain_ref(xn_oracle, cfg, w, cos, sin, codes[:, :, :8], "bf16", scale)
+        t0 = time.perf_counter()
+        mimi_oracle.chain_ref(xn_oracle, cfg, w, cos, sin, codes, "bf16", scale)
+        dt = time.perf_counter() - t0
     return {"frames_per_s": round(batch * frames / dt, 1),
-            "sample": f"{batch} x {frames} frames, bf16, oracle ops + numpy f32 GEMMs, {os.cpu_count()} threads"}
+            "sample": f"{batch} x {frames} frames, bf16, oracle ops single-threaded + numpy f32 GEMMs on "
+                      f"{os.cpu_count()} BLAS threads (faster than OpenMP oracle ops beside the BLAS threads)"}
+
+
+class _oracle_threads:
+    """Temporarily sets the oracle's OpenMP thread count."""
+
+    def __init__(self, oracle, n: int):
+        self.oracle, self.n = oracle, n
+
+    def __enter__(self):
+        self.saved = self.oracle.get_num_threads()
+        self.oracle.set_num_threads(self.n)
+
+    def __exit__(self, *exc):
+        self.oracle.set_num_threads(self.saved)
 
 
 def cpu_rate(rows: int, steps: int, warmup: int) -> dict:
@@ -558,6 +659,8 @@ def main() -> int:
     ap.add_argument("--cpu-rows", type=int, default=1024, help="token rows in the CPU sample step")
     ap.add_argument("--e2e-steps", type=int, default=5, help="0 skips the end-to-end measurement")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--decode-steps", type=int, default=256,
+                    help="streaming-decode stream length (benchmark config 3); 0 skips it")
     ap.add_argument("--rows", type=int, default=CFG["batch"] * CFG["seq"],
                     help="token rows per GPU (a multiple of 4096; smaller values for profiling captures)")
     ap.add_argument("--ops", default=",".join(OPS), help="comma-separated subset of " + ",".join(OPS))
@@ -665,6 +768,9 @@ def main() -> int:
     mimi = None
     if args.mimi_steps > 0:
         mimi = mimi_rate(torch, dev, args.mimi_steps)
+    decode = None
+    if args.decode_steps > 0:
+        decode = {act: decode_rate(torch, dev, args.decode_steps, act) for act in ("silu", "gelu_erf")}
 
     if distributed:
         vals = [elapsed_ms, e2e_ms, mimi["ms_per_decode"] if mimi else 0.0, mimi["e2e_frames_per_s"] if mimi else 0.0]
@@ -707,6 +813,7 @@ def main() -> int:
                 "method": "per-sequence chunks; H2D, kernels and D2H on three streams"},
             "gpu_launches": len(ops) * args.steps,
             "mimi_decode": mimi,
+            "streaming_decode": decode,
             "clocks": clocks,
         }
         if not args.no_cpu_baseline and world == 1:
@@ -714,6 +821,8 @@ def main() -> int:
             line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
             if mimi is not None:
                 line["cpu_baseline"]["mimi_decode"] = cpu_mimi_rate()
+            if decode is not None:
+                line["cpu_baseline"]["streaming_decode"] = {act: cpu_decode_rate(act) for act in decode}
         print(json.dumps(line), flush=True)
     if distributed:
         dist.barrier()

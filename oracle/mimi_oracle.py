@@ -38,10 +38,23 @@ def to_storage(a: np.ndarray, dtype: str) -> np.ndarray:
     return np.where(nan, ((u >> 16) | 0x40).astype(np.uint16), r)
 
 
-def _mm(a: np.ndarray, b_t: np.ndarray, dtype: str) -> np.ndarray:
+class _Widened:
+    """Weights widened to f32 once, as a CPU GEMM library keeps them packed."""
+
+    def __init__(self, dtype: str):
+        self.dtype, self.cache = dtype, {}
+
+    def __call__(self, b_t: np.ndarray) -> np.ndarray:
+        key = id(b_t)
+        if key not in self.cache:
+            self.cache[key] = (b_t, np.ascontiguousarray(storage_to_f32(b_t, self.dtype).T))
+        return self.cache[key][1]
+
+
+def _mm(a: np.ndarray, b_t: np.ndarray, dtype: str, widened: _Widened | None = None) -> np.ndarray:
     """a [..., K] @ b_t[N, K]^T in f32, rounded to T."""
-    af, bf = storage_to_f32(a, dtype), storage_to_f32(b_t, dtype)
-    return to_storage(np.matmul(af, bf.T), dtype)
+    bf_t = widened(b_t) if widened is not None else storage_to_f32(b_t, dtype).T
+    return to_storage(np.matmul(storage_to_f32(a, dtype), bf_t), dtype)
 
 
 def _bmm(a: np.ndarray, b: np.ndarray, dtype: str) -> np.ndarray:
@@ -88,3 +101,40 @@ def chain_ref(oracle, cfg, w: dict, cos: np.ndarray, sin: np.ndarray, codes: np.
         m = _mm(h, w[p + "linear2.weight"], dtype)
         x = oracle.residual_prologue(x, m, w[p + "layer_scale_2.scale"], dtype)
     return x
+
+
+def stream_ref(oracle, cfg, w: dict, cos: np.ndarray, sin: np.ndarray, xs: list, dtype: str, scale: float,
+               context: int, act: str = "gelu_erf", mask: str = "absolute") -> list:
+    """The streaming decoder transformer (pocket_tts/src/mimi_transformer.rs:
+    StreamingTransformerLayer::forward with MimiStreamingMultiheadAttention;
+    mimi-rs/src/models/mimi.rs:1317-1445) over a stream of step inputs
+    xs[s] = [B, t_s, D]: per layer a cat-then-trim KV cache of `context`
+    positions, rope_i at the absolute position, the attention op sequence with
+    apply_causality_mask(offset) ("absolute") or the additive causal mask
+    ("relative", pocket_tts/src/transformer.rs:35-52), LayerNorm / LayerScale /
+    residual adds and the MLP (`act` = gelu_erf as Pocket, or silu). Returns
+    the per-step outputs."""
+    L, D, H = cfg.num_layers, cfg.d_model, cfg.num_heads
+    caches = [oracle.KvCacheRef(context) for _ in range(L)]
+    total, outs = 0, []
+    wide = _Widened(dtype)
+    for x in xs:
+        B, T, _ = x.shape
+        for l in range(L):
+            p = f"layers.{l}."
+            y = oracle.layer_norm(x, w[p + "norm1.weight"], w[p + "norm1.bias"], cfg.eps, dtype)
+            q, k, v = oracle.split_qkv(_mm(y, w[p + "self_attn.in_proj_weight"], dtype, wide), H)
+            q = oracle.rope(q, cos, sin, total, dtype, interleaved=True)
+            k = oracle.rope(k, cos, sin, total, dtype, interleaved=True)
+            kk, vv = caches[l].append(k, v)
+            offset = total if mask == "absolute" else kk.shape[2] - T
+            a = oracle.attention_step(q, kk, vv, scale, offset, dtype).reshape(B, T, D)
+            attn = _mm(a, w[p + "self_attn.out_proj.weight"], dtype, wide)
+            x = oracle.residual_prologue(x, attn, w[p + "layer_scale_1.scale"], dtype)
+            y2 = oracle.layer_norm(x, w[p + "norm2.weight"], w[p + "norm2.bias"], cfg.eps, dtype)
+            h = oracle.unary(_mm(y2, w[p + "linear1.weight"], dtype, wide), act, dtype)
+            x = oracle.residual_prologue(x, _mm(h, w[p + "linear2.weight"], dtype, wide),
+                                         w[p + "layer_scale_2.scale"], dtype)
+        outs.append(x)
+        total += T
+    return outs

@@ -19,9 +19,10 @@
 // in logical (oldest-first) order through the same slot map, so the sums run
 // in the reference's key order. One CTA per (batch, head, query) holds the
 // query and the kv_len scores on chip: phase 1 gives each thread whole keys
-// (a 16-byte-vector dot product per key, no shuffles), phase 2 gives each warp
-// every 4th key with the head dimension spread over the lanes (coalesced rows
-// of V), and the four warp partials are added in a fixed order.
+// (a 16-byte-vector dot product per key, no shuffles), phase 2 gives each
+// thread one 16-byte column block of V for a strided group of keys (many
+// independent loads in flight), and the group partials are added in a fixed
+// order.
 #include <math.h>
 
 #include <type_traits>
@@ -149,30 +150,14 @@ __device__ __forceinline__ float dot_row(const T *row, const float *qs) {
   return acc;
 }
 
-template <typename T, int DPL>
-__device__ __forceinline__ void load_lane_dims(const T *p, float (&x)[DPL]) {
-  if constexpr (DPL * sizeof(T) == 16) {
-    unpack<T>(ld_cached(p), x);
-  } else if constexpr (DPL * sizeof(T) == 8) {
-    unpack_half<T>(ld_cached8(p), x);
-  } else if constexpr (DPL == 2 && sizeof(T) == 2) {
-    const uint32_t w = __ldg(reinterpret_cast<const unsigned int *>(p));
-    const float2 f = std::is_same_v<T, __half> ? h2_to_f2(w) : bf2_to_f2(w);
-    x[0] = f.x;
-    x[1] = f.y;
-  } else {
-#pragma unroll
-    for (int j = 0; j < DPL; ++j) x[j] = Elem<T>::to_f32(p[j]);
-  }
-}
-
 template <typename T, int D>
 __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const AttnParams p) {
-  constexpr int DPL = D / 32;  // head dims per lane in the weighted sum
-  constexpr int kWarps = kAttnThreads / 32;
+  constexpr int V = Elem<T>::kVec;           // elements per 16-byte vector
+  constexpr int kVpr = D / V;                // vectors per cached row
+  constexpr int kGroups = kAttnThreads / kVpr;  // key groups in the weighted sum
   extern __shared__ float scores[];  // [kv_len]: scores, then probabilities
   __shared__ float qs[D];
-  __shared__ float part[kWarps][D];
+  __shared__ float part[kGroups * D];
   __shared__ float red[32];
   const int64_t bh = blockIdx.x;  // bi * h + hh
   const int64_t i = blockIdx.y;   // query index within the step
@@ -183,6 +168,13 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
   const int64_t first = n - kv_len;  // position of logical key 0
   const int64_t last_visible = p.mask_mode == XN_MASK_ABSOLUTE ? total + i : i + kv_len - p.t;
   const int64_t nvis = last_visible + 1 < kv_len ? last_visible + 1 : kv_len;
+  // Logical key j sits at slot (first + j) % cap; j < kv_len <= cap, so one
+  // conditional subtraction replaces the per-key division.
+  const int64_t slot0 = first % p.cap;
+  auto slot_of = [&](int64_t j) -> int64_t {
+    const int64_t s = slot0 + j;
+    return s >= p.cap ? s - p.cap : s;
+  };
   const T *kc = static_cast<const T *>(p.k_cache) + bh * p.cap * D;
   const T *vc = static_cast<const T *>(p.v_cache) + bh * p.cap * D;
   T *out = static_cast<T *>(p.out) + ((bi * p.t + i) * p.h + hh) * D;
@@ -198,8 +190,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
   for (int64_t j = tid; j < kv_len; j += kAttnThreads) {
     float s = -INFINITY;
     if (j < nvis) {
-      const int64_t slot = (first + j) % p.cap;
-      s = Elem<T>::round(dot_row<T, D>(kc + slot * D, qs));
+      s = Elem<T>::round(dot_row<T, D>(kc + slot_of(j) * D, qs));
       s = Elem<T>::round(__fmul_rn(s, scale_t));
     }
     scores[j] = s;
@@ -220,29 +211,30 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
     scores[j] = Elem<T>::round(div_by(scores[j], sum, rs));
   __syncthreads();
 
-  // Phase 2: out = T(sum_j p_j v_j); warp w takes keys j = w, w + 4, ...;
-  // masked keys have p = 0 and are skipped.
-  const int warp = tid >> 5, lane = tid & 31;
-  float acc[DPL];
+  // Phase 2: out = T(sum_j p_j v_j). Thread = (key group g, vector c of the
+  // row): it accumulates keys j = g, g + kGroups, ... for the V head dims of
+  // vector c, with several 16-byte loads in flight; the group partials are
+  // then added in group order. Masked keys (p = 0) are skipped.
+  const int c = tid % kVpr, g = tid / kVpr;
+  float acc[V];
 #pragma unroll
-  for (int k = 0; k < DPL; ++k) acc[k] = 0.f;
+  for (int k = 0; k < V; ++k) acc[k] = 0.f;
   const int64_t upto = nvis > 0 ? nvis : 0;
-#pragma unroll 4
-  for (int64_t j = warp; j < upto; j += kWarps) {
-    const int64_t slot = (first + j) % p.cap;
-    float x[DPL];
-    load_lane_dims<T, DPL>(vc + slot * D + lane * DPL, x);
+#pragma unroll 8
+  for (int64_t j = g; j < upto; j += kGroups) {
+    float x[V];
+    unpack<T>(ld_cached(vc + slot_of(j) * D + c * V), x);
     const float pj = scores[j];
 #pragma unroll
-    for (int k = 0; k < DPL; ++k) acc[k] = __fmaf_rn(pj, x[k], acc[k]);
+    for (int k = 0; k < V; ++k) acc[k] = __fmaf_rn(pj, x[k], acc[k]);
   }
 #pragma unroll
-  for (int k = 0; k < DPL; ++k) part[warp][lane * DPL + k] = acc[k];
+  for (int k = 0; k < V; ++k) part[g * D + c * V + k] = acc[k];
   __syncthreads();
   for (int k = tid; k < D; k += kAttnThreads) {
-    float s = part[0][k];
+    float s = part[k];
 #pragma unroll
-    for (int w = 1; w < kWarps; ++w) s = __fadd_rn(s, part[w][k]);
+    for (int w = 1; w < kGroups; ++w) s = __fadd_rn(s, part[w * D + k]);
     // No visible key: the reference's softmax of an all -inf row is NaN.
     out[k] = Elem<T>::from_f32(nvis > 0 ? s : __int_as_float(0x7fc00000));
   }

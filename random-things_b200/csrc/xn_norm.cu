@@ -280,6 +280,23 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : (kMaxBlock =
     h[k] = make_uint4(0u, 0u, 0u, 0u);
     if (active && vi < p.nvec) h[k] = ld_stream(src + vi);
   }
+  // Short rows per thread (NV <= 2, the shapes chosen for few or narrow rows):
+  // fetch the weight / bias vectors together with the row, so their latency
+  // is not added after the reductions.
+  constexpr bool kPre = NV <= 2;
+  const T *wp = static_cast<const T *>(p.w);
+  const T *bp = static_cast<const T *>(p.b);
+  uint4 wpre[kPre ? NV : 1], bpre[kPre ? NV : 1];
+  if constexpr (kPre) {
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int vi = lr + k * tpr;
+      if (active && vi < p.nvec) {
+        if (wp != nullptr) wpre[k] = ld_cached(wp + vi * N);
+        if (kLN && bp != nullptr) bpre[k] = ld_cached(bp + vi * N);
+      }
+    }
+  }
   if constexpr (kBranch) {
     const uint4 *br = reinterpret_cast<const uint4 *>(static_cast<const T *>(p.branch) + base);
     uint4 b[NV];
@@ -307,7 +324,6 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : (kMaxBlock =
   // 2) Row statistics in f32, then 3) the epilogue dst = T(norm(h) * w (+ b)).
   const float cols_f = __ll2float_rn(p.cols);
   uint4 *dst = reinterpret_cast<uint4 *>(static_cast<T *>(p.dst) + base);
-  const T *wp = static_cast<const T *>(p.w);
   if constexpr (kLN) {
     float2 s2 = make_float2(0.f, 0.f);
 #pragma unroll
@@ -337,7 +353,6 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : (kMaxBlock =
     // x + (-0) == x exactly (signed zeros included), so "no centring" is the
     // same instruction with a -0 shift.
     const float2 nshift = splat2(p.remove_mean ? -mean : -0.f);
-    const T *bp = static_cast<const T *>(p.b);
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
       const int vi = lr + k * tpr;
@@ -345,13 +360,13 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : (kMaxBlock =
         float2 x[KP], w[KP], b[KP];
         P::unpack(opaque(h[k]), x);
         if (wp != nullptr) {
-          P::unpack(ld_cached(wp + vi * N), w);
+          P::unpack(kPre ? wpre[k] : ld_cached(wp + vi * N), w);
         } else {
 #pragma unroll
           for (int j = 0; j < KP; ++j) w[j] = splat2(1.f);
         }
         if (bp != nullptr) {
-          P::unpack(ld_cached(bp + vi * N), b);
+          P::unpack(kPre ? bpre[k] : ld_cached(bp + vi * N), b);
         } else {
 #pragma unroll
           for (int j = 0; j < KP; ++j) b[j] = splat2(0.f);
@@ -382,7 +397,7 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : (kMaxBlock =
         float2 x[KP], w[KP];
         P::unpack(opaque(h[k]), x);
         if (wp != nullptr) {
-          P::unpack(ld_cached(wp + vi * N), w);
+          P::unpack(kPre ? wpre[k] : ld_cached(wp + vi * N), w);
         } else {
 #pragma unroll
           for (int j = 0; j < KP; ++j) w[j] = splat2(1.f);
@@ -546,6 +561,12 @@ int launch_norm(NormParams p, cudaStream_t st, const char *op) {
     tpr = 512;
   } else if (nvec <= 1024LL * 4) {
     tpr = pow2_ceil(ceil_div(nvec, 4));
+  }
+  // Few rows (decode steps): spread each row over more threads, down to one
+  // access per thread, while the whole launch stays under 64K threads; this
+  // shortens the per-thread chain and brings the weights forward (kPre).
+  if (vec && tpr > 0 && tpr < 256) {
+    while (tpr < 256 && tpr < nvec && p.rows * tpr * 2 <= 65536) tpr *= 2;
   }
   if (tpr > 0) {
     const int nv = static_cast<int>(pow2_ceil(ceil_div(nvec, tpr)));

@@ -166,3 +166,104 @@ class MimiDecoderChain:
     def decode(self, codes: torch.Tensor) -> torch.Tensor:
         """codes [B, n_q, T] -> decoder-transformer output [B, T, D]."""
         return self.transformer(self.rvq_decode(codes))
+
+
+class StreamingDecoderChain:
+    """The decoder transformer in streaming mode: each step takes t new frames
+    [B, t, D] and attends to the last `context` positions through per-layer
+    ring-buffer KV caches, as StreamingTransformer::forward with
+    MimiStreamingMultiheadAttention does step by step
+    (pocket_tts/src/mimi_transformer.rs:114-145, 234-266; mimi.rs:1317-1445).
+
+    Per layer and step: fused LayerNorm (+ LayerScale + residual from the
+    previous block), QKV GEMM, xn_kv_append_rope (split + rope_i on q and k +
+    cache write, no cat / trim copies), xn_attention_decode (scores, scale,
+    mask, softmax, weighted sum of V in one launch), output GEMM, fused
+    LayerNorm + residual, MLP (GEMM, GELU(erf) or SiLU in place, GEMM).
+
+    The position counter lives in device memory, so `capture(t)` records one
+    CUDA graph for a whole step (all layers + the position advance) that
+    `step_graph` replays for every step."""
+
+    def __init__(self, cfg: MimiChainConfig, weights: dict[str, torch.Tensor], cos: torch.Tensor,
+                 sin: torch.Tensor, batch: int, *, act: str = "gelu_erf", mask: str = "absolute",
+                 context: int | None = None):
+        if act not in ("gelu_erf", "silu"):
+            raise ValueError(f"unknown activation {act!r}")
+        self.cfg, self.w, self.cos, self.sin = cfg, weights, cos, sin
+        self.act, self.mask, self.batch = act, mask, batch
+        self.context = int(context if context is not None else cfg.context)
+        dtype = weights["layers.0.norm1.weight"].dtype
+        dev = weights["layers.0.norm1.weight"].device
+        H, hd = cfg.num_heads, cfg.head_dim
+        self.scale = float(torch.tensor(1.0 / math.sqrt(hd), dtype=torch.float32).to(dtype).float())
+        self.k = [torch.zeros((batch, H, self.context, hd), dtype=dtype, device=dev) for _ in range(cfg.num_layers)]
+        self.v = [torch.zeros_like(k) for k in self.k]
+        self.total = 0
+        self.total_dev = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.graph = None
+
+    def reset(self) -> None:
+        """Forget the stream (the caches' contents are overwritten as it refills)."""
+        self.total = 0
+        self.total_dev.zero_()
+
+    def _layers(self, x: torch.Tensor, total: int | None, total_dev: torch.Tensor | None) -> torch.Tensor:
+        cfg, w, eps = self.cfg, self.w, self.cfg.eps
+        H = cfg.num_heads
+        resid = x
+        y = xn.layer_norm(resid, w["layers.0.norm1.weight"], w["layers.0.norm1.bias"], eps)
+        for l in range(cfg.num_layers):
+            p = f"layers.{l}."
+            qkv = torch.matmul(y, w[p + "self_attn.in_proj_weight"].t())
+            q = xn.kv_append_rope(qkv, H, self.cos, self.sin, self.k[l], self.v[l], total, interleaved=True,
+                                  total_dev=total_dev)
+            a = xn.attention_decode(q, self.k[l], self.v[l], total, self.context, self.scale, mask=self.mask,
+                                    total_dev=total_dev)
+            attn = torch.matmul(a, w[p + "self_attn.out_proj.weight"].t())
+            y2, resid = xn.layer_norm_residual(resid, attn, w[p + "norm2.weight"], w[p + "norm2.bias"], eps,
+                                               layer_scale=w[p + "layer_scale_1.scale"])
+            h = torch.matmul(y2, w[p + "linear1.weight"].t())
+            xn.unary_(h, h, self.act)
+            m = torch.matmul(h, w[p + "linear2.weight"].t())
+            if l + 1 < cfg.num_layers:
+                q_ = f"layers.{l + 1}."
+                y, resid = xn.layer_norm_residual(resid, m, w[q_ + "norm1.weight"], w[q_ + "norm1.bias"], eps,
+                                                  layer_scale=w[p + "layer_scale_2.scale"])
+            else:
+                resid = xn.residual_add(resid, m, w[p + "layer_scale_2.scale"])
+        return resid
+
+    def step(self, x: torch.Tensor) -> torch.Tensor:
+        """One eager step on x [B, t, D] with the host-side position."""
+        out = self._layers(x, self.total, None)
+        self.total += x.shape[1]
+        self.total_dev.fill_(self.total)
+        return out
+
+    def capture(self, t: int = 1) -> None:
+        """Records one step of t frames (reading the device position) as a CUDA graph."""
+        cfg = self.cfg
+        dev = self.total_dev.device
+        self.x_static = torch.zeros((self.batch, t, cfg.d_model), dtype=self.k[0].dtype, device=dev)
+        saved = self.total_dev.clone()
+        stream = torch.cuda.Stream(dev)
+        stream.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(stream):  # warm-up outside the graph (cuBLAS handles, workspaces)
+            self._layers(self.x_static, None, self.total_dev)
+        torch.cuda.current_stream(dev).wait_stream(stream)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=stream):
+            self.out_static = self._layers(self.x_static, None, self.total_dev)
+            xn.position_advance(self.total_dev, t)
+        self.total_dev.copy_(saved)
+        self.graph_t = t
+
+    def step_graph(self, x: torch.Tensor) -> torch.Tensor:
+        """One step by graph replay; returns the graph's output buffer (valid
+        until the next replay)."""
+        self.x_static.copy_(x)
+        self.graph.replay()
+        self.total += self.graph_t
+        return self.out_static

@@ -74,3 +74,80 @@ def test_mimi_chain_small_config_f32(oracle, xn, cuda):
                     "f32", chain.scale)
     rms = np.sqrt(np.mean(ref.astype(np.float64) ** 2))
     assert np.max(np.abs(got.astype(np.float64) - ref)) <= 2e-4 * rms
+
+
+def _stream_setup(dtype_name, cfg_kwargs, B, seed=0, **chain_kw):
+    import mimi_chain as mc
+
+    tdt = {"f32": torch.float32, "bf16": torch.bfloat16}[dtype_name]
+    cfg = mc.MimiChainConfig(**cfg_kwargs)
+    dev = torch.device("cuda:0")
+    w = mc.synthetic_weights(cfg, tdt, dev, seed)
+    cos, sin = mc.rope_tables(cfg, tdt, dev)
+    chain = mc.StreamingDecoderChain(cfg, w, cos, sin, B, **chain_kw)
+    return mc, cfg, w, cos, sin, chain, dev, tdt
+
+
+def _rel_err(got, ref, dtype, how):
+    from helpers import storage_to_f32
+
+    g, r = storage_to_f32(got, dtype).astype(np.float64), storage_to_f32(ref, dtype).astype(np.float64)
+    rms = np.sqrt(np.mean(r ** 2))
+    return (np.max(np.abs(g - r)) if how == "max" else np.sqrt(np.mean((g - r) ** 2))) / rms
+
+
+@pytest.mark.parametrize("mask", ["absolute", "relative"])
+@pytest.mark.parametrize("act", ["gelu_erf", "silu"])
+def test_streaming_chain_matches_reference_stream(oracle, xn, cuda, mask, act):
+    """Small f32 config with chunked steps past the context (cache trims, ring
+    wraps): every step's output against the reference streaming sequence."""
+    from mimi_oracle import stream_ref
+
+    torch.backends.cuda.matmul.allow_tf32 = False
+    kw = dict(d_model=128, num_heads=4, num_layers=2, dim_feedforward=256)
+    mc, cfg, w, cos, sin, chain, dev, tdt = _stream_setup("f32", kw, 3, act=act, mask=mask, context=6)
+    g = torch.Generator().manual_seed(7)
+    steps = [2, 1, 3, 1, 1, 2, 1]
+    xs = [torch.randn((3, t, cfg.d_model), generator=g) for t in steps]
+    got = [from_device(chain.step(x.to(dev)), "f32") for x in xs]
+    ref = stream_ref(oracle, cfg, _np(w, "f32"), from_device(cos, "f32"), from_device(sin, "f32"),
+                     [x.numpy() for x in xs], "f32", chain.scale, 6, act=act, mask=mask)
+    for s, (a, b) in enumerate(zip(got, ref)):
+        assert _rel_err(a, b, "f32", "max") <= 2e-4, f"step {s}"
+
+
+@pytest.mark.parametrize("dtype,tol", [("f32", 2e-4), ("bf16", 5e-2)])
+def test_streaming_chain_config3(oracle, xn, cuda, dtype, tol):
+    """Benchmark config 3 shapes (B 16, D 1024, 16 heads of 64, 6 layers, MLP
+    4096, SiLU) for the first steps, t = 1 per step."""
+    from mimi_oracle import stream_ref
+
+    torch.backends.cuda.matmul.allow_tf32 = False
+    kw = dict(d_model=1024, num_heads=16, num_layers=6, dim_feedforward=4096)
+    mc, cfg, w, cos, sin, chain, dev, tdt = _stream_setup(dtype, kw, 16, act="silu", context=256)
+    g = torch.Generator().manual_seed(3)
+    xs = [torch.randn((16, 1, 1024), generator=g).to(tdt) for _ in range(4)]
+    got = [from_device(chain.step(x.to(dev)), dtype) for x in xs]
+    ref = stream_ref(oracle, cfg, _np(w, dtype), from_device(cos, dtype), from_device(sin, dtype),
+                     [from_device(x, dtype) for x in xs], dtype, chain.scale, 256, act="silu")
+    for s, (a, b) in enumerate(zip(got, ref)):
+        err = _rel_err(a, b, dtype, "max" if dtype == "f32" else "rms")
+        assert err <= tol, f"step {s}: {err:.3e}"
+
+
+def test_streaming_chain_graph_replay_matches_eager(xn, cuda):
+    """One captured step graph replayed over 40 steps (past the context of 32)
+    equals eager stepping bit for bit."""
+    kw = dict(d_model=256, num_heads=4, num_layers=3, dim_feedforward=512)
+    _, cfg, w, cos, sin, eager, dev, tdt = _stream_setup("bf16", kw, 4, context=32)
+    import mimi_chain as mc
+
+    graphed = mc.StreamingDecoderChain(cfg, w, cos, sin, 4, context=32)
+    graphed.capture(1)
+    g = torch.Generator().manual_seed(1)
+    for s in range(40):
+        x = torch.randn((4, 1, cfg.d_model), generator=g).to(tdt).to(dev)
+        a = eager.step(x)
+        b = graphed.step_graph(x)
+        assert torch.equal(a, b), f"step {s}"
+    assert int(graphed.total_dev.item()) == 40
