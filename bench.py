@@ -661,6 +661,9 @@ def main() -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--decode-steps", type=int, default=256,
                     help="streaming-decode stream length (benchmark config 3); 0 skips it")
+    ap.add_argument("--decode-only", action="store_true",
+                    help="run only the config-3 streaming-decode measurement")
+    ap.add_argument("--decode-acts", default="silu,gelu_erf", help="MLP activations for --decode-only")
     ap.add_argument("--rows", type=int, default=CFG["batch"] * CFG["seq"],
                     help="token rows per GPU (a multiple of 4096; smaller values for profiling captures)")
     ap.add_argument("--ops", default=",".join(OPS), help="comma-separated subset of " + ",".join(OPS))
@@ -697,6 +700,12 @@ def main() -> int:
             if "gbs" in pt:
                 pt["frac"] = round(pt["gbs"] / peak, 3)
             print(json.dumps(pt), flush=True)
+        return 0
+    if args.decode_only:
+        xn.lib()
+        acts = [a for a in args.decode_acts.split(",") if a]
+        print(json.dumps({"streaming_decode": {a: decode_rate(torch, dev, args.decode_steps, a) for a in acts}}),
+              flush=True)
         return 0
     distributed = world > 1
     if distributed:

@@ -314,6 +314,20 @@ XN_API int xn_attention_decode(void *out, const void *q, const void *k_cache, co
                         const int64_t *total_dev, int64_t cap, int64_t context, int mask_mode,
                         float scale, int dtype, void *stream);
 
+/*
+ * xn_kv_append_rope followed by xn_attention_decode in one launch: each
+ * (batch, head, query) block writes its head's t new k (rotated) and v rows
+ * into the ring caches and rotates its query on chip, then attends. Same
+ * results as the two calls (q is not written out). qkv, cos and sin must be
+ * 16-byte aligned. With total_dev, a position outside the tables skips the
+ * step and sets *err_flag (when not NULL) to 1.
+ */
+XN_API int xn_decode_attention_step(void *out, void *k_cache, void *v_cache, const void *qkv,
+                             const void *cos, const void *sin, int64_t b, int64_t h, int64_t t,
+                             int64_t d, int64_t total, const int64_t *total_dev, int64_t max_pos,
+                             int64_t cap, int64_t context, int mask_mode, float scale,
+                             int interleaved, int dtype, int *err_flag, void *stream);
+
 /* *total_dev += t on the device, ordered on `stream` (end of a decode step). */
 XN_API int xn_position_advance(int64_t *total_dev, int64_t t, void *stream);
 

@@ -133,24 +133,46 @@ struct AttnParams {
   const int64_t *total_dev;
   int mask_mode;
   float scale;
+  // Fused step only: the packed projection and the RoPE tables.
+  const void *qkv;
+  const void *cos;
+  const void *sin;
+  int64_t max_pos;
+  int *err_flag;
 };
 
-// The D head-dim values of one row at `row` as f32 (16-byte vector loads).
-template <typename T, int D>
+// One 16-byte vector of a cached row: read-only path for caches written by
+// an earlier launch, coherent loads where this launch wrote them.
+template <typename T, bool kCoherent>
+__device__ __forceinline__ uint4 ld_row_vec(const T *p) {
+  if constexpr (kCoherent) {
+    return ld_plain(p);
+  } else {
+    return ld_cached(p);
+  }
+}
+
+// q . row over the D head dims (16-byte vector loads, f32 FMA in dim order).
+template <typename T, int D, bool kCoherent>
 __device__ __forceinline__ float dot_row(const T *row, const float *qs) {
   constexpr int V = Elem<T>::kVec;
   float acc = 0.f;
 #pragma unroll
   for (int v = 0; v < D / V; ++v) {
     float x[V];
-    unpack<T>(ld_cached(row + v * V), x);
+    unpack<T>(ld_row_vec<T, kCoherent>(row + v * V), x);
 #pragma unroll
     for (int j = 0; j < V; ++j) acc = __fmaf_rn(qs[v * V + j], x[j], acc);
   }
   return acc;
 }
 
-template <typename T, int D>
+// kFused: the block first does this head's part of xn_kv_append_rope (the t
+// new k rows rotated and v rows copied into their ring slots, identical bytes
+// from every block of the head) and rotates its own query into shared memory;
+// then it attends as the plain kernel does, reading the caches with coherent
+// loads. kInterleaved picks the RoPE form of the fused prologue.
+template <typename T, int D, bool kFused, bool kInterleaved>
 __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const AttnParams p) {
   constexpr int V = Elem<T>::kVec;           // elements per 16-byte vector
   constexpr int kVpr = D / V;                // vectors per cached row
@@ -175,13 +197,76 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
     const int64_t s = slot0 + j;
     return s >= p.cap ? s - p.cap : s;
   };
-  const T *kc = static_cast<const T *>(p.k_cache) + bh * p.cap * D;
-  const T *vc = static_cast<const T *>(p.v_cache) + bh * p.cap * D;
+  T *kw = static_cast<T *>(const_cast<void *>(p.k_cache)) + bh * p.cap * D;
+  T *vw = static_cast<T *>(const_cast<void *>(p.v_cache)) + bh * p.cap * D;
+  const T *kc = kw;
+  const T *vc = vw;
   T *out = static_cast<T *>(p.out) + ((bi * p.t + i) * p.h + hh) * D;
   const int tid = threadIdx.x;
 
-  for (int k = tid; k < D; k += kAttnThreads)
-    qs[k] = Elem<T>::to_f32(static_cast<const T *>(p.q)[(bh * p.t + i) * D + k]);
+  if constexpr (kFused) {
+    if (total < 0 || total + p.t > p.max_pos) {  // device position past the tables
+      if (tid == 0 && p.err_flag != nullptr) atomicOr(p.err_flag, 1);
+      return;  // uniform over the block, before any barrier
+    }
+    constexpr int C = kInterleaved ? kVpr : kVpr / 2;  // work items per row
+    const int64_t half = D / 2;
+    const int64_t n_items = (2 * p.t + 1) * C;  // t k rows, t v rows, this block's q row
+    for (int64_t it = tid; it < n_items; it += kAttnThreads) {
+      const int64_t r = it / C;
+      const int c = static_cast<int>(it % C);
+      int which;
+      int64_t i2;
+      if (r < 2 * p.t) {
+        which = 1 + static_cast<int>(r / p.t);
+        i2 = r % p.t;
+      } else {
+        which = 0;
+        i2 = i;
+      }
+      const int64_t pos = total + i2;
+      const T *src = static_cast<const T *>(p.qkv) + ((bi * p.t + i2) * 3 + which) * p.h * D + hh * D;
+      T *dst = which == 1 ? kw + (pos % p.cap) * D : vw + (pos % p.cap) * D;
+      const T *cs = static_cast<const T *>(p.cos) + pos * half;
+      const T *sn = static_cast<const T *>(p.sin) + pos * half;
+      if constexpr (kInterleaved) {
+        const int e = c * V;
+        uint4 y = ld_stream(src + e);
+        if (which != 2) y = rotate_interleaved<T>(y, ld_cached8(cs + e / 2), ld_cached8(sn + e / 2));
+        if (which == 0) {
+          float f[V];
+          unpack<T>(y, f);
+#pragma unroll
+          for (int k = 0; k < V; ++k) qs[e + k] = f[k];
+        } else {
+          st_vec(dst + e, y);
+        }
+      } else {
+        const int e1 = c * V, e2 = c * V + static_cast<int>(half);
+        uint4 y1 = ld_stream(src + e1), y2 = ld_stream(src + e2);
+        if (which != 2) {
+          const uint4 x1 = y1, x2 = y2;
+          rotate_halfsplit<T>(x1, x2, ld_cached(cs + e1), ld_cached(sn + e1), y1, y2);
+        }
+        if (which == 0) {
+          float f1[V], f2[V];
+          unpack<T>(y1, f1);
+          unpack<T>(y2, f2);
+#pragma unroll
+          for (int k = 0; k < V; ++k) {
+            qs[e1 + k] = f1[k];
+            qs[e2 + k] = f2[k];
+          }
+        } else {
+          st_vec(dst + e1, y1);
+          st_vec(dst + e2, y2);
+        }
+      }
+    }
+  } else {
+    for (int k = tid; k < D; k += kAttnThreads)
+      qs[k] = Elem<T>::to_f32(static_cast<const T *>(p.q)[(bh * p.t + i) * D + k]);
+  }
   __syncthreads();
 
   // Phase 1: scores T(T(q.k) * T(scale)), -inf where masked.
@@ -190,7 +275,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
   for (int64_t j = tid; j < kv_len; j += kAttnThreads) {
     float s = -INFINITY;
     if (j < nvis) {
-      s = Elem<T>::round(dot_row<T, D>(kc + slot_of(j) * D, qs));
+      s = Elem<T>::round(dot_row<T, D, kFused>(kc + slot_of(j) * D, qs));
       s = Elem<T>::round(__fmul_rn(s, scale_t));
     }
     scores[j] = s;
@@ -223,7 +308,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
 #pragma unroll 8
   for (int64_t j = g; j < upto; j += kGroups) {
     float x[V];
-    unpack<T>(ld_cached(vc + slot_of(j) * D + c * V), x);
+    unpack<T>(ld_row_vec<T, kFused>(vc + slot_of(j) * D + c * V), x);
     const float pj = scores[j];
 #pragma unroll
     for (int k = 0; k < V; ++k) acc[k] = __fmaf_rn(pj, x[k], acc[k]);
@@ -267,33 +352,41 @@ int launch_append(AppendParams p, int interleaved, cudaStream_t st) {
   return check_launch("xn_kv_append_rope");
 }
 
-template <typename T, int D>
+template <typename T, int D, bool kFused, bool kInterleaved>
 void launch_attn_d(const AttnParams &p, cudaStream_t st) {
   const dim3 grid(static_cast<unsigned>(p.b * p.h), static_cast<unsigned>(p.t));
   const size_t smem = static_cast<size_t>(p.context) * sizeof(float);
-  attention_decode_kernel<T, D><<<grid, kAttnThreads, smem, st>>>(p);
+  attention_decode_kernel<T, D, kFused, kInterleaved><<<grid, kAttnThreads, smem, st>>>(p);
+}
+
+template <typename T, bool kFused, bool kInterleaved>
+int launch_attn_f(const AttnParams &p, int64_t d, cudaStream_t st, const char *op) {
+  switch (d) {
+    case 32:
+      launch_attn_d<T, 32, kFused, kInterleaved>(p, st);
+      break;
+    case 64:
+      launch_attn_d<T, 64, kFused, kInterleaved>(p, st);
+      break;
+    case 128:
+      launch_attn_d<T, 128, kFused, kInterleaved>(p, st);
+      break;
+    default:
+      return fail(XN_E_INVALID, "%s: head dim %lld not in {32, 64, 128}", op, (long long)d);
+  }
+  return check_launch(op);
 }
 
 template <typename T>
-int launch_attn(const AttnParams &p, int64_t d, cudaStream_t st) {
+int launch_attn(const AttnParams &p, int64_t d, int fused, int interleaved, cudaStream_t st, const char *op) {
   // Vector loads need 16-byte aligned rows: d * sizeof(T) is a multiple of 16
   // for every supported d, so aligned bases suffice.
   if (!is_aligned16(p.k_cache) || !is_aligned16(p.v_cache))
-    return fail(XN_E_INVALID, "xn_attention_decode: k_cache and v_cache must be 16-byte aligned");
-  switch (d) {
-    case 32:
-      launch_attn_d<T, 32>(p, st);
-      break;
-    case 64:
-      launch_attn_d<T, 64>(p, st);
-      break;
-    case 128:
-      launch_attn_d<T, 128>(p, st);
-      break;
-    default:
-      return fail(XN_E_INVALID, "xn_attention_decode: head dim %lld not in {32, 64, 128}", (long long)d);
-  }
-  return check_launch("xn_attention_decode");
+    return fail(XN_E_INVALID, "%s: k_cache and v_cache must be 16-byte aligned", op);
+  if (!fused) return launch_attn_f<T, false, false>(p, d, st, op);
+  if (!is_aligned16(p.qkv) || !is_aligned16(p.cos) || !is_aligned16(p.sin))
+    return fail(XN_E_INVALID, "%s: qkv, cos and sin must be 16-byte aligned", op);
+  return interleaved ? launch_attn_f<T, true, true>(p, d, st, op) : launch_attn_f<T, true, false>(p, d, st, op);
 }
 
 }  // namespace
@@ -345,8 +438,42 @@ int xn_attention_decode(void *out, const void *q, const void *k_cache, const voi
   if (b == 0 || h == 0 || t == 0) return ok();
   if (out == nullptr || q == nullptr || k_cache == nullptr || v_cache == nullptr)
     return fail(XN_E_INVALID, "%s: null pointer", op);
-  AttnParams p{out, q, k_cache, v_cache, b, h, t, total, cap, context, total_dev, mask_mode, scale};
-  XN_DISPATCH_FLOAT(dtype, return launch_attn<T>(p, d, as_stream(stream)));
+  AttnParams p{out, q, k_cache, v_cache, b, h, t, total, cap, context, total_dev, mask_mode, scale,
+               nullptr, nullptr, nullptr, 0, nullptr};
+  XN_DISPATCH_FLOAT(dtype, return launch_attn<T>(p, d, 0, 0, as_stream(stream), op));
+  return fail(XN_E_DTYPE, "%s: unsupported dtype %d", op, dtype);
+}
+
+int xn_decode_attention_step(void *out, void *k_cache, void *v_cache, const void *qkv, const void *cos,
+                             const void *sin, int64_t b, int64_t h, int64_t t, int64_t d, int64_t total,
+                             const int64_t *total_dev, int64_t max_pos, int64_t cap, int64_t context,
+                             int mask_mode, float scale, int interleaved, int dtype, int *err_flag,
+                             void *stream) {
+  using namespace xn;
+  const char *op = "xn_decode_attention_step";
+  if (!is_float_dtype(dtype)) return fail(XN_E_DTYPE, "%s: unsupported dtype %d", op, dtype);
+  if (b < 0 || h < 0 || t < 0) return fail(XN_E_INVALID, "%s: negative size", op);
+  if (d != 32 && d != 64 && d != 128) return fail(XN_E_INVALID, "%s: head dim %lld not in {32, 64, 128}", op, (long long)d);
+  if (context <= 0 || context > cap || context > kMaxContext)
+    return fail(XN_E_INVALID, "%s: need 0 < context <= cap and context <= %d (context=%lld cap=%lld)", op,
+                kMaxContext, (long long)context, (long long)cap);
+  if (t > cap) return fail(XN_E_INVALID, "%s: t=%lld new positions exceed cap=%lld", op, (long long)t, (long long)cap);
+  if (mask_mode != XN_MASK_RELATIVE && mask_mode != XN_MASK_ABSOLUTE)
+    return fail(XN_E_INVALID, "%s: unknown mask mode %d", op, mask_mode);
+  if (total_dev == nullptr) {
+    if (total < 0) return fail(XN_E_INVALID, "%s: negative position %lld", op, (long long)total);
+    if (total + t > max_pos)
+      return fail(XN_E_RANGE, "%s: pos %lld + t %lld exceeds the %lld rows of cos/sin", op, (long long)total,
+                  (long long)t, (long long)max_pos);
+  }
+  if (b * h > 0x7fffffffLL || t > 65535) return fail(XN_E_INVALID, "%s: grid too large (b*h=%lld, t=%lld)", op, (long long)(b * h), (long long)t);
+  if (b == 0 || h == 0 || t == 0) return ok();
+  if (out == nullptr || k_cache == nullptr || v_cache == nullptr || qkv == nullptr || cos == nullptr ||
+      sin == nullptr)
+    return fail(XN_E_INVALID, "%s: null pointer", op);
+  AttnParams p{out, nullptr, k_cache, v_cache, b, h, t, total, cap, context, total_dev, mask_mode, scale,
+               qkv, cos, sin, max_pos, err_flag};
+  XN_DISPATCH_FLOAT(dtype, return launch_attn<T>(p, d, 1, interleaved, as_stream(stream), op));
   return fail(XN_E_DTYPE, "%s: unsupported dtype %d", op, dtype);
 }
 

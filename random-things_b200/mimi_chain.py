@@ -176,9 +176,9 @@ class StreamingDecoderChain:
     (pocket_tts/src/mimi_transformer.rs:114-145, 234-266; mimi.rs:1317-1445).
 
     Per layer and step: fused LayerNorm (+ LayerScale + residual from the
-    previous block), QKV GEMM, xn_kv_append_rope (split + rope_i on q and k +
-    cache write, no cat / trim copies), xn_attention_decode (scores, scale,
-    mask, softmax, weighted sum of V in one launch), output GEMM, fused
+    previous block), QKV GEMM, xn_decode_attention_step (split + rope_i on q
+    and k + cache write, no cat / trim copies, then scores, scale, mask,
+    softmax and the weighted sum of V, all in one launch), output GEMM, fused
     LayerNorm + residual, MLP (GEMM, GELU(erf) or SiLU in place, GEMM).
 
     The position counter lives in device memory, so `capture(t)` records one
@@ -216,10 +216,8 @@ class StreamingDecoderChain:
         for l in range(cfg.num_layers):
             p = f"layers.{l}."
             qkv = torch.matmul(y, w[p + "self_attn.in_proj_weight"].t())
-            q = xn.kv_append_rope(qkv, H, self.cos, self.sin, self.k[l], self.v[l], total, interleaved=True,
-                                  total_dev=total_dev)
-            a = xn.attention_decode(q, self.k[l], self.v[l], total, self.context, self.scale, mask=self.mask,
-                                    total_dev=total_dev)
+            a = xn.decode_attention_step(qkv, H, self.cos, self.sin, self.k[l], self.v[l], total, self.context,
+                                         self.scale, interleaved=True, mask=self.mask, total_dev=total_dev)
             attn = torch.matmul(a, w[p + "self_attn.out_proj.weight"].t())
             y2, resid = xn.layer_norm_residual(resid, attn, w[p + "norm2.weight"], w[p + "norm2.bias"], eps,
                                                layer_scale=w[p + "layer_scale_1.scale"])

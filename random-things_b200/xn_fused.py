@@ -76,6 +76,8 @@ SIGNATURES = {
     "xn_attention_decode": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _int, _f32,
                             _int, _vp],
     "xn_position_advance": [_vp, _i64, _vp],
+    "xn_decode_attention_step": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _i64,
+                                 _i64, _int, _f32, _int, _int, _vp, _vp],
 }
 _RESTYPE = {"xn_last_error": ctypes.c_char_p}
 
@@ -693,6 +695,52 @@ def attention_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     _same_dtype(q, k_cache, v_cache, out)
     _call("xn_attention_decode", _p(out), _p(q), _p(k_cache), _p(v_cache), b, h, t, d, tot, tdev,
           k_cache.shape[2], int(context), modes[mask], float(scale), _dtype_code(q), _stream(q))
+    return out
+
+
+def decode_attention_step(qkv: torch.Tensor, heads: int, cos: torch.Tensor, sin: torch.Tensor,
+                          k_cache: torch.Tensor, v_cache: torch.Tensor, total: int | None, context: int,
+                          scale: float, *, interleaved: bool = True, mask: str = "relative",
+                          total_dev: torch.Tensor | None = None, err_flag: torch.Tensor | None = None,
+                          out: torch.Tensor | None = None) -> torch.Tensor:
+    """kv_append_rope followed by attention_decode in one launch (q stays on
+    chip): the step's attention output [B, T, H*D] from the packed projection
+    qkv [B, T, 3*H*D], with the caches updated as kv_append_rope does."""
+    op = "decode_attention_step"
+    if qkv.dim() != 3 or not qkv.is_contiguous():
+        raise XnError(f"{op}: expected a contiguous [B, T, 3*H*D] projection, got {tuple(qkv.shape)}")
+    b, t, c = qkv.shape
+    if c % (3 * heads):
+        raise XnError(f"{op}: width {c} is not 3 * heads * d")
+    d = c // (3 * heads)
+    if k_cache.dim() != 4 or tuple(k_cache.shape) != (b, heads, k_cache.shape[2], d):
+        raise XnError(f"{op}: k_cache must be [B, H, cap, D] = [{b}, {heads}, cap, {d}], got {tuple(k_cache.shape)}")
+    _check_same_shape(k_cache.shape, v_cache.shape, f"{op} caches")
+    if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise XnError(f"{op}: caches must be contiguous")
+    _check_same_shape(cos.shape, sin.shape, f"{op} cos/sin")
+    max_pos, d_over_2 = cos.shape
+    if d_over_2 * 2 != d:
+        raise XnError(f"{op} requires even d dimension, got d={d}")
+    modes = {"relative": XN_MASK_RELATIVE, "absolute": XN_MASK_ABSOLUTE}
+    if mask not in modes:
+        raise XnError(f"{op}: unknown mask mode {mask!r}")
+    tot, tdev = _total_args(total, total_dev, op)
+    if tdev is None and tot + t > max_pos:
+        raise XnError(f"{op} position out of range, pos={tot} + t={t} > max_pos={max_pos}", XN_E_RANGE)
+    if out is None:
+        out = torch.empty((b, t, heads * d), dtype=qkv.dtype, device=qkv.device)
+    elif out.numel() != b * t * heads * d or not out.is_contiguous():
+        raise XnError(f"{op}: out must be a contiguous [B, T, H*D] tensor")
+    _dev(qkv, cos, sin, k_cache, v_cache, out)
+    _same_dtype(qkv, cos, sin, k_cache, v_cache, out)
+    if err_flag is not None:
+        _dev(err_flag)
+        if err_flag.dtype != torch.int32:
+            raise XnError(f"{op}: err_flag must be an int32 CUDA tensor")
+    _call("xn_decode_attention_step", _p(out), _p(k_cache), _p(v_cache), _p(qkv), _p(cos), _p(sin), b, heads, t,
+          d, tot, tdev, max_pos, k_cache.shape[2], int(context), modes[mask], float(scale), int(interleaved),
+          _dtype_code(qkv), _p(err_flag), _stream(qkv))
     return out
 
 

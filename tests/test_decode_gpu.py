@@ -179,3 +179,32 @@ def test_kv_append_device_position_out_of_range(oracle, xn, cuda):
     assert not torch.all(K[:, :, 3] == 7.0)  # position 3 written
     with pytest.raises(xn.XnError, match="out of range"):
         xn.kv_append_rope(qkv, h, cos, sin, K, V, 3)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16", "f16"])
+@pytest.mark.parametrize("interleaved", [True, False])
+@pytest.mark.parametrize("d", [32, 64, 128])
+def test_fused_step_equals_two_launches(oracle, xn, cuda, dtype, interleaved, d):
+    """xn_decode_attention_step gives the outputs and cache contents of
+    xn_kv_append_rope + xn_attention_decode, bit for bit, over a stream with
+    chunks, wrap and trim."""
+    b, h, cap, context = 2, 3, 12, 10
+    tdt = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}[dtype]
+    cos, sin = (to_device(a, dtype, cuda) for a in _tables(oracle, d, 64, dtype))
+    g = torch.Generator().manual_seed(d)
+    K1 = torch.zeros((b, h, cap, d), dtype=tdt, device=cuda)
+    V1, K2, V2 = torch.zeros_like(K1), torch.zeros_like(K1), torch.zeros_like(K1)
+    total = 0
+    for t in [3, 1, 2, 1, 1, 4, 1, 2, 1]:
+        qkv = torch.randn((b, t, 3 * h * d), generator=g).to(tdt).to(cuda)
+        for mask in ("relative", "absolute"):
+            K1c, V1c, K2c, V2c = K1.clone(), V1.clone(), K2.clone(), V2.clone()
+            q = xn.kv_append_rope(qkv, h, cos, sin, K1c, V1c, total, interleaved=interleaved)
+            a = xn.attention_decode(q, K1c, V1c, total, context, 0.125, mask=mask)
+            f = xn.decode_attention_step(qkv, h, cos, sin, K2c, V2c, total, context, 0.125,
+                                         interleaved=interleaved, mask=mask)
+            assert torch.equal(a, f)
+            assert torch.equal(K1c, K2c) and torch.equal(V1c, V2c)
+        xn.kv_append_rope(qkv, h, cos, sin, K1, V1, total, interleaved=interleaved)
+        xn.decode_attention_step(qkv, h, cos, sin, K2, V2, total, context, 0.125, interleaved=interleaved)
+        total += t
