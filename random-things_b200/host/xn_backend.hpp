@@ -78,6 +78,22 @@ struct Storage {
 // inplace_ops.rs:172-473 use these unary ops on the path.
 enum class UnaryOp { Silu, GeluErf };
 
+// Per-layer streaming-decode state: k and v are [b, h, cap, d] ring buffers
+// (position p in slot p % cap) and `total` counts the positions appended. It
+// stands for the reference's KvCache (mimi.rs:1099-1153,
+// pocket_tts/src/mimi_transformer.rs:10-61; cat then trim) and
+// StreamingMHAState (pocket_tts/src/transformer.rs:5-33; slice_set into a
+// preallocated buffer). The caller owns the two buffers.
+template <typename T>
+struct RingKvCache {
+  Storage<T> k, v;
+  size_t b = 0, h = 0, cap = 0, d = 0;
+  size_t total = 0;
+};
+
+// Which causal mask the decode attention applies (xn_fused.h XN_MASK_*).
+enum class DecodeMask { Relative = XN_MASK_RELATIVE, Absolute = XN_MASK_ABSOLUTE };
+
 // The CUDA device of the reference (cuda_backend.rs:34-54): one stream on
 // which every op is enqueued.
 class CudaDevice {
@@ -312,7 +328,75 @@ class CudaDevice {
           "rvq_decode_sum");
   }
 
+  // ---- Streaming decode: append the step's k / v (rotated k) to the ring
+  // cache and return the rotated q [b, h, t, d] (mimi.rs:1330-1354).
+  template <typename T>
+  void kv_append_rope(Storage<T> &q_out, RingKvCache<T> &cache, const Storage<T> &qkv, const Storage<T> &cos,
+                      const Storage<T> &sin, size_t t, bool interleaved) const {
+    const size_t b = cache.b, h = cache.h, d = cache.d;
+    check_cache(cache, "kv_append_rope");
+    expect_at_least(qkv, b * t * 3 * h * d, "kv_append_rope qkv");
+    expect_at_least(q_out, b * h * t * d, "kv_append_rope q_out");
+    const size_t max_pos = decode_max_pos(cos, sin, d, cache.total, t, "kv_append_rope");
+    check(xn_kv_append_rope(q_out.data, cache.k.data, cache.v.data, qkv.data, cos.data, sin.data, (int64_t)b,
+                            (int64_t)h, (int64_t)t, (int64_t)d, (int64_t)cache.total, nullptr, (int64_t)max_pos,
+                            (int64_t)cache.cap, interleaved ? 1 : 0, DTypeOf<T>::value, nullptr, stream_),
+          "kv_append_rope");
+    cache.total += t;
+  }
+
+  // Attention of q [b, h, t, d] (the step's t queries, already appended) over
+  // the last min(total, context) cached positions; out is [b, t, h * d]
+  // (mimi.rs:1356-1374).
+  template <typename T>
+  void attention_decode(Storage<T> &out, const Storage<T> &q, const RingKvCache<T> &cache, size_t t,
+                        size_t context, float scale, DecodeMask mask) const {
+    check_cache(cache, "attention_decode");
+    if (cache.total < t) throw Error("attention_decode: the step's positions are not in the cache");
+    expect_at_least(q, cache.b * cache.h * t * cache.d, "attention_decode q");
+    expect_at_least(out, cache.b * t * cache.h * cache.d, "attention_decode out");
+    check(xn_attention_decode(out.data, q.data, cache.k.data, cache.v.data, (int64_t)cache.b, (int64_t)cache.h,
+                              (int64_t)t, (int64_t)cache.d, (int64_t)(cache.total - t), nullptr, (int64_t)cache.cap,
+                              (int64_t)context, static_cast<int>(mask), scale, DTypeOf<T>::value, stream_),
+          "attention_decode");
+  }
+
+  // kv_append_rope + attention_decode in one launch.
+  template <typename T>
+  void decode_attention_step(Storage<T> &out, RingKvCache<T> &cache, const Storage<T> &qkv,
+                             const Storage<T> &cos, const Storage<T> &sin, size_t t, size_t context, float scale,
+                             DecodeMask mask, bool interleaved) const {
+    const size_t b = cache.b, h = cache.h, d = cache.d;
+    check_cache(cache, "decode_attention_step");
+    expect_at_least(qkv, b * t * 3 * h * d, "decode_attention_step qkv");
+    expect_at_least(out, b * t * h * d, "decode_attention_step out");
+    const size_t max_pos = decode_max_pos(cos, sin, d, cache.total, t, "decode_attention_step");
+    check(xn_decode_attention_step(out.data, cache.k.data, cache.v.data, qkv.data, cos.data, sin.data, (int64_t)b,
+                                   (int64_t)h, (int64_t)t, (int64_t)d, (int64_t)cache.total, nullptr,
+                                   (int64_t)max_pos, (int64_t)cache.cap, (int64_t)context, static_cast<int>(mask),
+                                   scale, interleaved ? 1 : 0, DTypeOf<T>::value, nullptr, stream_),
+          "decode_attention_step");
+    cache.total += t;
+  }
+
  private:
+  template <typename T>
+  static void check_cache(const RingKvCache<T> &c, const char *op) {
+    expect_at_least(c.k, c.b * c.h * c.cap * c.d, op);
+    expect_at_least(c.v, c.b * c.h * c.cap * c.d, op);
+  }
+  template <typename T>
+  static size_t decode_max_pos(const Storage<T> &cos, const Storage<T> &sin, size_t d, size_t pos, size_t t,
+                               const char *op) {
+    if (d % 2 != 0) throw Error(std::string(op) + " requires even d dimension, got d=" + std::to_string(d));
+    if (cos.len != sin.len) throw Error(std::string(op) + " cos/sin shape mismatch");
+    const size_t max_pos = d ? cos.len / (d / 2) : 0;
+    if (pos + t > max_pos)
+      throw Error(std::string(op) + " position out of range, pos=" + std::to_string(pos) + " + t=" +
+                      std::to_string(t) + " > max_pos=" + std::to_string(max_pos),
+                  XN_E_RANGE);
+    return max_pos;
+  }
   template <typename T>
   static void expect_len(const Storage<T> &s, size_t n, const char *what) {
     if (s.len != n)

@@ -180,6 +180,52 @@ void test_rope_identity(const CudaDevice &dev) {
   for (int i = 0; i < 1280; ++i) CHECK(std::fabs(v[i] - k[i]) < 1e-5f);
 }
 
+// Streaming decode on the ring cache (mimi.rs:1317-1384 op sequence): with
+// identity RoPE tables and a zero query every visible key scores 0, so each
+// step's output is the mean of the visible value rows. Values of step s are
+// all s + 1; context 2 keeps the last two positions.
+void test_decode_attention_mean_of_visible_values(const CudaDevice &dev) {
+  const size_t b = 1, h = 1, d = 32, cap = 2, context = 2, steps = 4;
+  for (int fused = 0; fused < 2; ++fused) {
+    DeviceVec<float> k(b * h * cap * d), v(b * h * cap * d);
+    xn::RingKvCache<float> cache;
+    cache.k = k.s;
+    cache.v = v.s;
+    cache.b = b, cache.h = h, cache.cap = cap, cache.d = d;
+    DeviceVec<float> cos(std::vector<float>(8 * d / 2, 1.0f)), sin(std::vector<float>(8 * d / 2, 0.0f));
+    DeviceVec<float> q(b * h * d), out(b * h * d);
+    const float expect[steps] = {1.0f, 1.5f, 2.5f, 3.5f};
+    for (size_t s = 0; s < steps; ++s) {
+      std::vector<float> qkv(3 * d, 0.0f);
+      for (size_t i = 0; i < d; ++i) {
+        qkv[d + i] = 0.25f * i;               // k (scores stay 0: q = 0)
+        qkv[2 * d + i] = static_cast<float>(s + 1);  // v
+      }
+      DeviceVec<float> qkv_d(qkv);
+      if (fused) {
+        dev.decode_attention_step(out.s, cache, qkv_d.s, cos.s, sin.s, 1, context, 0.125f, xn::DecodeMask::Relative,
+                                  true);
+      } else {
+        dev.kv_append_rope(q.s, cache, qkv_d.s, cos.s, sin.s, 1, true);
+        dev.attention_decode(out.s, q.s, cache, 1, context, 0.125f, xn::DecodeMask::Relative);
+      }
+      auto o = out.to_vec();
+      for (size_t i = 0; i < d; ++i) CHECK(std::fabs(o[i] - expect[s]) < 1e-6f);
+    }
+    CHECK(cache.total == steps);
+    bool threw = false;
+    DeviceVec<float> qkv_last(3 * d);
+    try {
+      cache.total = 8;  // past the 8 rows of the tables
+      dev.decode_attention_step(out.s, cache, qkv_last.s, cos.s, sin.s, 1, context, 0.125f, xn::DecodeMask::Relative,
+                                true);
+    } catch (const xn::Error &e) {
+      threw = e.code == XN_E_RANGE;
+    }
+    CHECK(threw);
+  }
+}
+
 }  // namespace
 
 int main() {
@@ -196,6 +242,7 @@ int main() {
       {"test_apply_causality_mask", test_apply_causality_mask},
       {"test_rope_position_offset", test_rope_position_offset},
       {"test_rope_identity", test_rope_identity},
+      {"test_decode_attention_mean_of_visible_values", test_decode_attention_mean_of_visible_values},
   };
   int failed = 0;
   for (const auto &t : tests) {
