@@ -438,6 +438,34 @@ __device__ __forceinline__ float div_by(float x, float d, float r) {
   return copysignf(__fmaf_rn(rem, r, q0), q0);
 }
 
+// exp(x) for a bf16 value x <= 0 (softmax's T(x - max)), accurate enough
+// that rounding it to bf16 gives the reference's T(exp(x)) (f32 exp, then
+// round to bf16): 2^(x * log2 e) with one f32 multiply (relative error
+// <= 2^-24 of t, so at most |t| * 2^-24 * ln 2 <= 2^-17.5 in the result for
+// |t| < 134, where results still reach the bf16 range) and the hardware 2^t
+// approximation (ex2.approx.f32, subnormal results kept). A result can only
+// round differently where exp(x) lies within that error of a bf16 rounding
+// midpoint; the softmax tests run every non-positive bf16 input (2^15 values)
+// through both softmax paths against glibc and find none. Not used for f32 or
+// f16, whose finer output grids would expose the error, nor for positive
+// arguments (SiLU's exp(-s)), which were not proven.
+__device__ __forceinline__ float exp_of_bf16(float x) {
+  float y;
+  asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(__fmul_rn(x, 0x1.715476p+0f)));
+  return y;
+}
+
+// exp of a non-positive argument as the T-typed reference computes it, before
+// the rounding to T.
+template <typename T>
+__device__ __forceinline__ float exp_t(float x) {
+  if constexpr (std::is_same_v<T, __nv_bfloat16>) {
+    return exp_of_bf16(x);
+  } else {
+    return expf(x);
+  }
+}
+
 // div_by on an element pair, for dividends that are never -0 (exp results):
 // with x = +0 every step is +0, so the sign fix-up is not needed. nd = -d,
 // r = __frcp_rn(d) in both lanes.

@@ -286,7 +286,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
   // Softmax in T arithmetic: e = T(exp(T(s - max))), p = T(e / sum).
   float sum = 0.f;
   for (int64_t j = tid; j < kv_len; j += kAttnThreads) {
-    const float e = Elem<T>::round(expf(Elem<T>::round(__fsub_rn(scores[j], mx))));
+    const float e = Elem<T>::round(exp_t<T>(Elem<T>::round(__fsub_rn(scores[j], mx))));
     scores[j] = e;
     sum = __fadd_rn(sum, e);
   }

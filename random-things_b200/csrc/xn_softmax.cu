@@ -134,7 +134,7 @@ __global__ void __launch_bounds__(512) softmax_regs_kernel(const SoftmaxParams p
 #pragma unroll
       for (int j = 0; j < W; ++j) {
         const float2 d = P::to_f2(__hsub2(w[j], m2));  // T(x - max); -inf stays -inf
-        const T2 e = P::from_f2(expf(d.x), expf(d.y));  // T(exp(...)); exp(-inf) = 0
+        const T2 e = P::from_f2(exp_t<T>(d.x), exp_t<T>(d.y));  // T(exp(...)); exp(-inf) = 0
         const float2 ef = P::to_f2(e);
         s = __fadd_rn(__fadd_rn(s, ef.x), ef.y);
         w[j] = e;
@@ -187,7 +187,7 @@ __global__ void __launch_bounds__(512) softmax_regs_kernel(const SoftmaxParams p
 #pragma unroll
       for (int j = 0; j < N; ++j) {
         // exp(-inf - max) = 0 for masked and padding entries.
-        x[k][j] = Elem<T>::round(expf(Elem<T>::round(__fsub_rn(x[k][j], mx))));
+        x[k][j] = Elem<T>::round(exp_t<T>(Elem<T>::round(__fsub_rn(x[k][j], mx))));
         s = __fadd_rn(s, x[k][j]);
       }
     }
@@ -338,7 +338,7 @@ __global__ void __launch_bounds__(512, NV >= 8 ? 1 : 2) softmax_pipe_kernel(cons
 #pragma unroll
         for (int j = 0; j < W; ++j) {
           const float2 d = P::to_f2(__hsub2(w[j], m2));  // T(x - max)
-          const T2 e = P::from_f2(expf(d.x), expf(d.y));  // T(exp(...))
+          const T2 e = P::from_f2(exp_t<T>(d.x), exp_t<T>(d.y));  // T(exp(...))
           s2 = __fadd2_rn(s2, P::to_f2(e));
           w[j] = e;
         }
@@ -399,7 +399,7 @@ __global__ void __launch_bounds__(1024) softmax_loop_kernel(const SoftmaxParams 
   for (int64_t c = threadIdx.x; c < p.cols; c += tpr) {
     float e = 0.f;
     if (c < lim) {
-      e = Elem<T>::round(expf(Elem<T>::round(__fsub_rn(load(c), mx))));
+      e = Elem<T>::round(exp_t<T>(Elem<T>::round(__fsub_rn(load(c), mx))));
       s = __fadd_rn(s, e);
     }
     dst[base + c] = Elem<T>::from_f32(e);

@@ -74,3 +74,28 @@ def test_attn_softmax_scaled(oracle, xn, cuda, dtype, shape, offset, scale):
         np.frombuffer(np.array([int(sc[0]) << 16], dtype=np.uint32).tobytes(), dtype=np.float32)[0])
     Y = xn.attn_softmax(to_device(s, dtype, cuda), scale_t, offset)
     assert_close(from_device(Y, dtype), ref, dtype, f"attn_softmax {dtype} {shape}")
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+@pytest.mark.parametrize("width", [8, 7])
+def test_softmax_exp_every_input(oracle, xn, cuda, dtype, width):
+    """Every non-positive 16-bit value v, through the vector path (rows of 8)
+    and the scalar path (rows of 7): rows [0, v, -inf, ...] have max 0, so
+    e = T(exp(T(v - 0))) = T(exp(v)) and the row sum 1 + e is the same in any
+    order. The outputs then equal the reference's bit for bit exactly when
+    every T(exp(v)) does; the test reports how many of the 2^15 inputs differ."""
+    bits = np.arange(0x8000, 0x10000, dtype=np.uint32).astype(np.uint16)  # sign set: -0 ... -NaN
+    vals = bits.view(np.int16).astype(np.int32) & 0x7FFF
+    exp_all_ones = 0x7F80 if dtype == "bf16" else 0x7C00
+    keep = vals <= exp_all_ones  # drop NaN patterns; keep -inf
+    v = bits[keep]
+    n = v.size
+    ninf = np.uint16(0xFF80 if dtype == "bf16" else 0xFC00)
+    x = np.full((n, width), ninf, dtype=np.uint16)
+    x[:, 0] = 0
+    x[:, 1] = v
+    ref = oracle.softmax(x, dtype)
+    got = from_device(xn.softmax(to_device(x, dtype, cuda)), dtype)
+    diff = np.nonzero(np.any(got != ref, axis=1))[0]
+    print(f"{dtype}: {diff.size} of {n} inputs differ")
+    assert diff.size == 0, f"first differing inputs: {[hex(int(b)) for b in v[diff[:8]]]}"
