@@ -427,6 +427,7 @@ def sweep(torch, xn, device, widths, rows_list, dtypes, reps: int, mem_cap_gb: f
     # L2 flush before every timed launch: write 256 MB (> the 126 MB L2), then
     # read another 256 MB buffer, so the L2 holds only clean lines of the
     # second buffer and the timed launch pays for no write-back of the flush.
+    # Events are created per launch inside the loop below.
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
     flush_clean = torch.zeros(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
     out = []
@@ -491,6 +492,10 @@ def sweep(torch, xn, device, widths, rows_list, dtypes, reps: int, mem_cap_gb: f
                     for _ in range(reps):
                         flush.zero_()
                         flush_clean.sum()
+                        # Keep the GPU busy (a fixed ~0.5 ms spin) while the host enqueues the
+                        # start event, the op and the stop event, so host launch latency never
+                        # shows up between the two events of a short launch.
+                        torch.cuda._sleep(1_000_000)
                         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                         e0.record()
                         fn()

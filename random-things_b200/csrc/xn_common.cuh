@@ -391,7 +391,14 @@ __device__ __forceinline__ uint4 rotate_interleaved(const uint4 &x, const uint2 
 // larger groups combine per-warp partials through shared memory `red`, which
 // must hold one float per warp of the block. The combination order is fixed,
 // so results are deterministic run to run.
+//
+// kReuse = false drops the trailing barrier that protects `red` from the
+// caller's next write to it. That is safe when every reduction of a row has
+// its own `red` array and each one is reached by every thread: a warp writes
+// an array again only after passing the barrier of a later reduction, which
+// every warp reaches only after its own reads of that array.
 // ---------------------------------------------------------------------------
+template <bool kReuse = true>
 __device__ __forceinline__ float group_sum(float v, int tpr, float *red) {
   const int width = tpr < 32 ? tpr : 32;
   for (int o = width >> 1; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -403,10 +410,11 @@ __device__ __forceinline__ float group_sum(float v, int tpr, float *red) {
   __syncthreads();
   float s = red[first];
   for (int w = 1; w < wpr; ++w) s = __fadd_rn(s, red[first + w]);
-  __syncthreads();  // `red` may be reused by the caller's next reduction
+  if constexpr (kReuse) __syncthreads();  // `red` may be reused by the caller's next reduction
   return s;
 }
 
+template <bool kReuse = true>
 __device__ __forceinline__ float group_max(float v, int tpr, float *red) {
   const int width = tpr < 32 ? tpr : 32;
   for (int o = width >> 1; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -418,7 +426,7 @@ __device__ __forceinline__ float group_max(float v, int tpr, float *red) {
   __syncthreads();
   float s = red[first];
   for (int w = 1; w < wpr; ++w) s = fmaxf(s, red[first + w]);
-  __syncthreads();
+  if constexpr (kReuse) __syncthreads();
   return s;
 }
 

@@ -88,6 +88,53 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const GatherParams p) 
   }
 }
 
+// Rows shorter than a warp's 32 x kUnroll units: a work item is `rpi`
+// consecutive output rows, read as one flat span of rpi * row_units units, so
+// every lane still has kUnroll accesses in flight and the stores of a warp are
+// one contiguous run. Each lane looks up the id of the row its unit falls in.
+template <typename U>
+__global__ void __launch_bounds__(256) gather_short_rows_kernel(const GatherParams p, int rpi) {
+  const int lane = threadIdx.x & 31;
+  const int ru = static_cast<int>(p.row_units);  // < 32 * kGatherUnroll
+  const int span = rpi * ru;
+  const int64_t items = (p.out_rows + rpi - 1) / rpi;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const bool one_slice = p.out_rows == p.n_ids;  // left == 1: no division by n_ids
+  for (int64_t item = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); item < items;
+       item += warps) {
+    const int64_t row0 = item * rpi;
+    U v[kGatherUnroll];
+    bool live[kGatherUnroll];
+#pragma unroll
+    for (int k = 0; k < kGatherUnroll; ++k) {
+      const int f = lane + k * 32;
+      const int r = f / ru;
+      const int64_t orow = row0 + r;
+      live[k] = f < span && orow < p.out_rows;
+      v[k] = U{};
+      if (live[k]) {
+        const int64_t l = one_slice ? 0 : orow / p.n_ids;
+        const int64_t i = orow - l * p.n_ids;
+        const int64_t id = load_id(p.ids, i, p.ids_i64);
+        if (id < 0 || id >= p.src_dim) {
+          if (p.err != nullptr) atomicOr(p.err, 1);
+        } else {
+          const U *src = static_cast<const U *>(p.src) + (l * p.src_dim + id) * p.row_units + (f - r * ru);
+          if constexpr (sizeof(U) == 16) {
+            v[k] = ld_stream(src);
+          } else {
+            v[k] = *src;
+          }
+        }
+      }
+    }
+    U *d = static_cast<U *>(p.dst) + row0 * p.row_units;
+#pragma unroll
+    for (int k = 0; k < kGatherUnroll; ++k)
+      if (live[k]) d[lane + k * 32] = v[k];
+  }
+}
+
 struct RvqTables {
   const void *p[XN_RVQ_MAX_CODEBOOKS];
 };
@@ -274,12 +321,32 @@ int xn_index_select(void *dst, const void *src, const void *ids, int ids_is_i64,
   const bool vec = row_bytes % 16 == 0 && is_aligned16(dst) && is_aligned16(src);
   p.row_units = vec ? row_bytes / 16 : right;
   // Enough warps for every work item, capped at 8 blocks of 8 warps per SM.
-  const int64_t items = out_rows * ceil_div(p.row_units, 32 * kGatherUnroll);
+  // Rows of at most half a warp's span are packed several to a work item.
+  const int64_t span = 32 * kGatherUnroll;
+  const int rpi = p.row_units > 0 && p.row_units * 2 <= span ? static_cast<int>(span / p.row_units) : 1;
+  const int64_t items = rpi > 1 ? ceil_div(out_rows, static_cast<int64_t>(rpi)) : out_rows * ceil_div(p.row_units, span);
   int64_t grid = ceil_div(items, 8);
   const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
   if (grid > cap) grid = cap;
-  if (vec) {
+  if (vec && rpi > 1) {
+    gather_short_rows_kernel<uint4><<<grid, 256, 0, st>>>(p, rpi);
+  } else if (vec) {
     gather_rows_kernel<uint4><<<grid, 256, 0, st>>>(p);
+  } else if (rpi > 1) {
+    switch (eb) {
+      case 1:
+        gather_short_rows_kernel<uint8_t><<<grid, 256, 0, st>>>(p, rpi);
+        break;
+      case 2:
+        gather_short_rows_kernel<uint16_t><<<grid, 256, 0, st>>>(p, rpi);
+        break;
+      case 4:
+        gather_short_rows_kernel<uint32_t><<<grid, 256, 0, st>>>(p, rpi);
+        break;
+      default:
+        gather_short_rows_kernel<unsigned long long><<<grid, 256, 0, st>>>(p, rpi);
+        break;
+    }
   } else {
     switch (eb) {
       case 1:

@@ -262,7 +262,8 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : (kMaxBlock =
   using P = Pairs<T>;
   constexpr int KP = P::kP;
   constexpr int N = Elem<T>::kVec;
-  __shared__ float red[32];
+  // One scratch array per reduction (see group_sum's kReuse); one row per group.
+  __shared__ float red_a[32], red_b[32];
   const int tpr = p.tpr;
   const int g = threadIdx.x / tpr;
   const int lr = threadIdx.x - g * tpr;
@@ -333,7 +334,7 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : (kMaxBlock =
 #pragma unroll
       for (int j = 0; j < KP; ++j) s2 = __fadd2_rn(s2, x[j]);
     }
-    const float mean = __fdiv_rn(group_sum(__fadd_rn(s2.x, s2.y), tpr, red), cols_f);
+    const float mean = __fdiv_rn(group_sum<false>(__fadd_rn(s2.x, s2.y), tpr, red_a), cols_f);
     const float2 nmean = splat2(-mean);
     float2 v2 = make_float2(0.f, 0.f);
 #pragma unroll
@@ -348,7 +349,7 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : (kMaxBlock =
         }
       }
     }
-    const float var = __fdiv_rn(group_sum(__fadd_rn(v2.x, v2.y), tpr, red), cols_f);
+    const float var = __fdiv_rn(group_sum<false>(__fadd_rn(v2.x, v2.y), tpr, red_b), cols_f);
     const float2 inv = splat2(__fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(var, p.eps))));
     // x + (-0) == x exactly (signed zeros included), so "no centring" is the
     // same instruction with a -0 shift.
@@ -386,7 +387,7 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : (kMaxBlock =
 #pragma unroll
       for (int j = 0; j < KP; ++j) s2 = __ffma2_rn(x[j], x[j], s2);
     }
-    const float s = group_sum(__fadd_rn(s2.x, s2.y), tpr, red);
+    const float s = group_sum<false>(__fadd_rn(s2.x, s2.y), tpr, red_a);
     const float m = __fsqrt_rn(__fadd_rn(__fdiv_rn(s, cols_f), p.eps));
     const float r = __frcp_rn(m);
     const float2 nm2 = splat2(-m), r2 = splat2(r);

@@ -220,7 +220,8 @@ __global__ void __launch_bounds__(512) softmax_regs_kernel(const SoftmaxParams p
 template <typename T, int NV, bool kCausal>
 __global__ void __launch_bounds__(512, NV >= 8 ? 1 : 2) softmax_pipe_kernel(const SoftmaxParams p) {
   constexpr int N = Elem<T>::kVec;
-  __shared__ float red[32];
+  // One scratch array per reduction of a row (see group_sum's kReuse).
+  __shared__ float red_max[32], red_sum[32];
   const int tpr = p.tpr;
   const int g = threadIdx.x / tpr;
   const int lr = threadIdx.x - g * tpr;
@@ -288,7 +289,7 @@ __global__ void __launch_bounds__(512, NV >= 8 ? 1 : 2) softmax_pipe_kernel(cons
         }
         m = fmaxf(m, fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3])));
       }
-      const float2 nmx = splat2(-group_max(m, tpr, red));
+      const float2 nmx = splat2(-group_max<false>(m, tpr, red_max));
 #pragma unroll
       for (int k = 0; k < NV; ++k) {
         float2 *x2 = reinterpret_cast<float2 *>(&cur[k]);
@@ -331,7 +332,7 @@ __global__ void __launch_bounds__(512, NV >= 8 ? 1 : 2) softmax_pipe_kernel(cons
         for (int j = 0; j < W; ++j) mx2 = __hmax2(mx2, w[j]);
       }
       const float2 mf = P::to_f2(mx2);
-      const T2 m2 = P::splat(group_max(fmaxf(mf.x, mf.y), tpr, red));  // exact: the max is a T value
+      const T2 m2 = P::splat(group_max<false>(fmaxf(mf.x, mf.y), tpr, red_max));  // exact: the max is a T value
 #pragma unroll
       for (int k = 0; k < NV; ++k) {
         T2 *w = reinterpret_cast<T2 *>(&cur[k]);
@@ -344,7 +345,7 @@ __global__ void __launch_bounds__(512, NV >= 8 ? 1 : 2) softmax_pipe_kernel(cons
         }
       }
     }
-    const float s = group_sum(__fadd_rn(s2.x, s2.y), tpr, red);
+    const float s = group_sum<false>(__fadd_rn(s2.x, s2.y), tpr, red_sum);
     // s >= 1 for a live row: its maximum contributes exp(0).
     const float2 rs = splat2(__frcp_rn(s)), ns = splat2(-s);
     if (row < p.rows) {

@@ -79,10 +79,12 @@ def test_rvq_bad_code_flag(xn, cuda):
     assert torch.all(Y[0, 0] == 3) and torch.all(Y[0, 1] == 1) and torch.all(Y[0, 2] == 3)
 
 
-@pytest.mark.parametrize("dtype,row", [("bf16", 1024), ("bf16", 4096), ("f32", 4096), ("bf16", 24576)])
-def test_index_select_bulk_path_with_bad_ids(oracle, xn, cuda, dtype, row):
-    """Rows of 2-48 KB take the bulk-copy path; bad ids interleaved with good
-    ones give zero rows and bit 1 of the flag, the other rows stay exact."""
+@pytest.mark.parametrize("dtype,row", [("bf16", 1024), ("bf16", 4096), ("f32", 4096), ("bf16", 24576),
+                                       ("bf16", 256), ("f32", 64), ("bf16", 24), ("f32", 12)])
+def test_index_select_bad_ids_in_every_row_shape(oracle, xn, cuda, dtype, row):
+    """Rows of 48 B to 48 KB (several rows per warp item, one item per row,
+    several items per row); bad ids interleaved with good ones give zero rows
+    and bit 1 of the flag, the other rows stay exact."""
     r = rng(row)
     table = to_storage(randn(r, (300, row)), dtype)
     ids = r.integers(0, 300, size=777)
