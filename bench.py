@@ -241,6 +241,24 @@ class LlamaPrefillOps:
         t = getattr(self, name)
         return t[b0:b1] if name in ("q", "k", "qo", "ko") else t[b0 * seq:b1 * seq]
 
+    def transfer_step(self, chunk: int = 1):
+        """The copies of e2e_step alone (same bytes, chunks and streams, no
+        kernels): the host-link bound of the end-to-end step."""
+        t = self.torch
+        B, seq = self.cfg["batch"], self.cfg["seq"]
+        for b0 in range(0, B, chunk):
+            b1 = min(B, b0 + chunk)
+            with t.cuda.stream(self.s_h2d):
+                for k, v in self.h_in.items():
+                    self._chunk(k, b0, b1).copy_(v[b0:b1] if k in ("q", "k") else v[b0 * seq:b1 * seq],
+                                                 non_blocking=True)
+            with t.cuda.stream(self.s_d2h):
+                for k, v in self.h_out.items():
+                    dst = v[b0:b1] if k in ("qo", "ko") else v[b0 * seq:b1 * seq]
+                    dst.copy_(self._chunk(k, b0, b1), non_blocking=True)
+        self.s_comp.wait_stream(self.s_h2d)
+        self.s_comp.wait_stream(self.s_d2h)
+
     def e2e_step(self, chunk: int = 1):
         """Chunk c's H2D waits for the previous step's kernels on chunk c (its
         inputs are being overwritten) and chunk c's kernels wait for the
@@ -762,7 +780,7 @@ def main() -> int:
 
     # End-to-end with host buffers (timed on the compute stream, which waits
     # for the last D2H copy of each step).
-    e2e_ms = float("nan")
+    e2e_ms = xfer_ms = float("nan")
     if args.e2e_steps > 0:
         wl.host_buffers()
         torch.cuda.synchronize()
@@ -778,6 +796,15 @@ def main() -> int:
         e1.record(stream)
         torch.cuda.synchronize()
         e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
+        # The same transfers without kernels: the PCIe bound the e2e step is measured against.
+        wl.transfer_step()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.e2e_steps):
+            wl.transfer_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        xfer_ms = e0.elapsed_time(e1) / args.e2e_steps
 
     mimi = None
     if args.mimi_steps > 0:
@@ -824,7 +851,10 @@ def main() -> int:
                 "value": round(world * step_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": UNIT,
                 "h2d_bytes_per_step": wl.h2d_bytes, "d2h_bytes_per_step": wl.d2h_bytes,
                 "ms_per_step": round(e2e_ms, 3),
-                "method": "per-sequence chunks; H2D, kernels and D2H on three streams"},
+                "transfer_only_ms_per_step": round(xfer_ms, 3),
+                "frac_of_transfer_bound": round(xfer_ms / e2e_ms, 3),
+                "method": "per-sequence chunks; H2D, kernels and D2H on three streams; the transfer bound is "
+                          "the same copies with no kernels"},
             "gpu_launches": len(ops) * args.steps,
             "mimi_decode": mimi,
             "streaming_decode": decode,
