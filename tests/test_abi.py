@@ -106,3 +106,34 @@ def test_python_mirror_checks(xn):
         xn.rms_norm(x, torch.ones(3), 1e-5)
     with pytest.raises(xn.XnError, match="3D or 4D"):
         xn.apply_causality_mask(torch.zeros(3, 3), 0)
+
+
+def test_error_messages_are_per_thread(xn):
+    """xn_last_error() is thread-local: two threads that fail different checks
+    at the same time each read back their own message (the C ABI is
+    reentrant; status codes never depend on another thread's call)."""
+    import threading
+
+    lib = xn.lib()
+    barrier = threading.Barrier(2)
+    seen = {}
+
+    def norm_thread():
+        barrier.wait()
+        for _ in range(200):
+            rc = lib.xn_rms_norm(1, 1, 1, None, None, None, 4, 8, 0.0, 2, None)
+            seen.setdefault("norm", set()).add((rc, xn.last_error().split(":")[0]))
+
+    def rope_thread():
+        barrier.wait()
+        for _ in range(200):
+            rc = lib.xn_rope(1, 1, 1, 1, 1, 1, 5, 8, 6, 10, 0, 0, 2, None)
+            seen.setdefault("rope", set()).add((rc, xn.last_error().split(":")[0]))
+
+    threads = [threading.Thread(target=norm_thread), threading.Thread(target=rope_thread)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    assert seen["norm"] == {(xn.XN_E_INVALID, "xn_rms_norm")}
+    assert seen["rope"] == {(xn.XN_E_RANGE, "xn_rope")}

@@ -60,3 +60,43 @@ def test_row_sharding_with_gather(world, rows):
         assert p.exitcode == 0
     assert all(ok for _, ok, _ in results)
     assert sum(c for _, _, c in results) == rows
+
+
+def _dying_worker(rank, world, port, q):
+    import datetime
+    import sys
+    from pathlib import Path
+
+    repo = Path(__file__).resolve().parents[1]
+    sys.path.insert(0, str(repo / "random-things_b200"))
+    import xn_fused
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    dist.barrier()
+    if rank == world - 1:
+        os._exit(3)  # this rank dies between steps, with nothing in flight
+    try:
+        xn_fused.all_gather_rows(torch.zeros((4, 8)), 4 * world)
+        q.put((rank, "no error"))
+    except Exception as e:  # the surviving rank must get an error, not hang
+        q.put((rank, type(e).__name__))
+
+
+def test_dead_rank_fails_the_gather_instead_of_hanging():
+    """A rank that exits between steps: the surviving rank's next collective
+    (the optional output all-gather) ends with an error within the process
+    group's short timeout, instead of waiting for ever."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    world = 2
+    procs = [ctx.Process(target=_dying_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    rank, outcome = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+    assert rank == 0 and outcome != "no error", outcome
+    assert procs[1].exitcode == 3
