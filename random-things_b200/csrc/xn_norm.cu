@@ -38,45 +38,14 @@ struct NormParams {
   int nvec;  // accesses per row
 };
 
-// Element access in units of N elements: N = kVec (16-byte vectors) or 1.
-template <typename T, bool kVector>
-struct Acc {
-  static constexpr int N = kVector ? Elem<T>::kVec : 1;
-  __device__ __forceinline__ static void load_stream(const void *base, int64_t e, float (&f)[N]) {
-    if constexpr (kVector) {
-      unpack<T>(ld_stream(static_cast<const T *>(base) + e), f);
-    } else {
-      f[0] = ld_elem<T>(base, e);
-    }
-  }
-  __device__ __forceinline__ static void load_cached(const void *base, int64_t e, float (&f)[N]) {
-    if constexpr (kVector) {
-      unpack<T>(ld_cached(static_cast<const T *>(base) + e), f);
-    } else {
-      f[0] = Elem<T>::to_f32(__ldg(static_cast<const T *>(base) + e));
-    }
-  }
-  __device__ __forceinline__ static void store(void *base, int64_t e, const float (&f)[N]) {
-    if constexpr (kVector) {
-      st_vec(static_cast<T *>(base) + e, pack<T>(f));
-    } else {
-      st_elem<T>(base, e, f[0]);
-    }
-  }
-};
-
-// One row per row group, the row held in registers as raw 16-byte vectors
-// (packed T), which halves the registers a bf16 / f16 row needs and lets each
-// thread keep up to 8 loads in flight. All loads of a thread (src, then
-// branch) are issued before any store; stores of residual_out / dst come last,
-// which also makes exact aliasing of dst or residual_out with src safe.
-// 256-thread blocks are held to 64 registers so four fit on an SM (1024
-// threads, each with up to 8 x 16-byte loads in flight); LayerNorm with 8
-// accesses per thread needs a few more and runs three blocks per SM.
-template <typename T, bool kVector, int NV, bool kLN, int kMaxBlock, bool kBranch>
-__global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? ((kLN && NV == 8) ? 3 : 4) : 1) norm_regs_kernel(const NormParams p) {
-  constexpr int N = Acc<T, kVector>::N;
-  using Raw = std::conditional_t<kVector, uint4, T>;
+// Scalar rows (widths that are not a multiple of the 16-byte vector, or
+// unaligned pointers): one row per row group of tpr threads, NV elements per
+// thread held in registers. All loads of a thread (src, then branch) are
+// issued before any store; stores of residual_out / dst come last, which also
+// makes exact aliasing of dst or residual_out with src safe. The arithmetic
+// is the vector kernel's, one element at a time.
+template <typename T, int NV, bool kLN, int kMaxBlock, bool kBranch>
+__global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : 1) norm_rows_kernel(const NormParams p) {
   __shared__ float red[32];
   const int tpr = p.tpr;
   const int g = threadIdx.x / tpr;
@@ -85,170 +54,81 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? ((kLN && NV == 8
   const int64_t row = static_cast<int64_t>(blockIdx.x) * rpb + g;
   const bool active = row < p.rows;
   const int64_t base = row * p.cols;
-  const Raw *src = reinterpret_cast<const Raw *>(static_cast<const T *>(p.src) + base);
+  const T *src = static_cast<const T *>(p.src) + base;
 
-  auto unpack_raw = [](const Raw &r, float (&f)[N]) {
-    if constexpr (kVector) {
-      unpack<T>(r, f);
-    } else {
-      f[0] = Elem<T>::to_f32(r);
-    }
-  };
-  auto pack_raw = [](const float (&f)[N]) -> Raw {
-    if constexpr (kVector) {
-      return pack<T>(f);
-    } else {
-      return Elem<T>::from_f32(f[0]);
-    }
-  };
-  // Second and third passes re-unpack the packed row (see opaque()).
-  auto unpack_again = [](const Raw &r, float (&f)[N]) {
-    if constexpr (kVector) {
-      unpack<T>(opaque(r), f);
-    } else {
-      f[0] = Elem<T>::to_f32(r);
-    }
-  };
-  auto load_raw = [](const Raw *ptr) -> Raw {
-    if constexpr (kVector) {
-      return ld_stream(ptr);
-    } else {
-      return *ptr;
-    }
-  };
-
-  // 1) h = src (+ T(branch * ls)), each op rounded to T, kept as packed T.
-  Raw h[NV];
+  // 1) h = src (+ T(branch * ls)), each op rounded to T; invalid slots hold 0.
+  float h[NV];
 #pragma unroll
   for (int k = 0; k < NV; ++k) {
-    const int vi = lr + k * tpr;
-    if (active && vi < p.nvec) {
-      h[k] = load_raw(src + vi);
-    } else {
-      h[k] = Raw{};
-    }
+    const int e = lr + k * tpr;
+    h[k] = (active && e < p.nvec) ? Elem<T>::to_f32(src[e]) : 0.f;
   }
   if constexpr (kBranch) {
-    const Raw *br = reinterpret_cast<const Raw *>(static_cast<const T *>(p.branch) + base);
-    Raw b[NV];
+    const T *br = static_cast<const T *>(p.branch) + base;
+    float b[NV];
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
-      const int vi = lr + k * tpr;
-      if (active && vi < p.nvec) b[k] = load_raw(br + vi);
+      const int e = lr + k * tpr;
+      b[k] = (active && e < p.nvec) ? Elem<T>::to_f32(br[e]) : 0.f;
     }
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
-      const int vi = lr + k * tpr;
-      if (active && vi < p.nvec) {
-        float x[N], y[N];
-        unpack_raw(h[k], x);
-        unpack_raw(b[k], y);
-        if (p.ls != nullptr) {
-          float s[N];
-          Acc<T, kVector>::load_cached(p.ls, static_cast<int64_t>(vi) * N, s);
-#pragma unroll
-          for (int j = 0; j < N; ++j) y[j] = Elem<T>::round(__fmul_rn(y[j], s[j]));
-        }
-#pragma unroll
-        for (int j = 0; j < N; ++j) x[j] = __fadd_rn(x[j], y[j]);
-        h[k] = pack_raw(x);  // rounds each sum to T
-      }
-    }
-    if (p.res_out != nullptr) {
-      Raw *ro = reinterpret_cast<Raw *>(static_cast<T *>(p.res_out) + base);
-#pragma unroll
-      for (int k = 0; k < NV; ++k) {
-        const int vi = lr + k * tpr;
-        if (active && vi < p.nvec) ro[vi] = h[k];
+      const int e = lr + k * tpr;
+      if (active && e < p.nvec) {
+        float y = b[k];
+        if (p.ls != nullptr) y = Elem<T>::round(__fmul_rn(y, ld_elem<T>(p.ls, e)));
+        h[k] = Elem<T>::round(__fadd_rn(h[k], y));
+        if (p.res_out != nullptr) st_elem<T>(p.res_out, base + e, h[k]);
       }
     }
   }
 
-  // 2) Row statistics in f32.
+  // 2) Row statistics in f32, then 3) dst = T(norm(h) * w (+ b)).
   const float cols_f = __ll2float_rn(p.cols);
-  float scale_a, shift_m, inv_m = 0.f;  // LN: inv_std, mean ; RMS: m, 1/m
   if constexpr (kLN) {
     float s = 0.f;
 #pragma unroll
-    for (int k = 0; k < NV; ++k) {
-      float x[N];
-      unpack_raw(h[k], x);
-#pragma unroll
-      for (int j = 0; j < N; ++j) s = __fadd_rn(s, x[j]);
-    }
-    s = group_sum(s, tpr, red);
-    const float mean = __fdiv_rn(s, cols_f);
+    for (int k = 0; k < NV; ++k) s = __fadd_rn(s, h[k]);
+    const float mean = __fdiv_rn(group_sum(s, tpr, red), cols_f);
     float v = 0.f;
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
       if (lr + k * tpr < p.nvec) {
-        float x[N];
-        unpack_again(h[k], x);
-#pragma unroll
-        for (int j = 0; j < N; ++j) {
-          const float d = __fsub_rn(x[j], mean);
-          v = __fmaf_rn(d, d, v);
-        }
+        const float d = __fsub_rn(h[k], mean);
+        v = __fmaf_rn(d, d, v);
       }
     }
-    v = group_sum(v, tpr, red);
-    const float var = __fdiv_rn(v, cols_f);
-    scale_a = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(var, p.eps)));
-    shift_m = mean;
+    const float var = __fdiv_rn(group_sum(v, tpr, red), cols_f);
+    const float inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(var, p.eps)));
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int e = lr + k * tpr;
+      if (active && e < p.nvec) {
+        const float w = p.w != nullptr ? ld_elem<T>(p.w, e) : 1.f;
+        const float b = p.b != nullptr ? ld_elem<T>(p.b, e) : 0.f;
+        const float c = p.remove_mean ? __fsub_rn(h[k], mean) : h[k];
+        st_elem<T>(p.dst, base + e, __fadd_rn(__fmul_rn(__fmul_rn(c, inv), w), b));
+      }
+    }
   } else {
     float s = 0.f;
 #pragma unroll
+    for (int k = 0; k < NV; ++k) s = __fmaf_rn(h[k], h[k], s);
+    const float m = __fsqrt_rn(__fadd_rn(__fdiv_rn(group_sum(s, tpr, red), cols_f), p.eps));
+    const float r = __frcp_rn(m);
+#pragma unroll
     for (int k = 0; k < NV; ++k) {
-      float x[N];
-      unpack_raw(h[k], x);
-#pragma unroll
-      for (int j = 0; j < N; ++j) s = __fmaf_rn(x[j], x[j], s);
-    }
-    s = group_sum(s, tpr, red);
-    scale_a = __fsqrt_rn(__fadd_rn(__fdiv_rn(s, cols_f), p.eps));
-    inv_m = __frcp_rn(scale_a);
-    shift_m = 0.f;
-  }
-
-  // 3) Epilogue: dst = T(norm(h) * w (+ b)).
-  Raw *dst = reinterpret_cast<Raw *>(static_cast<T *>(p.dst) + base);
-#pragma unroll
-  for (int k = 0; k < NV; ++k) {
-    const int vi = lr + k * tpr;
-    if (active && vi < p.nvec) {
-      const int64_t col = static_cast<int64_t>(vi) * N;
-      float x[N], wv[N], out[N];
-      unpack_again(h[k], x);
-      if (p.w != nullptr) {
-        Acc<T, kVector>::load_cached(p.w, col, wv);
-      } else {
-#pragma unroll
-        for (int j = 0; j < N; ++j) wv[j] = 1.f;
-      }
-      if constexpr (kLN) {
-        float bv[N];
-        if (p.b != nullptr) {
-          Acc<T, kVector>::load_cached(p.b, col, bv);
-        } else {
-#pragma unroll
-          for (int j = 0; j < N; ++j) bv[j] = 0.f;
-        }
-#pragma unroll
-        for (int j = 0; j < N; ++j) {
-          const float c = p.remove_mean ? __fsub_rn(x[j], shift_m) : x[j];
-          out[j] = __fadd_rn(__fmul_rn(__fmul_rn(c, scale_a), wv[j]), bv[j]);
-        }
-      } else {
+      const int e = lr + k * tpr;
+      if (active && e < p.nvec) {
+        const float w = p.w != nullptr ? ld_elem<T>(p.w, e) : 1.f;
         // T(x / m * alpha): the IEEE quotient x / m via div_by, then * alpha.
-#pragma unroll
-        for (int j = 0; j < N; ++j) out[j] = __fmul_rn(div_by(x[j], scale_a, inv_m), wv[j]);
+        st_elem<T>(p.dst, base + e, __fmul_rn(div_by(h[k], m, r), w));
       }
-      dst[vi] = pack_raw(out);
     }
   }
 }
 
-// The 16-byte vector path. Same row-group structure as norm_regs_kernel, with
+// The 16-byte vector path. Same row-group structure as norm_rows_kernel, with
 // every f32 step on adjacent element pairs through the sm_100 paired
 // instructions (two IEEE f32 operations per instruction, so per pair: LN one
 // add for the sum, two for the centred squares, four in the epilogue; RMS one
@@ -474,7 +354,7 @@ __global__ void __launch_bounds__(1024) norm_loop_kernel(const NormParams p) {
 // Accesses per thread: up to 8 in 256- and 512-thread blocks (4 with a
 // branch, whose vectors are held too) and up to 4 in the 1024-thread shape
 // used for the widest rows. Only shapes within the cap are instantiated.
-template <int N, bool kBranch, int kMaxBlock>
+template <bool kBranch, int kMaxBlock>
 constexpr int kMaxNv = (kBranch || kMaxBlock > 512) ? 4 : 8;
 
 // One launch of the row-group kernel with NV accesses per thread: the paired
@@ -484,15 +364,14 @@ void launch_nv(const NormParams &p, int block, int64_t grid, cudaStream_t st) {
   if constexpr (kVector) {
     norm_vec_kernel<T, NV, kLN, kMaxBlock, kBranch><<<grid, block, 0, st>>>(p);
   } else {
-    norm_regs_kernel<T, false, NV, kLN, kMaxBlock, kBranch><<<grid, block, 0, st>>>(p);
+    norm_rows_kernel<T, NV, kLN, kMaxBlock, kBranch><<<grid, block, 0, st>>>(p);
   }
 }
 
 // Returns false when no instantiated kernel has this shape (a dispatcher bug).
 template <typename T, bool kVector, bool kLN, int kMaxBlock, bool kBranch>
 bool launch_regs_b(NormParams p, int nv, int block, int64_t grid, cudaStream_t st) {
-  constexpr int N = Acc<T, kVector>::N;
-  constexpr int cap = kMaxNv<N, kBranch, kMaxBlock>;
+  constexpr int cap = kMaxNv<kBranch, kMaxBlock>;
   switch (nv) {
     case 1:
       launch_nv<T, kVector, 1, kLN, kMaxBlock, kBranch>(p, block, grid, st);

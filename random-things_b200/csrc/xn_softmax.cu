@@ -69,16 +69,14 @@ struct Pair<__half> {
   }
 };
 
-// One row per row group, held in registers. Steps, in the reference's T
-// arithmetic (cpu_backend.rs:667-689): [x = T(x * scale)], max, e = T(exp(T(x -
-// max))), sum of f32(e), y = T(e / sum). For 16-bit T the row stays packed and
-// the max, the subtraction and the scale run as paired bf16x2 / f16x2
-// instructions, which round exactly once as the reference's T operations do;
-// exp and the division run in f32. Causal rows (kCausal) treat columns past
-// offset + (row % t1) as -inf, i.e. they are neither read nor exp'd and give 0.
-template <typename T, bool kVector, int NV, bool kCausal>
-__global__ void __launch_bounds__(512) softmax_regs_kernel(const SoftmaxParams p) {
-  constexpr int N = kVector ? Elem<T>::kVec : 1;
+// Scalar rows (widths that are not a multiple of the 16-byte vector, or
+// unaligned pointers): one row per row group, NV elements per thread held in
+// registers. Steps, in the reference's T arithmetic (cpu_backend.rs:667-689):
+// [x = T(x * scale)], max, e = T(exp(T(x - max))), sum of f32(e),
+// y = T(e / sum). Causal rows (kCausal) treat columns past
+// offset + (row % t1) as -inf: they are neither read nor exp'd and give 0.
+template <typename T, int NV, bool kCausal>
+__global__ void __launch_bounds__(512) softmax_rows_kernel(const SoftmaxParams p) {
   __shared__ float red[32];
   const int tpr = p.tpr;
   const int g = threadIdx.x / tpr;
@@ -97,117 +95,31 @@ __global__ void __launch_bounds__(512) softmax_regs_kernel(const SoftmaxParams p
   const T *src = static_cast<const T *>(p.src) + row * p.cols;
   T *dst = static_cast<T *>(p.dst) + row * p.cols;
 
-  if constexpr (kVector && !std::is_same_v<T, float>) {
-    using P = Pair<T>;
-    using T2 = typename P::T2;
-    constexpr int W = N / 2;  // pairs per vector
-    uint4 raw[NV];
-    T2 mx2 = P::neg_inf();
-    const T2 sc2 = P::splat(p.scale);
+  float x[NV];
+  float mx = -INFINITY;
 #pragma unroll
-    for (int k = 0; k < NV; ++k) {
-      const int e0 = (lr + k * tpr) * N;
-      if (e0 < lim) {
-        raw[k] = ld_stream(src + e0);
-        T2 *w = reinterpret_cast<T2 *>(&raw[k]);
-#pragma unroll
-        for (int j = 0; j < W; ++j) {
-          if (p.scaled) w[j] = __hmul2(w[j], sc2);
-          if constexpr (kCausal) {
-            if (e0 + 2 * j >= lim) w[j] = P::neg_inf();
-            else if (e0 + 2 * j + 1 >= lim) w[j] = P::mask_high(w[j]);
-          }
-          mx2 = __hmax2(mx2, w[j]);
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < W; ++j) reinterpret_cast<T2 *>(&raw[k])[j] = P::neg_inf();
-      }
+  for (int k = 0; k < NV; ++k) {
+    const int e = lr + k * tpr;
+    x[k] = -INFINITY;  // masked and padding entries: exp(-inf - max) = 0
+    if (e < lim) {
+      x[k] = Elem<T>::to_f32(src[e]);
+      if (p.scaled) x[k] = Elem<T>::round(__fmul_rn(x[k], Elem<T>::round(p.scale)));
     }
-    const float2 mf = P::to_f2(mx2);
-    const float mx = group_max(fmaxf(mf.x, mf.y), tpr, red);
-    const T2 m2 = P::splat(mx);  // exact: mx is a T value
-    float s = 0.f;
+    mx = fmaxf(mx, x[k]);
+  }
+  mx = group_max(mx, tpr, red);
+  float s = 0.f;
 #pragma unroll
-    for (int k = 0; k < NV; ++k) {
-      T2 *w = reinterpret_cast<T2 *>(&raw[k]);
+  for (int k = 0; k < NV; ++k) {
+    x[k] = Elem<T>::round(exp_t<T>(Elem<T>::round(__fsub_rn(x[k], mx))));
+    s = __fadd_rn(s, x[k]);
+  }
+  s = group_sum(s, tpr, red);
+  const float rs = __frcp_rn(s);
 #pragma unroll
-      for (int j = 0; j < W; ++j) {
-        const float2 d = P::to_f2(__hsub2(w[j], m2));  // T(x - max); -inf stays -inf
-        const T2 e = P::from_f2(exp_t<T>(d.x), exp_t<T>(d.y));  // T(exp(...)); exp(-inf) = 0
-        const float2 ef = P::to_f2(e);
-        s = __fadd_rn(__fadd_rn(s, ef.x), ef.y);
-        w[j] = e;
-      }
-    }
-    s = group_sum(s, tpr, red);
-    const float rs = __frcp_rn(s);  // s >= 1: the row maximum contributes exp(0)
-#pragma unroll
-    for (int k = 0; k < NV; ++k) {
-      const int e0 = (lr + k * tpr) * N;
-      if (active && lr + k * tpr < p.nvec) {
-        T2 *w = reinterpret_cast<T2 *>(&raw[k]);
-#pragma unroll
-        for (int j = 0; j < W; ++j) {
-          const float2 e = P::to_f2(w[j]);
-          w[j] = P::from_f2(div_by(e.x, s, rs), div_by(e.y, s, rs));
-        }
-        st_vec(dst + e0, raw[k]);
-      }
-    }
-  } else {
-    float x[NV][N];
-    float mx = -INFINITY;
-#pragma unroll
-    for (int k = 0; k < NV; ++k) {
-      const int e0 = (lr + k * tpr) * N;
-      if (e0 < lim) {
-        if constexpr (kVector) {
-          unpack<T>(ld_stream(src + e0), x[k]);
-        } else {
-          x[k][0] = Elem<T>::to_f32(src[e0]);
-        }
-#pragma unroll
-        for (int j = 0; j < N; ++j) {
-          if (p.scaled) x[k][j] = Elem<T>::round(__fmul_rn(x[k][j], Elem<T>::round(p.scale)));
-          if constexpr (kCausal) {
-            if (e0 + j >= lim) x[k][j] = -INFINITY;
-          }
-          mx = fmaxf(mx, x[k][j]);
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < N; ++j) x[k][j] = -INFINITY;
-      }
-    }
-    mx = group_max(mx, tpr, red);
-    float s = 0.f;
-#pragma unroll
-    for (int k = 0; k < NV; ++k) {
-#pragma unroll
-      for (int j = 0; j < N; ++j) {
-        // exp(-inf - max) = 0 for masked and padding entries.
-        x[k][j] = Elem<T>::round(exp_t<T>(Elem<T>::round(__fsub_rn(x[k][j], mx))));
-        s = __fadd_rn(s, x[k][j]);
-      }
-    }
-    s = group_sum(s, tpr, red);
-    const float rs = __frcp_rn(s);
-#pragma unroll
-    for (int k = 0; k < NV; ++k) {
-      const int vi = lr + k * tpr;
-      if (active && vi < p.nvec) {
-        const int e0 = vi * N;
-        float y[N];
-#pragma unroll
-        for (int j = 0; j < N; ++j) y[j] = div_by(x[k][j], s, rs);
-        if constexpr (kVector) {
-          st_vec(dst + e0, pack<T>(y));
-        } else {
-          dst[e0] = Elem<T>::from_f32(y[0]);
-        }
-      }
-    }
+  for (int k = 0; k < NV; ++k) {
+    const int e = lr + k * tpr;
+    if (active && e < p.nvec) dst[e] = Elem<T>::from_f32(div_by(x[k], s, rs));
   }
 }
 
@@ -215,7 +127,9 @@ __global__ void __launch_bounds__(512) softmax_regs_kernel(const SoftmaxParams p
 // row, row + step, ... (step = all groups of the grid) and issues the loads of
 // its next row before computing the current one, so HBM reads stay in flight
 // through the reductions and the exp / divide work. Arithmetic as
-// softmax_regs_kernel. The loop bound depends only on the block, so blocks
+// softmax_rows_kernel; for 16-bit T the row stays packed and the max, the
+// subtraction and the scale run as paired bf16x2 / f16x2 instructions, which
+// round exactly once as the reference's T operations do. The loop bound depends only on the block, so blocks
 // whose row groups span several warps keep their __syncthreads uniform.
 template <typename T, int NV, bool kCausal>
 __global__ void __launch_bounds__(512, NV >= 8 ? 1 : 2) softmax_pipe_kernel(const SoftmaxParams p) {
@@ -452,26 +366,25 @@ bool launch_softmax_pipe(const SoftmaxParams &p, int nv, int block, int64_t grid
 // Returns false when no instantiated kernel has this shape (a dispatcher bug).
 template <typename T, bool kVector, bool kCausal>
 bool launch_softmax_regs_c(const SoftmaxParams &p, int nv, int block, int64_t grid, cudaStream_t st) {
-  if constexpr (kVector) return launch_softmax_pipe<T, kCausal>(p, nv, block, grid, st);
-  constexpr int N = kVector ? Elem<T>::kVec : 1;
-  switch (nv) {
-    case 1:
-      softmax_regs_kernel<T, kVector, 1, kCausal><<<grid, block, 0, st>>>(p);
-      return true;
-    case 2:
-      softmax_regs_kernel<T, kVector, 2, kCausal><<<grid, block, 0, st>>>(p);
-      return true;
-    case 4:
-      softmax_regs_kernel<T, kVector, 4, kCausal><<<grid, block, 0, st>>>(p);
-      return true;
-    case 8:
-      if constexpr (8 * N <= 32) {
-        softmax_regs_kernel<T, kVector, 8, kCausal><<<grid, block, 0, st>>>(p);
+  if constexpr (kVector) {
+    return launch_softmax_pipe<T, kCausal>(p, nv, block, grid, st);
+  } else {
+    switch (nv) {
+      case 1:
+        softmax_rows_kernel<T, 1, kCausal><<<grid, block, 0, st>>>(p);
         return true;
-      }
-      return false;
-    default:
-      return false;
+      case 2:
+        softmax_rows_kernel<T, 2, kCausal><<<grid, block, 0, st>>>(p);
+        return true;
+      case 4:
+        softmax_rows_kernel<T, 4, kCausal><<<grid, block, 0, st>>>(p);
+        return true;
+      case 8:
+        softmax_rows_kernel<T, 8, kCausal><<<grid, block, 0, st>>>(p);
+        return true;
+      default:
+        return false;
+    }
   }
 }
 
