@@ -48,8 +48,8 @@ CFG = dict(batch=8, seq=4096, hidden=4096, heads_q=32, heads_kv=8, head_dim=128,
            vocab=128256, theta=500000.0, eps=1e-5)
 OPS = ["embedding_gather", "rms_norm", "rope_qk", "rms_norm_residual", "swiglu"]
 # Kernel-name fragments of each op (ncu launch list and roofline traffic).
-KERNELS = {"embedding_gather": "gather_rows_kernel", "rms_norm": "norm_regs_kernel",
-           "rope_qk": "rope_kernel", "rms_norm_residual": "norm_regs_kernel", "swiglu": "swiglu_kernel"}
+KERNELS = {"embedding_gather": "gather_rows_kernel", "rms_norm": "norm_vec_kernel",
+           "rope_qk": "rope_kernel", "rms_norm_residual": "norm_vec_kernel", "swiglu": "swiglu_kernel"}
 
 
 def op_bytes(cfg: dict, rows: int, s: int = 2, id_bytes: int = 4) -> dict:
