@@ -841,7 +841,8 @@ def main() -> int:
             "data": "synthetic (seeded N(0,1) activations, N(0,0.02) table, N(1,0.02) gains, uniform ids)",
             "config": config_block(world, cfg, ops),
             "pct_of_hbm_peak": round(100.0 * value / world / peak, 1),
-            "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": peak,
+            "roofline": {"bound": "hbm", "kernel": dom, "kernel_fn": KERNELS[dom], "achieved": round(achieved, 1),
+                         "peak": peak,
                          "peak_source": peak_src, "unit": "GB/s", "frac": round(achieved / peak, 3),
                          "traffic": traffic, "algorithmic_bytes": wl.bytes[dom]},
             "per_op": {n: {"ms": round(per_op_ms[n], 4), "bytes": wl.bytes[n],
