@@ -806,6 +806,23 @@ def main() -> int:
         torch.cuda.synchronize()
         xfer_ms = e0.elapsed_time(e1) / args.e2e_steps
 
+    # The optional output all-gather (not on the data path): the residual-RMSNorm
+    # output of every rank gathered into the full tensor on every rank, timed
+    # separately through the public API (NCCL over NVLink).
+    gather_ms = float("nan")
+    if distributed and hasattr(wl, "y2"):
+        for _ in range(3):
+            xn.all_gather_rows(wl.y2, wl.rows * world)
+        torch.cuda.synchronize()
+        dist.barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for _ in range(5):
+            xn.all_gather_rows(wl.y2, wl.rows * world)
+        g1.record(stream)
+        torch.cuda.synchronize()
+        gather_ms = g0.elapsed_time(g1) / 5
+
     mimi = None
     if args.mimi_steps > 0:
         mimi = mimi_rate(torch, dev, args.mimi_steps)
@@ -814,17 +831,20 @@ def main() -> int:
         decode = {act: decode_rate(torch, dev, args.decode_steps, act) for act in ("silu", "gelu_erf")}
 
     if distributed:
-        vals = [elapsed_ms, e2e_ms, mimi["ms_per_decode"] if mimi else 0.0, mimi["e2e_frames_per_s"] if mimi else 0.0]
+        vals = [elapsed_ms, e2e_ms, mimi["ms_per_decode"] if mimi else 0.0, gather_ms if gather_ms == gather_ms else 0.0,
+                mimi["e2e_frames_per_s"] if mimi else 0.0]
         t = torch.tensor(vals, dtype=torch.float64, device=dev)
-        dist.all_reduce(t[:3], op=dist.ReduceOp.MAX)
-        dist.all_reduce(t[3:], op=dist.ReduceOp.MIN)
+        dist.all_reduce(t[:4], op=dist.ReduceOp.MAX)
+        dist.all_reduce(t[4:], op=dist.ReduceOp.MIN)
         elapsed_ms, e2e_ms = float(t[0]), float(t[1])
+        if gather_ms == gather_ms:
+            gather_ms = float(t[3])
         if mimi:
             # Whole-job rate: every rank decodes its own batch; the slowest rank sets the time.
             n = mimi["batch"] * mimi["frames"]
             mimi["ms_per_decode"] = round(float(t[2]), 4)
             mimi["frames_per_s"] = round(world * n / (float(t[2]) * 1e-3), 1)
-            mimi["e2e_frames_per_s"] = round(world * float(t[3]), 1)
+            mimi["e2e_frames_per_s"] = round(world * float(t[4]), 1)
 
     if rank == 0:
         step_bytes = sum(wl.bytes.values())
@@ -857,6 +877,13 @@ def main() -> int:
                 "method": "per-sequence chunks; H2D, kernels and D2H on three streams; the transfer bound is "
                           "the same copies with no kernels"},
             "gpu_launches": len(ops) * args.steps,
+            "all_gather": None if gather_ms != gather_ms else {
+                "what": "optional output all-gather (xn_fused.all_gather_rows) of the residual-RMSNorm output, "
+                        f"[{wl.rows}, {cfg['hidden']}] bf16 per rank, into the full tensor on every rank; NCCL over "
+                        "NVLink; not on the data path",
+                "bytes_out": wl.rows * world * cfg["hidden"] * 2, "ms": round(gather_ms, 4),
+                "algbw_gbs": round(wl.rows * world * cfg["hidden"] * 2 / (gather_ms * 1e-3) / 1e9, 1),
+                "busbw_gbs": round(wl.rows * (world - 1) * cfg["hidden"] * 2 / (gather_ms * 1e-3) / 1e9, 1)},
             "mimi_decode": mimi,
             "streaming_decode": decode,
             "clocks": clocks,

@@ -770,8 +770,11 @@ def all_gather_rows(local: torch.Tensor, rows: int, group=None) -> torch.Tensor:
     world = dist.get_world_size(group)
     per = -(-rows // world) if world > 0 else 0
     tail = local.shape[1:]
-    padded = torch.zeros((per, *tail), dtype=local.dtype, device=local.device)
-    padded[: local.shape[0]] = local
+    if local.shape[0] == per and local.is_contiguous():
+        padded = local  # an even split needs no padding copy
+    else:
+        padded = torch.zeros((per, *tail), dtype=local.dtype, device=local.device)
+        padded[: local.shape[0]] = local
     if dist.get_backend(group) == "nccl":
         full = torch.empty((per * world, *tail), dtype=local.dtype, device=local.device)
         dist.all_gather_into_tensor(full, padded, group=group)
