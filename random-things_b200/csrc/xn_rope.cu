@@ -56,13 +56,25 @@ __global__ void __launch_bounds__(256) rope_kernel(const RopeParams p) {
   const RopeTensor tn = p.ten[which];
   const uint32_t H = tn.heads;
   const uint32_t hg_count = (H + p.hpt - 1) / p.hpt;
-  // item = ((bi * hg_count + hg) * T + ti) * chunks + c
+  // Work order follows the memory order of the layout, so consecutive warps
+  // stream consecutive bytes:
+  //   [B,H,T,D]: item = ((bi * hg_count + hg) * T + ti) * chunks + c
+  //   [B,T,H,D]: item = ((bi * T + ti) * hg_count + hg) * chunks + c
   const uint32_t c = item % p.chunks;
   uint32_t rest = item / p.chunks;
-  const uint32_t ti = rest % p.t;
-  rest /= p.t;
-  const uint32_t hg = rest % hg_count;
-  const uint32_t bi = rest / hg_count;
+  uint32_t ti, hg;
+  if (p.layout == XN_LAYOUT_BHTD) {
+    ti = rest % p.t;
+    rest /= p.t;
+    hg = rest % hg_count;
+    rest /= hg_count;
+  } else {
+    hg = rest % hg_count;
+    rest /= hg_count;
+    ti = rest % p.t;
+    rest /= p.t;
+  }
+  const uint32_t bi = rest;
 
   const int64_t d = p.d;
   const int64_t half = d / 2;
