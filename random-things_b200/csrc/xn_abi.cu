@@ -1,6 +1,7 @@
 // xn_abi.cu - error reporting and small host utilities of the C ABI.
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 
 #include "xn_internal.h"
@@ -46,6 +47,14 @@ int dtype_bytes(int dtype) {
     default:
       return 0;
   }
+}
+
+bool pdl_enabled() {
+  static const bool enabled = [] {
+    const char *v = std::getenv("XN_PDL");
+    return !(v != nullptr && v[0] == '0');
+  }();
+  return enabled;
 }
 
 int sm_count() {

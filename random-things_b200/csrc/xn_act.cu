@@ -73,6 +73,8 @@ constexpr int kUnroll = 4;
 
 template <typename T, int OP, bool kVector>
 __global__ void __launch_bounds__(kBlock) unary_kernel(void *dst, const void *src, int64_t n) {
+  griddep_wait();
+  griddep_release();
   constexpr int N = kVector ? Elem<T>::kVec : 1;
   const int64_t nacc = n / N;
   const int64_t base = static_cast<int64_t>(blockIdx.x) * kBlock * kUnroll + threadIdx.x;
@@ -126,6 +128,8 @@ template <typename T, bool kVector>
 __global__ void __launch_bounds__(kBlock) swiglu_kernel(void *dst, const void *gate, const void *up,
                                                          int64_t rows, int64_t cols, int64_t gs,
                                                          int64_t us) {
+  griddep_wait();
+  griddep_release();
   constexpr int N = kVector ? Elem<T>::kVec : 1;
   const int64_t cacc = cols / N;
   const int64_t c0 = static_cast<int64_t>(blockIdx.x) * kBlock * kUnroll + threadIdx.x;
@@ -188,6 +192,8 @@ __global__ void __launch_bounds__(kBlock) swiglu_kernel(void *dst, const void *g
 template <typename T, bool kVector>
 __global__ void __launch_bounds__(kBlock) residual_kernel(void *dst, const void *x, const void *branch,
                                                            const void *ls, int64_t rows, int64_t cols) {
+  griddep_wait();
+  griddep_release();
   constexpr int N = kVector ? Elem<T>::kVec : 1;
   const int64_t cacc = cols / N;
   const int64_t c0 = static_cast<int64_t>(blockIdx.x) * kBlock * kUnroll + threadIdx.x;
@@ -247,9 +253,9 @@ int launch_residual(void *dst, const void *x, const void *branch, const void *ls
   const int64_t gy = rows < 65535 ? rows : 65535;
   dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy));
   if (vec)
-    residual_kernel<T, true><<<grid, kBlock, 0, st>>>(dst, x, branch, ls, rows, cols);
+    launch_k(residual_kernel<T, true>, dim3(grid), dim3(kBlock), 0, st, dst, x, branch, ls, rows, cols);
   else
-    residual_kernel<T, false><<<grid, kBlock, 0, st>>>(dst, x, branch, ls, rows, cols);
+    launch_k(residual_kernel<T, false>, dim3(grid), dim3(kBlock), 0, st, dst, x, branch, ls, rows, cols);
   return check_launch("xn_residual_add");
 }
 
@@ -262,14 +268,14 @@ int launch_unary(void *dst, const void *src, int64_t n, int op, cudaStream_t st)
   if (grid > 0x7fffffffLL) return fail(XN_E_INVALID, "xn_unary: too many elements");
   if (op == XN_UNARY_SILU) {
     if (vec)
-      unary_kernel<T, XN_UNARY_SILU, true><<<grid, kBlock, 0, st>>>(dst, src, n);
+      launch_k(unary_kernel<T, XN_UNARY_SILU, true>, dim3(grid), dim3(kBlock), 0, st, dst, src, n);
     else
-      unary_kernel<T, XN_UNARY_SILU, false><<<grid, kBlock, 0, st>>>(dst, src, n);
+      launch_k(unary_kernel<T, XN_UNARY_SILU, false>, dim3(grid), dim3(kBlock), 0, st, dst, src, n);
   } else {
     if (vec)
-      unary_kernel<T, XN_UNARY_GELU_ERF, true><<<grid, kBlock, 0, st>>>(dst, src, n);
+      launch_k(unary_kernel<T, XN_UNARY_GELU_ERF, true>, dim3(grid), dim3(kBlock), 0, st, dst, src, n);
     else
-      unary_kernel<T, XN_UNARY_GELU_ERF, false><<<grid, kBlock, 0, st>>>(dst, src, n);
+      launch_k(unary_kernel<T, XN_UNARY_GELU_ERF, false>, dim3(grid), dim3(kBlock), 0, st, dst, src, n);
   }
   return check_launch("xn_unary");
 }
@@ -292,9 +298,9 @@ int launch_swiglu(void *dst, const void *gate, const void *up, int64_t rows, int
   const int64_t gy = rows < 65535 ? rows : 65535;
   dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy));
   if (vec)
-    swiglu_kernel<T, true><<<grid, kBlock, 0, st>>>(dst, gate, up, rows, cols, gs, us);
+    launch_k(swiglu_kernel<T, true>, dim3(grid), dim3(kBlock), 0, st, dst, gate, up, rows, cols, gs, us);
   else
-    swiglu_kernel<T, false><<<grid, kBlock, 0, st>>>(dst, gate, up, rows, cols, gs, us);
+    launch_k(swiglu_kernel<T, false>, dim3(grid), dim3(kBlock), 0, st, dst, gate, up, rows, cols, gs, us);
   return check_launch("xn_swiglu");
 }
 

@@ -19,6 +19,17 @@
 namespace xn {
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch (sm_90+). Every kernel of the library begins
+// with griddep_wait(), which returns once the previous kernel of the stream
+// has completed and its memory operations are visible (immediately when the
+// launch did not allow early scheduling), then griddep_release(), which lets
+// the next such kernel be scheduled as soon as every block of this one has
+// started. Nothing is read before the wait, so results never depend on it.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_release() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
 // Element traits. `round` maps an f32 value to the nearest T and back to f32:
 // it is the value the reference would hold after one T-typed operation.
 // ---------------------------------------------------------------------------

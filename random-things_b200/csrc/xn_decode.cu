@@ -58,6 +58,8 @@ __device__ __forceinline__ int64_t read_total(int64_t total, const int64_t *tota
 // Scalar form (kVector false): one rotation pair.
 template <typename T, bool kInterleaved, bool kVector>
 __global__ void __launch_bounds__(256) kv_append_rope_kernel(const AppendParams p) {
+  griddep_wait();
+  griddep_release();
   constexpr int V = kVector ? Elem<T>::kVec : 1;
   const int64_t item = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (item >= p.b * p.t * 3 * p.h * p.chunks) return;
@@ -174,6 +176,8 @@ __device__ __forceinline__ float dot_row(const T *row, const float *qs) {
 // loads. kInterleaved picks the RoPE form of the fused prologue.
 template <typename T, int D, bool kFused, bool kInterleaved>
 __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const AttnParams p) {
+  griddep_wait();
+  griddep_release();
   constexpr int V = Elem<T>::kVec;           // elements per 16-byte vector
   constexpr int kVpr = D / V;                // vectors per cached row
   constexpr int kGroups = kAttnThreads / kVpr;  // key groups in the weighted sum
@@ -325,7 +329,9 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
   }
 }
 
-__global__ void position_advance_kernel(int64_t *total_dev, int64_t t) { *total_dev += t; }
+__global__ void position_advance_kernel(int64_t *total_dev, int64_t t) {
+  griddep_wait();
+  griddep_release(); *total_dev += t; }
 
 template <typename T>
 int launch_append(AppendParams p, int interleaved, cudaStream_t st) {
@@ -340,14 +346,14 @@ int launch_append(AppendParams p, int interleaved, cudaStream_t st) {
   if (grid > 0x7fffffffLL) return fail(XN_E_INVALID, "xn_kv_append_rope: too many elements");
   if (vec) {
     if (interleaved)
-      kv_append_rope_kernel<T, true, true><<<grid, 256, 0, st>>>(p);
+      launch_k(kv_append_rope_kernel<T, true, true>, dim3(grid), dim3(256), 0, st, p);
     else
-      kv_append_rope_kernel<T, false, true><<<grid, 256, 0, st>>>(p);
+      launch_k(kv_append_rope_kernel<T, false, true>, dim3(grid), dim3(256), 0, st, p);
   } else {
     if (interleaved)
-      kv_append_rope_kernel<T, true, false><<<grid, 256, 0, st>>>(p);
+      launch_k(kv_append_rope_kernel<T, true, false>, dim3(grid), dim3(256), 0, st, p);
     else
-      kv_append_rope_kernel<T, false, false><<<grid, 256, 0, st>>>(p);
+      launch_k(kv_append_rope_kernel<T, false, false>, dim3(grid), dim3(256), 0, st, p);
   }
   return check_launch("xn_kv_append_rope");
 }
@@ -356,7 +362,7 @@ template <typename T, int D, bool kFused, bool kInterleaved>
 void launch_attn_d(const AttnParams &p, cudaStream_t st) {
   const dim3 grid(static_cast<unsigned>(p.b * p.h), static_cast<unsigned>(p.t));
   const size_t smem = static_cast<size_t>(p.context) * sizeof(float);
-  attention_decode_kernel<T, D, kFused, kInterleaved><<<grid, kAttnThreads, smem, st>>>(p);
+  launch_k(attention_decode_kernel<T, D, kFused, kInterleaved>, dim3(grid), dim3(kAttnThreads), smem, st, p);
 }
 
 template <typename T, bool kFused, bool kInterleaved>
@@ -481,7 +487,7 @@ int xn_position_advance(int64_t *total_dev, int64_t t, void *stream) {
   using namespace xn;
   if (total_dev == nullptr) return fail(XN_E_INVALID, "xn_position_advance: null pointer");
   if (t < 0) return fail(XN_E_INVALID, "xn_position_advance: negative t");
-  position_advance_kernel<<<1, 1, 0, as_stream(stream)>>>(total_dev, t);
+  launch_k(position_advance_kernel, dim3(1), dim3(1), 0, as_stream(stream), total_dev, t);
   return check_launch("xn_position_advance");
 }
 

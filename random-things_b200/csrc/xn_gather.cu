@@ -44,6 +44,8 @@ constexpr int kGatherUnroll = 4;
 
 template <typename U>
 __global__ void __launch_bounds__(256) gather_rows_kernel(const GatherParams p) {
+  griddep_wait();
+  griddep_release();
   const int lane = threadIdx.x & 31;
   const int64_t units_per_chunk = 32 * kGatherUnroll;
   const int64_t chunks = (p.row_units + units_per_chunk - 1) / units_per_chunk;
@@ -94,6 +96,8 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const GatherParams p) 
 // one contiguous run. Each lane looks up the id of the row its unit falls in.
 template <typename U>
 __global__ void __launch_bounds__(256) gather_short_rows_kernel(const GatherParams p, int rpi) {
+  griddep_wait();
+  griddep_release();
   const int lane = threadIdx.x & 31;
   const int ru = static_cast<int>(p.row_units);  // < 32 * kGatherUnroll
   const int span = rpi * ru;
@@ -189,6 +193,8 @@ __device__ __forceinline__ void frame_sum(const RvqParams &p, int64_t code_lane,
 // [batch, frames, dim] output: one warp per frame.
 template <typename T, bool kVector>
 __global__ void __launch_bounds__(256) rvq_btd_kernel(const RvqParams p) {
+  griddep_wait();
+  griddep_release();
   constexpr int N = kVector ? Elem<T>::kVec : 1;
   const int lane = threadIdx.x & 31;
   const int64_t frame = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
@@ -217,6 +223,8 @@ __global__ void __launch_bounds__(256) rvq_btd_kernel(const RvqParams p) {
 // then each warp writes 32 consecutive frames of a channel per store.
 template <typename T, bool kVector>
 __global__ void __launch_bounds__(256) rvq_bct_kernel(const RvqParams p) {
+  griddep_wait();
+  griddep_release();
   constexpr int N = kVector ? Elem<T>::kVec : 1;
   extern __shared__ float tile[];
   const int lane = threadIdx.x & 31;
@@ -250,6 +258,8 @@ __global__ void __launch_bounds__(256) rvq_bct_kernel(const RvqParams p) {
 // Fallback for very wide codebook rows in [batch, dim, frames]: strided stores.
 template <typename T>
 __global__ void __launch_bounds__(256) rvq_bct_wide_kernel(const RvqParams p) {
+  griddep_wait();
+  griddep_release();
   const int lane = threadIdx.x & 31;
   const int64_t frame = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (frame >= p.batch * p.frames) return;
@@ -278,22 +288,22 @@ int launch_rvq(RvqParams p, int out_bct, cudaStream_t st) {
   if (!out_bct) {
     const int64_t grid = ceil_div(frames_total, 8);
     if (vec)
-      rvq_btd_kernel<T, true><<<grid, 256, 0, st>>>(p);
+      launch_k(rvq_btd_kernel<T, true>, dim3(grid), dim3(256), 0, st, p);
     else
-      rvq_btd_kernel<T, false><<<grid, 256, 0, st>>>(p);
+      launch_k(rvq_btd_kernel<T, false>, dim3(grid), dim3(256), 0, st, p);
   } else if (p.dim <= kRvqTileMaxDim) {
     const int64_t grid = p.batch * ((p.frames + 31) / 32);
     const size_t smem = static_cast<size_t>(32) * (p.dim + 1) * sizeof(float);
     if (vec) {
       if (smem > 48 * 1024) cudaFuncSetAttribute(rvq_bct_kernel<T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-      rvq_bct_kernel<T, true><<<grid, 256, smem, st>>>(p);
+      launch_k(rvq_bct_kernel<T, true>, dim3(grid), dim3(256), smem, st, p);
     } else {
       if (smem > 48 * 1024) cudaFuncSetAttribute(rvq_bct_kernel<T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-      rvq_bct_kernel<T, false><<<grid, 256, smem, st>>>(p);
+      launch_k(rvq_bct_kernel<T, false>, dim3(grid), dim3(256), smem, st, p);
     }
   } else {
     p.nvec = static_cast<int>(p.dim);
-    rvq_bct_wide_kernel<T><<<ceil_div(frames_total, 8), 256, 0, st>>>(p);
+    launch_k(rvq_bct_wide_kernel<T>, dim3(ceil_div(frames_total, 8)), dim3(256), 0, st, p);
   }
   return check_launch("xn_rvq_decode_sum");
 }
@@ -329,37 +339,37 @@ int xn_index_select(void *dst, const void *src, const void *ids, int ids_is_i64,
   const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
   if (grid > cap) grid = cap;
   if (vec && rpi > 1) {
-    gather_short_rows_kernel<uint4><<<grid, 256, 0, st>>>(p, rpi);
+    launch_k(gather_short_rows_kernel<uint4>, dim3(grid), dim3(256), 0, st, p, rpi);
   } else if (vec) {
-    gather_rows_kernel<uint4><<<grid, 256, 0, st>>>(p);
+    launch_k(gather_rows_kernel<uint4>, dim3(grid), dim3(256), 0, st, p);
   } else if (rpi > 1) {
     switch (eb) {
       case 1:
-        gather_short_rows_kernel<uint8_t><<<grid, 256, 0, st>>>(p, rpi);
+        launch_k(gather_short_rows_kernel<uint8_t>, dim3(grid), dim3(256), 0, st, p, rpi);
         break;
       case 2:
-        gather_short_rows_kernel<uint16_t><<<grid, 256, 0, st>>>(p, rpi);
+        launch_k(gather_short_rows_kernel<uint16_t>, dim3(grid), dim3(256), 0, st, p, rpi);
         break;
       case 4:
-        gather_short_rows_kernel<uint32_t><<<grid, 256, 0, st>>>(p, rpi);
+        launch_k(gather_short_rows_kernel<uint32_t>, dim3(grid), dim3(256), 0, st, p, rpi);
         break;
       default:
-        gather_short_rows_kernel<unsigned long long><<<grid, 256, 0, st>>>(p, rpi);
+        launch_k(gather_short_rows_kernel<unsigned long long>, dim3(grid), dim3(256), 0, st, p, rpi);
         break;
     }
   } else {
     switch (eb) {
       case 1:
-        gather_rows_kernel<uint8_t><<<grid, 256, 0, st>>>(p);
+        launch_k(gather_rows_kernel<uint8_t>, dim3(grid), dim3(256), 0, st, p);
         break;
       case 2:
-        gather_rows_kernel<uint16_t><<<grid, 256, 0, st>>>(p);
+        launch_k(gather_rows_kernel<uint16_t>, dim3(grid), dim3(256), 0, st, p);
         break;
       case 4:
-        gather_rows_kernel<uint32_t><<<grid, 256, 0, st>>>(p);
+        launch_k(gather_rows_kernel<uint32_t>, dim3(grid), dim3(256), 0, st, p);
         break;
       default:
-        gather_rows_kernel<unsigned long long><<<grid, 256, 0, st>>>(p);
+        launch_k(gather_rows_kernel<unsigned long long>, dim3(grid), dim3(256), 0, st, p);
         break;
     }
   }

@@ -43,6 +43,31 @@ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 // Number of SMs of the current device (cached per device).
 int sm_count();
 
+// True unless the environment sets XN_PDL=0 (read once per process).
+bool pdl_enabled();
+
+// Launches `kernel` on `stream` with programmatic dependent launch allowed
+// (cudaLaunchAttributeProgrammaticStreamSerialization): the kernel's blocks
+// may be scheduled while the previous kernel of the stream drains. Every
+// kernel of this library starts with griddep_wait() (xn_common.cuh), which
+// holds it until that previous kernel has completed and its writes are
+// visible, so results do not depend on the attribute. Errors are left for
+// check_launch().
+template <typename... KArgs, typename... Args>
+void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, kernel, static_cast<Args &&>(args)...);
+}
+
 }  // namespace xn
 
 // Dispatches a float dtype to a template parameter named T.

@@ -46,6 +46,8 @@ struct NormParams {
 // is the vector kernel's, one element at a time.
 template <typename T, int NV, bool kLN, int kMaxBlock, bool kBranch>
 __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : 1) norm_rows_kernel(const NormParams p) {
+  griddep_wait();
+  griddep_release();
   __shared__ float red[32];
   const int tpr = p.tpr;
   const int g = threadIdx.x / tpr;
@@ -139,6 +141,8 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : 1) norm_rows
 template <typename T, int NV, bool kLN, int kMaxBlock, bool kBranch>
 __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : (kMaxBlock == 512 ? 2 : 1))
     norm_vec_kernel(const NormParams p) {
+  griddep_wait();
+  griddep_release();
   using P = Pairs<T>;
   constexpr int KP = P::kP;
   constexpr int N = Elem<T>::kVec;
@@ -302,6 +306,8 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : (kMaxBlock =
 // Rows wider than the register budget: one block per row, several passes.
 template <typename T, bool kLN>
 __global__ void __launch_bounds__(1024) norm_loop_kernel(const NormParams p) {
+  griddep_wait();
+  griddep_release();
   __shared__ float red[32];
   const int tpr = blockDim.x;
   const int64_t base = static_cast<int64_t>(blockIdx.x) * p.cols;
@@ -362,9 +368,9 @@ constexpr int kMaxNv = (kBranch || kMaxBlock > 512) ? 4 : 8;
 template <typename T, bool kVector, int NV, bool kLN, int kMaxBlock, bool kBranch>
 void launch_nv(const NormParams &p, int block, int64_t grid, cudaStream_t st) {
   if constexpr (kVector) {
-    norm_vec_kernel<T, NV, kLN, kMaxBlock, kBranch><<<grid, block, 0, st>>>(p);
+    launch_k(norm_vec_kernel<T, NV, kLN, kMaxBlock, kBranch>, dim3(grid), dim3(block), 0, st, p);
   } else {
-    norm_rows_kernel<T, NV, kLN, kMaxBlock, kBranch><<<grid, block, 0, st>>>(p);
+    launch_k(norm_rows_kernel<T, NV, kLN, kMaxBlock, kBranch>, dim3(grid), dim3(block), 0, st, p);
   }
 }
 
@@ -461,7 +467,7 @@ int launch_norm(NormParams p, cudaStream_t st, const char *op) {
     if (!launched) return fail(XN_E_INVALID, "%s: internal error, no kernel for %d accesses per thread", op, nv);
   } else {
     if (p.rows > 0x7fffffffLL) return fail(XN_E_INVALID, "%s: too many rows (%lld)", op, (long long)p.rows);
-    norm_loop_kernel<T, kLN><<<static_cast<unsigned>(p.rows), 1024, 0, st>>>(p);
+    launch_k(norm_loop_kernel<T, kLN>, dim3(static_cast<unsigned>(p.rows)), dim3(1024), 0, st, p);
   }
   return check_launch(op);
 }

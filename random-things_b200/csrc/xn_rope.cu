@@ -45,6 +45,8 @@ constexpr int kMaxHpt = 4;  // heads per thread (cos/sin reuse, loads in flight)
 
 template <typename T, bool kInterleaved, bool kVector>
 __global__ void __launch_bounds__(256) rope_kernel(const RopeParams p) {
+  griddep_wait();
+  griddep_release();
   constexpr int V = Elem<T>::kVec;
   uint32_t item = blockIdx.x * blockDim.x + threadIdx.x;
   int which = 0;
@@ -227,14 +229,14 @@ int launch_rope(const RopeJob &job, const void *cos, const void *sin, int64_t b,
     const unsigned grid = static_cast<unsigned>(ceil_div(total, 256));
     if (interleaved) {
       if (vec)
-        rope_kernel<T, true, true><<<grid, 256, 0, st>>>(p);
+        launch_k(rope_kernel<T, true, true>, dim3(grid), dim3(256), 0, st, p);
       else
-        rope_kernel<T, true, false><<<grid, 256, 0, st>>>(p);
+        launch_k(rope_kernel<T, true, false>, dim3(grid), dim3(256), 0, st, p);
     } else {
       if (vec)
-        rope_kernel<T, false, true><<<grid, 256, 0, st>>>(p);
+        launch_k(rope_kernel<T, false, true>, dim3(grid), dim3(256), 0, st, p);
       else
-        rope_kernel<T, false, false><<<grid, 256, 0, st>>>(p);
+        launch_k(rope_kernel<T, false, false>, dim3(grid), dim3(256), 0, st, p);
     }
     const int rc = check_launch(op);
     if (rc != XN_OK) return rc;

@@ -77,6 +77,8 @@ struct Pair<__half> {
 // offset + (row % t1) as -inf: they are neither read nor exp'd and give 0.
 template <typename T, int NV, bool kCausal>
 __global__ void __launch_bounds__(512) softmax_rows_kernel(const SoftmaxParams p) {
+  griddep_wait();
+  griddep_release();
   __shared__ float red[32];
   const int tpr = p.tpr;
   const int g = threadIdx.x / tpr;
@@ -133,6 +135,8 @@ __global__ void __launch_bounds__(512) softmax_rows_kernel(const SoftmaxParams p
 // whose row groups span several warps keep their __syncthreads uniform.
 template <typename T, int NV, bool kCausal>
 __global__ void __launch_bounds__(512, NV >= 8 ? 1 : 2) softmax_pipe_kernel(const SoftmaxParams p) {
+  griddep_wait();
+  griddep_release();
   constexpr int N = Elem<T>::kVec;
   // One scratch array per reduction of a row (see group_sum's kReuse).
   __shared__ float red_max[32], red_sum[32];
@@ -296,6 +300,8 @@ __global__ void __launch_bounds__(512, NV >= 8 ? 1 : 2) softmax_pipe_kernel(cons
 // second pass writes T(exp(...)) to dst and the third rescales it in place.
 template <typename T>
 __global__ void __launch_bounds__(1024) softmax_loop_kernel(const SoftmaxParams p) {
+  griddep_wait();
+  griddep_release();
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   const int64_t base = row * p.cols;
@@ -340,22 +346,22 @@ bool launch_softmax_pipe(const SoftmaxParams &p, int nv, int block, int64_t grid
   switch (nv) {
     case 1: {
       auto k = softmax_pipe_kernel<T, 1, kCausal>;
-      k<<<persistent_grid(k, block, grid), block, 0, st>>>(p);
+      launch_k(k, dim3(persistent_grid(k, block, grid)), dim3(block), 0, st, p);
       return true;
     }
     case 2: {
       auto k = softmax_pipe_kernel<T, 2, kCausal>;
-      k<<<persistent_grid(k, block, grid), block, 0, st>>>(p);
+      launch_k(k, dim3(persistent_grid(k, block, grid)), dim3(block), 0, st, p);
       return true;
     }
     case 4: {
       auto k = softmax_pipe_kernel<T, 4, kCausal>;
-      k<<<persistent_grid(k, block, grid), block, 0, st>>>(p);
+      launch_k(k, dim3(persistent_grid(k, block, grid)), dim3(block), 0, st, p);
       return true;
     }
     case 8: {
       auto k = softmax_pipe_kernel<T, 8, kCausal>;
-      k<<<persistent_grid(k, block, grid), block, 0, st>>>(p);
+      launch_k(k, dim3(persistent_grid(k, block, grid)), dim3(block), 0, st, p);
       return true;
     }
     default:
@@ -371,16 +377,16 @@ bool launch_softmax_regs_c(const SoftmaxParams &p, int nv, int block, int64_t gr
   } else {
     switch (nv) {
       case 1:
-        softmax_rows_kernel<T, 1, kCausal><<<grid, block, 0, st>>>(p);
+        launch_k(softmax_rows_kernel<T, 1, kCausal>, dim3(grid), dim3(block), 0, st, p);
         return true;
       case 2:
-        softmax_rows_kernel<T, 2, kCausal><<<grid, block, 0, st>>>(p);
+        launch_k(softmax_rows_kernel<T, 2, kCausal>, dim3(grid), dim3(block), 0, st, p);
         return true;
       case 4:
-        softmax_rows_kernel<T, 4, kCausal><<<grid, block, 0, st>>>(p);
+        launch_k(softmax_rows_kernel<T, 4, kCausal>, dim3(grid), dim3(block), 0, st, p);
         return true;
       case 8:
-        softmax_rows_kernel<T, 8, kCausal><<<grid, block, 0, st>>>(p);
+        launch_k(softmax_rows_kernel<T, 8, kCausal>, dim3(grid), dim3(block), 0, st, p);
         return true;
       default:
         return false;
@@ -422,7 +428,7 @@ int launch_softmax(SoftmaxParams p, cudaStream_t st) {
     if (!launched) return fail(XN_E_INVALID, "xn_softmax: internal error, no kernel for %d accesses per thread", nv);
   } else {
     if (p.rows > 0x7fffffffLL) return fail(XN_E_INVALID, "xn_softmax: too many rows");
-    softmax_loop_kernel<T><<<static_cast<unsigned>(p.rows), 1024, 0, st>>>(p);
+    launch_k(softmax_loop_kernel<T>, dim3(static_cast<unsigned>(p.rows)), dim3(1024), 0, st, p);
   }
   return check_launch("xn_softmax");
 }
@@ -431,6 +437,8 @@ int launch_softmax(SoftmaxParams p, cudaStream_t st) {
 template <typename T>
 __global__ void __launch_bounds__(256) causal_mask_kernel(void *dst, int64_t rows, int64_t t1,
                                                           int64_t t2, int64_t offset) {
+  griddep_wait();
+  griddep_release();
   const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (row >= rows) return;
   const int64_t first = offset + (row % t1) + 1;
@@ -485,7 +493,7 @@ int xn_causality_mask(void *dst, int64_t bh, int64_t t1, int64_t t2, int64_t off
   if (dst == nullptr) return fail(XN_E_INVALID, "xn_causality_mask: null dst");
   const int64_t grid = ceil_div(rows, 8);
   if (grid > 0x7fffffffLL) return fail(XN_E_INVALID, "xn_causality_mask: too many rows");
-  XN_DISPATCH_FLOAT(dtype, causal_mask_kernel<T><<<grid, 256, 0, as_stream(stream)>>>(dst, rows, t1, t2, offset);
+  XN_DISPATCH_FLOAT(dtype, launch_k(causal_mask_kernel<T>, dim3(grid), dim3(256), 0, as_stream(stream), dst, rows, t1, t2, offset);
                     return check_launch("xn_causality_mask"));
   return fail(XN_E_DTYPE, "xn_causality_mask: unsupported dtype %d", dtype);
 }

@@ -137,3 +137,23 @@ def test_error_messages_are_per_thread(xn):
         t.join()
     assert seen["norm"] == {(xn.XN_E_INVALID, "xn_rms_norm")}
     assert seen["rope"] == {(xn.XN_E_RANGE, "xn_rope")}
+
+
+def test_every_kernel_waits_for_its_predecessor_first():
+    """Launches allow programmatic dependent launch, so a kernel may start
+    while the previous kernel of the stream drains. Every kernel must
+    therefore begin with griddep_wait() (nothing read before it), and every
+    launch must go through launch_k (no bare <<<...>>> launches)."""
+    import re
+    from pathlib import Path
+
+    csrc = Path(__file__).resolve().parents[1] / "random-things_b200" / "csrc"
+    n_kernels = 0
+    for f in sorted(csrc.glob("*.cu")):
+        src = f.read_text()
+        assert "<<<" not in src, f"{f.name}: bare <<<>>> launch"
+        for m in re.finditer(r"__global__", src):
+            body = src[src.index("{", m.end()) + 1:].lstrip()
+            assert body.startswith("griddep_wait();"), f"{f.name}: kernel at offset {m.start()} does not wait first"
+            n_kernels += 1
+    assert n_kernels >= 19
