@@ -60,6 +60,18 @@ def test_swiglu_packed_projection(oracle, xn, cuda, dtype, rows, inter):
     assert_close(from_device(Y, dtype), ref, dtype, "swiglu packed")
 
 
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_swiglu_strided_past_the_grid_row_limit(oracle, xn, cuda, dtype):
+    """A strided (packed-projection) SwiGLU over 70000 rows: the launch grid
+    covers at most 65535 rows and the kernel loops over the rest."""
+    rows, inter = 70000, 24
+    r = rng(70000)
+    gu = to_storage(randn(r, (rows, 2 * inter), 2.0), dtype)
+    ref = oracle.swiglu(np.ascontiguousarray(gu[:, :inter]), np.ascontiguousarray(gu[:, inter:]), dtype)
+    GU = to_device(gu, dtype, cuda)
+    assert_close(from_device(xn.swiglu(GU[:, :inter], GU[:, inter:]), dtype), ref, dtype, "swiglu 70000 rows")
+
+
 def test_config_shapes(oracle, xn, cuda):
     """Config 1 SwiGLU [1,512,5632] f32; config 2 GELU [4,250,2048] f32 and bf16;
     config 3 SiLU [16,4096] bf16."""
