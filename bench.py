@@ -348,6 +348,47 @@ def mimi_rate(torch, device, steps: int, batch: int = 4, frames: int = 250) -> d
                     "fused ops; GEMMs on cuBLAS), one CUDA graph; seeded synthetic weights"}
 
 
+def gather_context(torch, xn, device, reps: int = 7) -> list:
+    """The config-4 embedding gather (32768 ids into the 128256 x 4096 table)
+    timed alone after different predecessors: a write flush or the step's
+    SwiGLU (both leave ~126 MB of dirty lines in L2, written back during the
+    gather) and the same followed by a clean 256 MB read (L2 left clean).
+    Shows how much of the gather's in-step time is its predecessor's
+    write-back."""
+    g = torch.Generator(device=device).manual_seed(0)
+    table = (torch.randn((CFG["vocab"], CFG["hidden"]), device=device, generator=g) * 0.02).to(torch.bfloat16)
+    rows = CFG["batch"] * CFG["seq"]
+    ids = torch.randint(0, CFG["vocab"], (rows,), dtype=torch.int32, device=device, generator=g)
+    out = torch.empty((rows, CFG["hidden"]), dtype=torch.bfloat16, device=device)
+    gate = torch.randn((rows, CFG["inter"]), device=device, generator=g).to(torch.bfloat16)
+    up = torch.randn((rows, CFG["inter"]), device=device, generator=g).to(torch.bfloat16)
+    act = torch.empty_like(gate)
+    wflush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=device)
+    rflush = torch.zeros(64 * 1024 * 1024, dtype=torch.float32, device=device)
+    nbytes = rows * 4 + 2 * rows * CFG["hidden"] * 2
+    peak, _ = measured_peak()
+
+    def timed(pre):
+        ts = []
+        for _ in range(reps):
+            pre()
+            torch.cuda._sleep(1_000_000)  # host enqueues the events and the op while the GPU is busy
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            xn.index_select(table, ids, 0, out=out)
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        ms = statistics.median(ts)
+        return {"ms": round(ms, 4), "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                "frac": round(nbytes / (ms * 1e-3) / 1e9 / peak, 3)}
+
+    return [dict(after="write flush (256 MB)", **timed(lambda: wflush.zero_())),
+            dict(after="write flush + clean read", **timed(lambda: (wflush.zero_(), rflush.sum()))),
+            dict(after="swiglu (the step's last op)", **timed(lambda: xn.swiglu_(act, gate, up))),
+            dict(after="swiglu + clean read", **timed(lambda: (xn.swiglu_(act, gate, up), rflush.sum())))]
+
+
 DECODE_CFG = dict(d_model=1024, num_heads=16, num_layers=6, dim_feedforward=4096)
 
 
@@ -687,6 +728,8 @@ def main() -> int:
     ap.add_argument("--decode-only", action="store_true",
                     help="run only the config-3 streaming-decode measurement")
     ap.add_argument("--decode-acts", default="silu,gelu_erf", help="MLP activations for --decode-only")
+    ap.add_argument("--gather-context", action="store_true",
+                    help="time the config-4 gather after dirty-L2 and clean-L2 predecessors")
     ap.add_argument("--rows", type=int, default=CFG["batch"] * CFG["seq"],
                     help="token rows per GPU (a multiple of 4096; smaller values for profiling captures)")
     ap.add_argument("--ops", default=",".join(OPS), help="comma-separated subset of " + ",".join(OPS))
@@ -723,6 +766,11 @@ def main() -> int:
             if "gbs" in pt:
                 pt["frac"] = round(pt["gbs"] / peak, 3)
             print(json.dumps(pt), flush=True)
+        return 0
+    if args.gather_context:
+        xn.lib()
+        for pt in gather_context(torch, xn, dev):
+            print(json.dumps({"op": "embedding_gather", **pt}), flush=True)
         return 0
     if args.decode_only:
         xn.lib()
