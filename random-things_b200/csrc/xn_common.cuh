@@ -451,9 +451,14 @@ __device__ __forceinline__ float group_max(float v, int tpr, float *red) {
 // no overflow is possible where it is used: |x/d| stays far inside the f32
 // range). d > 0, so the quotient has the sign of x (and of q0): copysign keeps
 // -0 / d == -0, which the correction step alone would turn into +0.
+// d = +inf (an RMSNorm row whose sum of squares overflowed) gives r = 0, and
+// -d * q0 would be -inf * 0 = NaN; with 0 in its place the steps return
+// q0 = x * 0 = +-0 for finite x and NaN for x = +-inf, the IEEE quotients.
+__device__ __forceinline__ float neg_divisor(float d) { return isinf(d) ? 0.f : -d; }
+
 __device__ __forceinline__ float div_by(float x, float d, float r) {
   const float q0 = __fmul_rn(x, r);
-  const float rem = __fmaf_rn(-d, q0, x);
+  const float rem = __fmaf_rn(neg_divisor(d), q0, x);
   return copysignf(__fmaf_rn(rem, r, q0), q0);
 }
 

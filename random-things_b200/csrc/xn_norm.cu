@@ -274,7 +274,7 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : (kMaxBlock =
     const float s = group_sum<false>(__fadd_rn(s2.x, s2.y), tpr, red_a);
     const float m = __fsqrt_rn(__fadd_rn(__fdiv_rn(s, cols_f), p.eps));
     const float r = __frcp_rn(m);
-    const float2 nm2 = splat2(-m), r2 = splat2(r);
+    const float2 nm2 = splat2(neg_divisor(m)), r2 = splat2(r);  // m = inf: see neg_divisor
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
       const int vi = lr + k * tpr;

@@ -1,0 +1,62 @@
+"""Non-finite and extreme inputs through the fused ops, against the oracle:
+rows holding +-inf or NaN, and bf16 rows whose values are finite but large
+enough that the f32 sum of squares overflows (RMSNorm's divisor becomes inf,
+so the reference's x / m is +-0). The results must follow the reference's
+IEEE arithmetic element for element: the same non-finite pattern, and the
+same values elsewhere within the usual tolerance."""
+import numpy as np
+import pytest
+
+from helpers import assert_close, from_device, randn, rng, storage_to_f32, to_device, to_storage
+
+pytestmark = pytest.mark.gpu
+
+
+def _rows(dtype, cols):
+    r = rng(cols)
+    x = randn(r, (8, cols))
+    x[1, 3] = np.inf
+    x[2, 5] = -np.inf
+    x[3, 7] = np.nan
+    x[4, :] = 3.0e19  # finite; squares overflow f32 (sum of squares = inf)
+    x[4, ::3] = -2.0e20
+    x[5, :] = 0.0
+    x[6, 0] = 1.0e30
+    return to_storage(x, dtype)
+
+
+def _same_nonfinite(got, ref, dtype):
+    g, r = storage_to_f32(got, dtype), storage_to_f32(ref, dtype)
+    assert np.array_equal(np.isnan(g), np.isnan(r)), "NaN pattern differs"
+    assert np.array_equal(np.isinf(g), np.isinf(r)), "inf pattern differs"
+    assert np.array_equal(g[np.isinf(g)], r[np.isinf(r)]), "inf signs differ"
+    fin = np.isfinite(r)
+    return got[fin], ref[fin]
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16", "f16"])
+@pytest.mark.parametrize("cols", [37, 64, 1000])
+def test_norms_and_softmax_special_values(oracle, xn, cuda, dtype, cols):
+    x = _rows(dtype, cols)
+    w = to_storage(randn(rng(1), cols, 0.02, 1.0), dtype)
+    b = to_storage(randn(rng(2), cols, 0.1), dtype)
+    X, W, B = (to_device(a, dtype, cuda) for a in (x, w, b))
+    for got, ref, what in [
+        (xn.rms_norm(X, W, 1e-5), oracle.rms_norm(x, w, 1e-5, dtype), "rms_norm"),
+        (xn.layer_norm(X, W, B, 1e-5), oracle.layer_norm(x, w, b, 1e-5, dtype), "layer_norm"),
+        (xn.softmax(X), oracle.softmax(x, dtype), "softmax"),
+    ]:
+        g, r = _same_nonfinite(from_device(got, dtype), ref, dtype)
+        if g.size:
+            assert_close(g, r, dtype, f"{what} finite part")
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_activations_special_values(oracle, xn, cuda, dtype):
+    x = to_storage(np.array([np.inf, -np.inf, np.nan, 0.0, -0.0, 88.0, -88.0, 1e30, -1e30], np.float32), dtype)
+    X = to_device(x, dtype, cuda)
+    for op in ("silu", "gelu_erf"):
+        g, r = _same_nonfinite(from_device(getattr(xn, op)(X), dtype), oracle.unary(x, op, dtype), dtype)
+        assert np.array_equal(g, r) or dtype == "f32", f"{op}"
+        if dtype == "f32":
+            assert_close(g, r, dtype, op)
