@@ -412,11 +412,11 @@ int launch_softmax(SoftmaxParams p, cudaStream_t st) {
   if (nvec <= 512LL * nv_cap) {
     int64_t tpr = pow2_ceil(ceil_div(nvec, 4));
     if (tpr > 512) tpr = 512;
-    // 16-bit rows of more than 128 vectors (1024 elements): 8 vectors per
-    // thread (the 128-register shape), so rows of up to 2048 elements sit in
-    // one warp and longer ones span half as many warps, with fewer block
-    // barriers per row.
-    if (vec && n == 8 && nvec > 128) tpr = pow2_ceil(ceil_div(nvec, 8));
+    // Rows of more than 128 vectors (1024 16-bit or 512 f32 elements): 8
+    // vectors per thread (the 128-register shape), so rows of up to 256
+    // vectors sit in one warp and longer ones span half as many warps, with
+    // fewer block barriers per row.
+    if (vec && nvec > 128) tpr = pow2_ceil(ceil_div(nvec, 8));
     const int nv = static_cast<int>(pow2_ceil(ceil_div(nvec, tpr)));
     const int block = tpr < 256 ? 256 : static_cast<int>(tpr);
     const int64_t grid = ceil_div(p.rows, block / tpr);
