@@ -473,11 +473,26 @@ __device__ __forceinline__ float div_by(float x, float d, float r) {
 // through both softmax paths against glibc and find none. Not used for f32 or
 // f16, whose finer output grids would expose the error, nor for positive
 // arguments (SiLU's exp(-s)), which were not proven.
-__device__ __forceinline__ float exp_of_bf16(float x) {
+constexpr float kLog2e = 0x1.715476p+0f;
+
+// 2^t by the hardware approximation, subnormal results kept.
+__device__ __forceinline__ float ex2_approx(float t) {
   float y;
-  asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(__fmul_rn(x, 0x1.715476p+0f)));
+  asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(t));
   return y;
 }
+
+// The same approximation with subnormal results flushed to zero, which saves
+// the instructions that keep them. For t >= -126 (normal results) it returns
+// the value of ex2_approx: the softmax tests run every bf16 argument that
+// takes this path through it against glibc.
+__device__ __forceinline__ float ex2_approx_ftz(float t) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(t));
+  return y;
+}
+
+__device__ __forceinline__ float exp_of_bf16(float x) { return ex2_approx(__fmul_rn(x, kLog2e)); }
 
 // exp of a non-positive argument as the T-typed reference computes it, before
 // the rounding to T.
@@ -488,6 +503,31 @@ __device__ __forceinline__ float exp_t(float x) {
   } else {
     return expf(x);
   }
+}
+
+// c + widen(w's low half), c + widen(w's high half) for a packed 16-bit pair
+// w, each rounded once to f32: sm_100's mixed-precision add, which takes the
+// 16-bit operand as it is, so the pair needs no unpacking. The same values as
+// __fadd2_rn(c, widened w).
+template <typename T>
+__device__ __forceinline__ float2 add2_widen(uint32_t w, float2 c);
+
+template <>
+__device__ __forceinline__ float2 add2_widen<__nv_bfloat16>(uint32_t w, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\tadd.rn.f32.bf16 %0, lo, %3;\n\tadd.rn.f32.bf16 %1, hi, %4;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "r"(w), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+template <>
+__device__ __forceinline__ float2 add2_widen<__half>(uint32_t w, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\tadd.rn.f32.f16 %0, lo, %3;\n\tadd.rn.f32.f16 %1, hi, %4;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "r"(w), "f"(c.x), "f"(c.y));
+  return d;
 }
 
 // div_by on an element pair, for dividends that are never -0 (exp results):
@@ -517,6 +557,66 @@ __device__ __forceinline__ float div_for_bf16(float s, float d) {
 
 __host__ __device__ __forceinline__ bool aligned16(const void *p) {
   return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+// ---------------------------------------------------------------------------
+// Bulk copies from global into this block's shared memory: cp.async.bulk, the
+// untiled form of the TMA engine, completing on an mbarrier of the block.
+// Both addresses 16-byte aligned, size a multiple of 16 bytes.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+// Makes the initialised barriers visible to the copy engine; a block barrier
+// must follow before other threads use them.
+__device__ __forceinline__ void mbar_init_fence() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+// Orders shared-memory accesses made (or synchronised with) before it ahead of
+// bulk copies issued after it: a buffer whose reads the block has finished is
+// then safe to refill.
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// L2 policy for data read once: its lines are the first to go.
+__device__ __forceinline__ uint64_t l2_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// Arms `bar` (one arrival, `bytes` of transactions) and starts the copy of
+// `bytes` from global `src` to shared `dst`; the barrier's phase completes
+// when the bytes have landed.
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
+                                          uint64_t policy) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// Waits until the phase of `bar` with the given parity has completed. Gives up
+// after `limit` polls (each poll may suspend the thread for a short,
+// hardware-chosen time) and returns false, so a copy that never completes
+// cannot hang the kernel.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t limit) {
+  const uint32_t a = smem_u32(bar);
+  for (uint32_t i = 0; i < limit; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
 }
 
 }  // namespace xn

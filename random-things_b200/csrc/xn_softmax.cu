@@ -11,7 +11,10 @@
 //
 // Design: like the norm kernels, a row group of tpr threads holds the whole row
 // in registers (one HBM read, one HBM write per element); max and sum are
-// group reductions. Rows wider than 16384 elements use a three-pass kernel.
+// group reductions. Narrower rows prefetch the next row into registers; wide
+// rows (up to 64 KB) are streamed into shared memory by bulk copies instead.
+// Rows wider than that, or wider than 16384 elements in the scalar path, use
+// a three-pass kernel.
 #include <math.h>
 
 #include <type_traits>
@@ -56,6 +59,8 @@ struct Pair<__nv_bfloat16> {
   __device__ __forceinline__ static T2 mask_high(T2 v) {
     return __halves2bfloat162(__low2bfloat16(v), __float2bfloat16(-INFINITY));
   }
+  // Both halves set to the low element.
+  __device__ __forceinline__ static T2 low2(T2 v) { return __low2bfloat162(v); }
 };
 template <>
 struct Pair<__half> {
@@ -67,6 +72,7 @@ struct Pair<__half> {
   __device__ __forceinline__ static T2 mask_high(T2 v) {
     return __halves2half2(__low2half(v), __float2half(-INFINITY));
   }
+  __device__ __forceinline__ static T2 low2(T2 v) { return __low2half2(v); }
 };
 
 // Scalar rows (widths that are not a multiple of the 16-byte vector, or
@@ -125,13 +131,187 @@ __global__ void __launch_bounds__(512) softmax_rows_kernel(const SoftmaxParams p
   }
 }
 
+// Per-thread steps of one vector row, shared by the register-prefetching and
+// the shared-memory-staged kernels. `cur` holds the thread's NV vectors of the
+// row: vector k starts at element (lr + k * tpr) * N. Vectors starting at or
+// past `lim` need not hold data: the first step overwrites them.
+//
+// For 16-bit T the row stays packed: the max, the subtraction and the scale
+// run as paired bf16x2 / f16x2 instructions, which round exactly once as the
+// reference's T operations do.
+
+// [x = T(x * scale)] on the live elements, -inf at and past `lim`, in place;
+// returns the thread's maximum. For 16-bit T, `mn` receives the minimum of the
+// thread's live elements (+inf when it has none), which tells softmax_exp
+// whether any of its exp results can be subnormal.
+template <typename T, int NV>
+__device__ __forceinline__ float softmax_prep(uint4 (&cur)[NV], int lr, int tpr, int lim, const SoftmaxParams &p,
+                                              float &mn) {
+  constexpr int N = Elem<T>::kVec;
+  if constexpr (std::is_same_v<T, float>) {
+    mn = -INFINITY;  // not used for f32
+    float m = -INFINITY;
+    const float2 sc = splat2(p.scale);
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int e0 = (lr + k * tpr) * N;
+      float2 *x2 = reinterpret_cast<float2 *>(&cur[k]);
+      float *x = reinterpret_cast<float *>(&cur[k]);
+      if (e0 + N <= lim) {
+        if (p.scaled) {
+          x2[0] = __fmul2_rn(x2[0], sc);
+          x2[1] = __fmul2_rn(x2[1], sc);
+        }
+      } else {  // the vector holding the row end, or padding: -inf past it
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+          if (e0 + j < lim) {
+            if (p.scaled) x[j] = __fmul_rn(x[j], p.scale);
+          } else {
+            x[j] = -INFINITY;
+          }
+        }
+      }
+      m = fmaxf(m, fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3])));
+    }
+    return m;
+  } else {
+    using P = Pair<T>;
+    using T2 = typename P::T2;
+    constexpr int W = N / 2;
+    T2 mx2 = P::neg_inf(), mn2 = P::splat(INFINITY);
+    const T2 sc2 = P::splat(p.scale);
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int e0 = (lr + k * tpr) * N;
+      T2 *w = reinterpret_cast<T2 *>(&cur[k]);
+      if (e0 + N <= lim) {
+#pragma unroll
+        for (int j = 0; j < W; ++j) {
+          if (p.scaled) w[j] = __hmul2(w[j], sc2);
+          mn2 = __hmin2(mn2, w[j]);
+        }
+      } else {  // the vector holding the row end, or padding: -inf past it
+#pragma unroll
+        for (int j = 0; j < W; ++j) {
+          if (e0 + 2 * j + 1 < lim) {
+            if (p.scaled) w[j] = __hmul2(w[j], sc2);
+            mn2 = __hmin2(mn2, w[j]);
+          } else if (e0 + 2 * j < lim) {
+            if (p.scaled) w[j] = __hmul2(w[j], sc2);
+            mn2 = __hmin2(mn2, P::low2(w[j]));
+            w[j] = P::mask_high(w[j]);
+          } else {
+            w[j] = P::neg_inf();
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < W; ++j) mx2 = __hmax2(mx2, w[j]);
+    }
+    const float2 nf = P::to_f2(mn2);
+    mn = fminf(nf.x, nf.y);
+    const float2 mf = P::to_f2(mx2);
+    return fmaxf(mf.x, mf.y);
+  }
+}
+
+// e = T(exp(T(x - mx))) in place (exp(-inf) = 0 for masked and padding
+// entries); returns the thread's f32 sum of e, kept as two interleaved partial
+// sums. mx is the row maximum, a T value; mn is softmax_prep's minimum.
+//
+// bf16: exp(d) = 2^(d log2 e) (exp_of_bf16). When mn - mx >= -86, every
+// d = T(x - mx) of the thread is >= -86 (rounding is monotonic, and the f32
+// difference is within half an f32 ulp of the exact one, which bf16's 0.5
+// spacing at 86 absorbs), so 2^(d log2 e) >= 2^-124.1 is normal and the
+// flush-to-zero form gives the same values with fewer instructions. Otherwise
+// (a row reaching below -86 relative to its max, an infinite input, a NaN)
+// the thread takes the form that keeps subnormals.
+template <typename T, int NV>
+__device__ __forceinline__ float softmax_exp(uint4 (&cur)[NV], float mx, float mn) {
+  float2 s2 = make_float2(0.f, 0.f);
+  if constexpr (std::is_same_v<T, float>) {
+    const float2 nmx = splat2(-mx);
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      float2 *x2 = reinterpret_cast<float2 *>(&cur[k]);
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const float2 d = __fadd2_rn(x2[j], nmx);
+        x2[j] = make_float2(expf(d.x), expf(d.y));
+        s2 = __fadd2_rn(s2, x2[j]);
+      }
+    }
+  } else {
+    using P = Pair<T>;
+    using T2 = typename P::T2;
+    const T2 m2 = P::splat(mx);  // exact: the max is a T value
+    // T(exp(...)) of one T(x - max) pair, by the form `kind` selects.
+    auto exp_pair = [](float2 d, auto kind) -> T2 {
+      if constexpr (std::is_same_v<T, __nv_bfloat16>) {
+        const float2 t = __fmul2_rn(d, splat2(kLog2e));
+        if constexpr (decltype(kind)::value)
+          return P::from_f2(ex2_approx_ftz(t.x), ex2_approx_ftz(t.y));
+        else
+          return P::from_f2(ex2_approx(t.x), ex2_approx(t.y));
+      } else {
+        return P::from_f2(expf(d.x), expf(d.y));
+      }
+    };
+    auto run = [&](auto kind) {
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        T2 *w = reinterpret_cast<T2 *>(&cur[k]);
+#pragma unroll
+        for (int j = 0; j < Elem<T>::kVec / 2; ++j) {
+          const T2 e = exp_pair(P::to_f2(__hsub2(w[j], m2)), kind);  // T(exp(T(x - max)))
+          s2 = add2_widen<T>(*reinterpret_cast<const uint32_t *>(&e), s2);
+          w[j] = e;
+        }
+      }
+    };
+    if (std::is_same_v<T, __nv_bfloat16> && __fsub_rn(mn, mx) >= -86.f)
+      run(std::true_type{});
+    else
+      run(std::false_type{});
+  }
+  return __fadd_rn(s2.x, s2.y);
+}
+
+// y = T(e / s) for the vectors below nvec, stored to the row at dst_row.
+// s >= 1 for a live row: its maximum contributes exp(0).
+template <typename T, int NV>
+__device__ __forceinline__ void softmax_store(uint4 (&cur)[NV], float s, T *dst_row, int lr, int tpr, int nvec) {
+  constexpr int N = Elem<T>::kVec;
+  const float2 rs = splat2(__frcp_rn(s)), ns = splat2(-s);
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int vi = lr + k * tpr;
+    if (vi < nvec) {
+      if constexpr (std::is_same_v<T, float>) {
+        float2 *x2 = reinterpret_cast<float2 *>(&cur[k]);
+        x2[0] = div_nonneg2(x2[0], ns, rs);
+        x2[1] = div_nonneg2(x2[1], ns, rs);
+      } else {
+        using P = Pair<T>;
+        using T2 = typename P::T2;
+        T2 *w = reinterpret_cast<T2 *>(&cur[k]);
+#pragma unroll
+        for (int j = 0; j < N / 2; ++j) {
+          const float2 q = div_nonneg2(P::to_f2(w[j]), ns, rs);
+          w[j] = P::from_f2(q.x, q.y);
+        }
+      }
+      st_vec(dst_row + vi * N, cur[k]);
+    }
+  }
+}
+
 // Vector rows, persistent and prefetching: each row group walks rows
 // row, row + step, ... (step = all groups of the grid) and issues the loads of
 // its next row before computing the current one, so HBM reads stay in flight
 // through the reductions and the exp / divide work. Arithmetic as
-// softmax_rows_kernel; for 16-bit T the row stays packed and the max, the
-// subtraction and the scale run as paired bf16x2 / f16x2 instructions, which
-// round exactly once as the reference's T operations do. The loop bound depends only on the block, so blocks
+// softmax_rows_kernel. The loop bound depends only on the block, so blocks
 // whose row groups span several warps keep their __syncthreads uniform.
 template <typename T, int NV, bool kCausal>
 __global__ void __launch_bounds__(512, NV >= 8 ? 1 : 2) softmax_pipe_kernel(const SoftmaxParams p) {
@@ -181,118 +361,140 @@ __global__ void __launch_bounds__(512, NV >= 8 ? 1 : 2) softmax_pipe_kernel(cons
     if (qn >= t1) qn -= t1;
     const int lim_next = row_lim(row + step, qn);
     load_row(row + step, lim_next, nxt);  // prefetch the next row of this group
-    float2 s2 = make_float2(0.f, 0.f);  // two interleaved partial sums
-    if constexpr (std::is_same_v<T, float>) {
-      float m = -INFINITY;
-      const float2 sc = splat2(p.scale);
-#pragma unroll
-      for (int k = 0; k < NV; ++k) {
-        const int e0 = (lr + k * tpr) * N;
-        float2 *x2 = reinterpret_cast<float2 *>(&cur[k]);
-        float *x = reinterpret_cast<float *>(&cur[k]);
-        if (e0 + N <= lim) {
-          if (p.scaled) {
-            x2[0] = __fmul2_rn(x2[0], sc);
-            x2[1] = __fmul2_rn(x2[1], sc);
-          }
-        } else {  // the vector holding the row end, or padding: -inf past it
-#pragma unroll
-          for (int j = 0; j < N; ++j) {
-            if (e0 + j < lim) {
-              if (p.scaled) x[j] = __fmul_rn(x[j], p.scale);
-            } else {
-              x[j] = -INFINITY;
-            }
-          }
-        }
-        m = fmaxf(m, fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3])));
-      }
-      const float2 nmx = splat2(-group_max<false>(m, tpr, red_max));
-#pragma unroll
-      for (int k = 0; k < NV; ++k) {
-        float2 *x2 = reinterpret_cast<float2 *>(&cur[k]);
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const float2 d = __fadd2_rn(x2[j], nmx);  // x - max; exp(-inf) = 0 for masked / padding
-          x2[j] = make_float2(expf(d.x), expf(d.y));
-          s2 = __fadd2_rn(s2, x2[j]);
-        }
-      }
-    } else {
-      using P = Pair<T>;
-      using T2 = typename P::T2;
-      constexpr int W = N / 2;
-      T2 mx2 = P::neg_inf();
-      const T2 sc2 = P::splat(p.scale);
-#pragma unroll
-      for (int k = 0; k < NV; ++k) {
-        const int e0 = (lr + k * tpr) * N;
-        T2 *w = reinterpret_cast<T2 *>(&cur[k]);
-        if (e0 + N <= lim) {
-          if (p.scaled) {
-#pragma unroll
-            for (int j = 0; j < W; ++j) w[j] = __hmul2(w[j], sc2);
-          }
-        } else {  // the vector holding the row end, or padding: -inf past it
-#pragma unroll
-          for (int j = 0; j < W; ++j) {
-            if (e0 + 2 * j + 1 < lim) {
-              if (p.scaled) w[j] = __hmul2(w[j], sc2);
-            } else if (e0 + 2 * j < lim) {
-              if (p.scaled) w[j] = __hmul2(w[j], sc2);
-              w[j] = P::mask_high(w[j]);
-            } else {
-              w[j] = P::neg_inf();
-            }
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < W; ++j) mx2 = __hmax2(mx2, w[j]);
-      }
-      const float2 mf = P::to_f2(mx2);
-      const T2 m2 = P::splat(group_max<false>(fmaxf(mf.x, mf.y), tpr, red_max));  // exact: the max is a T value
-#pragma unroll
-      for (int k = 0; k < NV; ++k) {
-        T2 *w = reinterpret_cast<T2 *>(&cur[k]);
-#pragma unroll
-        for (int j = 0; j < W; ++j) {
-          const float2 d = P::to_f2(__hsub2(w[j], m2));  // T(x - max)
-          const T2 e = P::from_f2(exp_t<T>(d.x), exp_t<T>(d.y));  // T(exp(...))
-          s2 = __fadd2_rn(s2, P::to_f2(e));
-          w[j] = e;
-        }
-      }
-    }
-    const float s = group_sum<false>(__fadd_rn(s2.x, s2.y), tpr, red_sum);
-    // s >= 1 for a live row: its maximum contributes exp(0).
-    const float2 rs = splat2(__frcp_rn(s)), ns = splat2(-s);
-    if (row < p.rows) {
-#pragma unroll
-      for (int k = 0; k < NV; ++k) {
-        const int vi = lr + k * tpr;
-        if (vi < p.nvec) {
-          if constexpr (std::is_same_v<T, float>) {
-            float2 *x2 = reinterpret_cast<float2 *>(&cur[k]);
-            x2[0] = div_nonneg2(x2[0], ns, rs);
-            x2[1] = div_nonneg2(x2[1], ns, rs);
-          } else {
-            using P = Pair<T>;
-            using T2 = typename P::T2;
-            T2 *w = reinterpret_cast<T2 *>(&cur[k]);
-#pragma unroll
-            for (int j = 0; j < N / 2; ++j) {
-              const float2 q = div_nonneg2(P::to_f2(w[j]), ns, rs);
-              w[j] = P::from_f2(q.x, q.y);
-            }
-          }
-          st_vec(dst + row * p.cols + vi * N, cur[k]);
-        }
-      }
-    }
+    float mn;
+    const float mx = group_max<false>(softmax_prep<T, NV>(cur, lr, tpr, lim, p, mn), tpr, red_max);
+    const float s = group_sum<false>(softmax_exp<T, NV>(cur, mx, mn), tpr, red_sum);
+    if (row < p.rows) softmax_store<T, NV>(cur, s, dst + row * p.cols, lr, tpr, p.nvec);
 #pragma unroll
     for (int k = 0; k < NV; ++k) cur[k] = nxt[k];
     q = qn;
     lim = lim_next;
+  }
+}
+
+// Vector rows staged through shared memory: one block per row, persistent over
+// rows blockIdx.x, blockIdx.x + gridDim.x, ... Thread 0 streams each row into
+// one of `stages` shared-memory buffers with a bulk copy (the TMA engine),
+// `stages` rows ahead, so the prefetch depth costs no registers and each
+// thread keeps only NV vectors of the current row. Causal rows copy only their
+// first `lim` columns (rounded up to the 16-byte vector). Arithmetic as
+// softmax_pipe_kernel; the block reductions go through shared memory.
+//
+// A bulk copy that does not complete within kStageWaitLimit polls (it cannot
+// happen with valid arguments; the limit guards against a hang) makes the
+// whole block stop: it waits, again bounded, for its copies still in flight
+// and writes NaN to every row it has not finished, so the failure shows in
+// the output instead of as a hang.
+constexpr int kMaxStages = 4;
+constexpr uint32_t kStageWaitLimit = 1u << 22;
+
+template <typename T, int NV, bool kCausal>
+__global__ void __launch_bounds__(NV >= 8 ? 512 : 1024) softmax_staged_kernel(const SoftmaxParams p, int stages,
+                                                                              int stage_bytes) {
+  griddep_wait();
+  griddep_release();
+  constexpr int N = Elem<T>::kVec;
+  extern __shared__ __align__(128) unsigned char stage_buf[];
+  __shared__ uint64_t full[kMaxStages];
+  __shared__ float red_max[32], red_sum[32];
+  const int tid = threadIdx.x, tpr = blockDim.x, warps = tpr >> 5;
+  const int64_t step = gridDim.x;
+  const int cols = static_cast<int>(p.cols);
+  const T *src = static_cast<const T *>(p.src);
+  T *dst = static_cast<T *>(p.dst);
+  // Query index tracking as in softmax_pipe_kernel, once for the row being
+  // computed (q) and once for the next row to copy (q_in, thread 0 only).
+  const int t1 = kCausal ? static_cast<int>(p.t1) : 1;
+  const int q_step = kCausal ? static_cast<int>(step % t1) : 0;
+  const int off = kCausal ? static_cast<int>(p.offset < p.cols ? p.offset : p.cols) : 0;
+  auto lim_of = [&](int q) -> int {
+    if constexpr (kCausal) {
+      const int l = off + q + 1;
+      return l < cols ? l : cols;
+    } else {
+      return cols;
+    }
+  };
+  auto next_q = [&](int q) -> int {
+    q += q_step;
+    return q >= t1 ? q - t1 : q;
+  };
+  int q = kCausal ? static_cast<int>(blockIdx.x % t1) : 0;
+  // The copy side's state lives in shared memory: only thread 0 uses it, once
+  // per row, and registers stay free for the row values.
+  __shared__ int64_t row_in;  // next row to copy
+  __shared__ int q_in, s_in;  // its query index and buffer
+  auto copy_next = [&]() {  // thread 0
+    const int64_t r = row_in;
+    const int b = s_in;
+    const uint32_t bytes = static_cast<uint32_t>((lim_of(q_in) + N - 1) / N) * 16u;
+    bulk_load(stage_buf + static_cast<size_t>(b) * stage_bytes, src + r * p.cols, bytes, &full[b], l2_evict_first());
+    row_in = r + step;
+    q_in = next_q(q_in);
+    s_in = b + 1 == stages ? 0 : b + 1;
+  };
+  if (tid == 0) {
+    for (int b = 0; b < stages; ++b) mbar_init(&full[b], 1);
+    mbar_init_fence();
+    row_in = blockIdx.x;
+    q_in = q;
+    s_in = 0;
+    for (int b = 0; b < stages && row_in < p.rows; ++b) copy_next();
+  }
+  __syncthreads();
+  int s = 0;
+  uint32_t parity = 0;
+  for (int64_t row = blockIdx.x; row < p.rows; row += step) {
+    const int lim = lim_of(q);
+    const bool arrived = mbar_wait(&full[s], parity, kStageWaitLimit);
+    const uint4 *buf = reinterpret_cast<const uint4 *>(stage_buf + static_cast<size_t>(s) * stage_bytes);
+    uint4 cur[NV];
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int vi = tid + k * tpr;
+      if (vi * N < lim) cur[k] = buf[vi];
+    }
+    float mn;
+    float m = softmax_prep<T, NV>(cur, tid, tpr, lim, p, mn);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((tid & 31) == 0) red_max[tid >> 5] = m;
+    // The block barrier of the max also tells every thread whether any wait gave up.
+    if (__syncthreads_or(!arrived)) {
+      if (tid == 0) {  // let the copies still in flight land before the block exits
+        int sw = s;
+        uint32_t pw = parity;
+        for (int64_t r = row; r < row_in; r += step) {
+          mbar_wait(&full[sw], pw, kStageWaitLimit);
+          if (++sw == stages) {
+            sw = 0;
+            pw ^= 1u;
+          }
+        }
+      }
+      const uint4 nan4 = std::is_same_v<T, float> ? make_uint4(0x7fc00000u, 0x7fc00000u, 0x7fc00000u, 0x7fc00000u)
+                                                  : (std::is_same_v<T, __half> ? make_uint4(0x7e007e00u, 0x7e007e00u,
+                                                                                            0x7e007e00u, 0x7e007e00u)
+                                                                               : make_uint4(0x7fc07fc0u, 0x7fc07fc0u,
+                                                                                            0x7fc07fc0u, 0x7fc07fc0u));
+      for (int64_t r = row; r < p.rows; r += step)
+        for (int vi = tid; vi < p.nvec; vi += tpr) st_vec(dst + r * p.cols + vi * N, nan4);
+      return;
+    }
+    // Every thread has read buffer s: refill it with the row `stages` ahead.
+    if (tid == 0 && row_in < p.rows) {
+      fence_async_smem();
+      copy_next();
+    }
+    float mx = red_max[0];
+    for (int w = 1; w < warps; ++w) mx = fmaxf(mx, red_max[w]);
+    const float sum = group_sum<false>(softmax_exp<T, NV>(cur, mx, mn), tpr, red_sum);
+    softmax_store<T, NV>(cur, sum, dst + row * p.cols, tid, tpr, p.nvec);
+    if (++s == stages) {
+      s = 0;
+      parity ^= 1u;
+    }
+    q = next_q(q);
   }
 }
 
@@ -400,12 +602,54 @@ bool launch_softmax_regs(const SoftmaxParams &p, int nv, int block, int64_t grid
                   : launch_softmax_regs_c<T, kVector, false>(p, nv, block, grid, st);
 }
 
+// Shared-memory-staged rows: 8 vectors per thread (blocks of up to 512
+// threads), two stage buffers. Used, as measured on B200, for 16-bit rows of
+// 512 to 4096 vectors (4096 to 32768 elements) and f32 rows of 2049 to 4096
+// vectors (8196 to 16384 elements); narrower rows run as fast or faster in the
+// register-prefetching kernel, and 4096 vectors (64 KB) is the widest row the
+// 512 threads hold.
+constexpr int kStagedNv = 8;
+constexpr int64_t kStagedMaxVec = 4096;
+constexpr int kStages = 2;
+
+static_assert(kStages <= kMaxStages && kStages * kStagedMaxVec * 16 <= 200 * 1024,
+              "the stage buffers must fit in one SM's shared memory");
+
+template <typename T>
+constexpr int64_t staged_min_vec() {
+  return std::is_same_v<T, float> ? 2049 : 512;
+}
+
+template <typename T, bool kCausal>
+void launch_softmax_staged(SoftmaxParams p, int64_t nvec, cudaStream_t st) {
+  auto kernel = softmax_staged_kernel<T, kStagedNv, kCausal>;
+  const int block = static_cast<int>(ceil_div(ceil_div(nvec, kStagedNv), 32) * 32);
+  const int stage_bytes = static_cast<int>(ceil_div(nvec * 16, 128) * 128);
+  const size_t smem = static_cast<size_t>(kStages) * stage_bytes;
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, block, smem) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  const int64_t all = static_cast<int64_t>(per_sm) * sm_count();
+  const int64_t grid = p.rows < all ? p.rows : all;
+  p.tpr = block;
+  p.nvec = static_cast<int>(nvec);
+  launch_k(kernel, dim3(static_cast<unsigned>(grid)), dim3(block), smem, st, p, kStages, stage_bytes);
+}
+
 template <typename T>
 int launch_softmax(SoftmaxParams p, cudaStream_t st) {
   constexpr int V = Elem<T>::kVec;
   const bool vec = p.cols % V == 0 && is_aligned16(p.dst) && is_aligned16(p.src);
   const int n = vec ? V : 1;
   const int64_t nvec = p.cols / n;
+  if (vec && nvec >= staged_min_vec<T>() && nvec <= kStagedMaxVec) {
+    if (p.causal)
+      launch_softmax_staged<T, true>(p, nvec, st);
+    else
+      launch_softmax_staged<T, false>(p, nvec, st);
+    return check_launch("xn_softmax");
+  }
   // exp needs more registers than the norms: groups of up to 512 threads with
   // up to 32 row values each keep rows of up to 16384 elements in registers.
   const int nv_cap = (32 / n) < 8 ? (32 / n) : 8;

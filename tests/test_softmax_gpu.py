@@ -99,3 +99,48 @@ def test_softmax_exp_every_input(oracle, xn, cuda, dtype, width):
     diff = np.nonzero(np.any(got != ref, axis=1))[0]
     print(f"{dtype}: {diff.size} of {n} inputs differ")
     assert diff.size == 0, f"first differing inputs: {[hex(int(b)) for b in v[diff[:8]]]}"
+    if width == 8:
+        # The same rows with the -inf columns masked by the fused causal mask
+        # (one query row per slice, offset 1: columns >= 2 are not read)
+        # instead of held in the data. A thread whose live values stay within
+        # 86 of the row max then takes the flush-to-zero exp, so every input
+        # v >= -86 goes through that form too.
+        xm = x.copy()
+        xm[:, 2:] = 0
+        got_m = from_device(xn.softmax_causal(to_device(xm.reshape(n, 1, width), dtype, cuda), 1), dtype)
+        diff = np.nonzero(np.any(got_m.reshape(n, width) != ref, axis=1))[0]
+        print(f"{dtype} (causal): {diff.size} of {n} inputs differ")
+        assert diff.size == 0, f"first differing inputs: {[hex(int(b)) for b in v[diff[:8]]]}"
+
+
+@pytest.mark.parametrize("dtype,rows,cols", [("bf16", 6000, 4096), ("bf16", 13500, 2048), ("f16", 3000, 8192),
+                                             ("bf16", 700, 32768), ("f32", 1100, 16384), ("f32", 5000, 1024)])
+def test_softmax_many_rows_per_block(oracle, xn, cuda, dtype, rows, cols):
+    """Enough rows that every block of the persistent kernels walks several:
+    each shared-memory stage buffer of the staged kernel is refilled more than
+    once (its barrier phases wrap). Also run in place (dst == src), which the
+    ABI allows, and compared bit for bit with the out-of-place result."""
+    r = rng(rows + cols)
+    x = to_storage(randn(r, (rows, cols), 2.0), dtype)
+    ref = oracle.softmax(x, dtype)
+    X = to_device(x, dtype, cuda)
+    Y = xn.softmax(X)
+    assert_close(from_device(Y, dtype), ref, dtype, f"softmax {dtype} {rows}x{cols}")
+    xn.softmax_(X, X)
+    assert np.array_equal(from_device(X, dtype), from_device(Y, dtype))
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_softmax_causal_many_rows(oracle, xn, cuda, dtype):
+    """Causal rows of varying length (offset + i + 1 of 4096 columns, most of
+    them ending inside a 16-byte vector), many per block; with and without the
+    fused score scale."""
+    shape, offset = (4, 8, 301, 4096), 4096 - 301 - 3
+    r = rng(77)
+    x = to_storage(randn(r, shape, 2.0), dtype)
+    ref = oracle.softmax_causal(x, offset, dtype)
+    X = to_device(x, dtype, cuda)
+    assert_close(from_device(xn.softmax_causal(X, offset), dtype), ref, dtype, f"softmax_causal {dtype} {shape}")
+    sc = to_storage(np.full(shape[-1], 0.125, dtype=np.float32), dtype)
+    ref_s = oracle.softmax_causal(oracle.broadcast_rows(x, sc, "mul", dtype), offset, dtype)
+    assert_close(from_device(xn.attn_softmax(X, 0.125, offset), dtype), ref_s, dtype, f"attn_softmax {dtype} {shape}")
