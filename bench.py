@@ -480,6 +480,9 @@ def cpu_decode_rate(act: str, steps: int = 3, batch: int = 16) -> dict:
 # exceed the memory cap are skipped (listed with the reason).
 # ---------------------------------------------------------------------------
 SWEEP_OPS = ["rms_norm_residual", "layer_norm", "rope", "swiglu", "softmax", "embedding_gather"]
+# Further ops the sweep can run (--sweep-ops), outside benchmark config 5's list.
+SWEEP_EXTRA_OPS = ["silu", "gelu_erf", "residual_add", "softmax_causal", "causal_mask", "rvq_decode"]
+RVQ_BINS, RVQ_BOOKS = 2048, 8
 
 
 def sweep(torch, xn, device, widths, rows_list, dtypes, reps: int, mem_cap_gb: float, ops=SWEEP_OPS) -> list[dict]:
@@ -497,8 +500,10 @@ def sweep(torch, xn, device, widths, rows_list, dtypes, reps: int, mem_cap_gb: f
             for cols in widths:
                 for rows in rows_list:
                     n_tensors = {"rms_norm_residual": 4, "layer_norm": 2, "rope": 2, "swiglu": 3, "softmax": 2,
-                                 "embedding_gather": 1}[op]
-                    need = n_tensors * rows * cols * s + (32768 * cols * s if op == "embedding_gather" else 0)
+                                 "embedding_gather": 1, "silu": 2, "gelu_erf": 2, "residual_add": 3,
+                                 "softmax_causal": 2, "causal_mask": 1, "rvq_decode": 1}[op]
+                    need = n_tensors * rows * cols * s + (32768 * cols * s if op == "embedding_gather" else 0) + \
+                        (RVQ_BOOKS * (RVQ_BINS * cols * s + rows * 8) if op == "rvq_decode" else 0)
                     point = {"op": op, "dtype": dname, "rows": rows, "cols": cols}
                     if need > mem_cap_gb * 1e9:
                         point["skipped"] = f"needs {need / 1e9:.1f} GB > cap {mem_cap_gb} GB"
@@ -540,6 +545,41 @@ def sweep(torch, xn, device, widths, rows_list, dtypes, reps: int, mem_cap_gb: f
                         x, y = rnd(rows, cols), torch.empty(rows, cols, dtype=dt, device=device)
                         fn = lambda: xn.softmax_(y, x)  # noqa: E731
                         nbytes = 2 * rows * cols * s
+                    elif op in ("silu", "gelu_erf"):
+                        x, y = rnd(rows, cols), torch.empty(rows, cols, dtype=dt, device=device)
+                        fn = lambda: xn.unary_(y, x, op)  # noqa: E731
+                        nbytes = 2 * rows * cols * s
+                    elif op == "residual_add":
+                        x, br, y = rnd(rows, cols), rnd(rows, cols), torch.empty(rows, cols, dtype=dt, device=device)
+                        ls = (rnd(cols).abs() * 0.05).to(dt)
+                        fn = lambda: xn.residual_add_(y, x, br, ls)  # noqa: E731
+                        nbytes = 3 * rows * cols * s + cols * s
+                    elif op in ("softmax_causal", "causal_mask"):
+                        # Prefill-shaped attention scores: slices of t1 = 1024 queries over
+                        # `cols` keys, the last query seeing every key (offset = cols - t1).
+                        t1 = min(1024, rows)
+                        if rows % t1:
+                            point["skipped"] = "rows must be a multiple of the 1024-query slice"
+                            out.append(point)
+                            continue
+                        offset = max(cols - t1, 0)
+                        live = sum(min(offset + i + 1, cols) for i in range(t1)) * (rows // t1)
+                        x = rnd(rows // t1, t1, cols)
+                        if op == "softmax_causal":
+                            y = torch.empty_like(x)
+                            fn = lambda: xn.softmax_causal_(y, x, offset)  # noqa: E731
+                            nbytes = (live + rows * cols) * s  # unmasked reads, every element written
+                        else:
+                            fn = lambda: xn.apply_causality_mask_(x, offset)  # noqa: E731
+                            nbytes = (rows * cols - live) * s  # the masked elements, written
+                    elif op == "rvq_decode":
+                        books = [rnd(RVQ_BINS, cols) for _ in range(RVQ_BOOKS)]
+                        codes = torch.randint(0, RVQ_BINS, (1, RVQ_BOOKS, rows), dtype=torch.int64, device=device,
+                                              generator=g)
+                        y = torch.empty(1, rows, cols, dtype=dt, device=device)
+                        fn = lambda: xn.rvq_decode_sum(books, codes, out_layout="btd", out=y)  # noqa: E731
+                        # per frame: Q codes, Q codebook rows (from L2 while the books fit), one output row
+                        nbytes = rows * (RVQ_BOOKS * 8 + RVQ_BOOKS * cols * s + cols * s)
                     else:
                         table = rnd(32768, cols)
                         ids = torch.randint(0, 32768, (rows,), dtype=torch.int32, device=device, generator=g)
@@ -739,7 +779,8 @@ def main() -> int:
     ap.add_argument("--sweep-rows", default="1024,16384,262144,1048576")
     ap.add_argument("--sweep-dtypes", default="f32,bf16")
     ap.add_argument("--sweep-mem-gb", type=float, default=48.0)
-    ap.add_argument("--sweep-ops", default=",".join(SWEEP_OPS))
+    ap.add_argument("--sweep-ops", default=",".join(SWEEP_OPS),
+                    help="comma-separated subset of " + ",".join(SWEEP_OPS + SWEEP_EXTRA_OPS))
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -757,11 +798,15 @@ def main() -> int:
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     if args.sweep:
+        sweep_ops = [o for o in args.sweep_ops.split(",") if o]
+        unknown = [o for o in sweep_ops if o not in SWEEP_OPS + SWEEP_EXTRA_OPS]
+        if unknown:
+            ap.error(f"--sweep-ops: unknown op(s) {unknown}")
         xn.lib()
         peak, _ = measured_peak()
         pts = sweep(torch, xn, dev, [int(v) for v in args.sweep_widths.split(",")],
                     [int(v) for v in args.sweep_rows.split(",")], args.sweep_dtypes.split(","), max(3, args.steps),
-                    args.sweep_mem_gb, [o for o in args.sweep_ops.split(",") if o])
+                    args.sweep_mem_gb, sweep_ops)
         for pt in pts:
             if "gbs" in pt:
                 pt["frac"] = round(pt["gbs"] / peak, 3)

@@ -34,14 +34,54 @@ __device__ __forceinline__ float gelu_erf(float x) {
 // bf16 pairs with native bf16x2 arithmetic. For +, - and * of two bf16
 // values, one rounding of the exact result (the bf16x2 instructions) equals the
 // reference's f32 operation followed by rounding to bf16, so every step below
-// is the reference's step; the division uses div_for_bf16 (exact after the
-// final rounding to bf16).
+// that is such an operation is the reference's step.
+//
+// e = T(exp(-s)): 2^(x log2 e) for x = -s with log2 e = kL2eHi + kL2eLo, where
+// kL2eHi has 16 significant bits, so x * kL2eHi (x has 8) is exact; the low
+// part enters as the factor 2^(x kL2eLo) = 1 + c, c to second order (|x
+// kL2eLo| < 2^-9). The result carries the error of the hardware ex2 only.
+// x is clamped to [-110, 100] first (exp(x) overflows to inf above 88.8 and
+// rounds to 0 below -103.9, so no result changes; NaN passes through), which
+// keeps c finite, and kL2eLo > 0 keeps c >= 0 where ex2 overflows (inf * c
+// then stays inf). A result that would be subnormal is flushed: it only feeds
+// T(1 + e) = 1.
+//
+// y = T(s / d) for bf16 s and d = T(1 + e): s * rcp.approx(d) is within 2^-20
+// (relative) of s / d, also where the reciprocal is subnormal (d > 2^126, where
+// it keeps 21 or more significant bits), and
+// a quotient of two bf16 values is never within 2^-18 of a bf16 rounding
+// midpoint (s = m * d with m a 9-bit odd significand would need the odd part of
+// m * d, at least 257, to equal the odd part of s, at most 255), so it rounds
+// to the IEEE quotient's bf16 value. d = inf gives s * 0, the IEEE s / inf.
+//
+// test_unary_bf16_exhaustive runs every finite bf16 input through this
+// function against the oracle's glibc expf and IEEE division.
+constexpr float kL2eHi = 0x1.7154p+0f;
+constexpr float kL2eLo = 0x1.d94aep-18f;
+constexpr float kLn2 = 0x1.62e43p-1f;
+constexpr float kLn2SqHalf = 0x1.ebfbep-3f;
+
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ __nv_bfloat162 silu_bf16x2(__nv_bfloat162 s) {
-  const float2 nf = __bfloat1622float2(__hneg2(s));  // T::zero() - s (exact)
-  const __nv_bfloat162 e = __floats2bfloat162_rn(expf(nf.x), expf(nf.y));
+  const __nv_bfloat162 xb = __hmin2_nan(__hmax2_nan(__hneg2(s), __float2bfloat162_rn(-110.f)),
+                                        __float2bfloat162_rn(100.f));
+  const float2 x = bf2_to_f2(*reinterpret_cast<const uint32_t *>(&xb));
+  const float2 th = __fmul2_rn(x, splat2(kL2eHi));
+  const float2 tl = __fmul2_rn(x, splat2(kL2eLo));
+  const float2 eh = make_float2(ex2_approx_ftz(th.x), ex2_approx_ftz(th.y));
+  const float2 c = __fmul2_rn(tl, __ffma2_rn(tl, splat2(kLn2SqHalf), splat2(kLn2)));
+  const float2 ef = __ffma2_rn(eh, c, eh);
+  const __nv_bfloat162 e = __floats2bfloat162_rn(ef.x, ef.y);
   const __nv_bfloat162 d = __hadd2(__float2bfloat162_rn(1.f), e);  // T::one() + e
-  const float2 sf = __bfloat1622float2(s), df = __bfloat1622float2(d);
-  return __floats2bfloat162_rn(div_for_bf16(sf.x, df.x), div_for_bf16(sf.y, df.y));
+  const float2 sf = bf2_to_f2(*reinterpret_cast<const uint32_t *>(&s));
+  const float2 df = bf2_to_f2(*reinterpret_cast<const uint32_t *>(&d));
+  const float2 y = __fmul2_rn(sf, make_float2(rcp_approx(df.x), rcp_approx(df.y)));
+  return __floats2bfloat162_rn(y.x, y.y);
 }
 
 __device__ __forceinline__ uint32_t bf2_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t *>(&v); }

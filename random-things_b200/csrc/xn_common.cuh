@@ -539,22 +539,6 @@ __device__ __forceinline__ float2 div_nonneg2(float2 x, float2 nd, float2 r) {
   return __ffma2_rn(rem, r, q0);
 }
 
-// s / d where s and d are bf16 values, d >= 1, and the quotient is then
-// rounded to bf16. For 8-bit significands s/d is never an exact bf16 rounding
-// midpoint: s = m*d with m a 9-bit odd significand would need the odd part of
-// m*d (>= 257) to equal the odd part of s (<= 255). The quotient is in fact at
-// least 2^-18 (relative) away from every midpoint, so a quotient with relative
-// error below 2^-21 (__fdividef: MUFU reciprocal + multiply, 2 ulp) rounds to
-// the same bf16 value as the IEEE quotient, and so does the IEEE quotient
-// rounded first to f32 (the reference's path). __fdividef needs |d| < 2^126:
-// larger d (only when exp overflows bf16's range, s < -87) are brought into
-// range by scaling both operands by 2^-64, which is exact there; d = inf gives
-// the IEEE result -0 / +0.
-__device__ __forceinline__ float div_for_bf16(float s, float d) {
-  const float sc = d > 0x1p126f ? 0x1p-64f : 1.f;
-  return __fdividef(__fmul_rn(s, sc), __fmul_rn(d, sc));
-}
-
 __host__ __device__ __forceinline__ bool aligned16(const void *p) {
   return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
 }

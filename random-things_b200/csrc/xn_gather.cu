@@ -13,6 +13,8 @@
 // device error flag instead of faulting. The RVQ kernel sums the n_q codebook
 // rows of a frame in registers and, for the [B, dim, T] layout, transposes a
 // tile of 32 frames through shared memory so the stores stay coalesced.
+#include <type_traits>
+
 #include "xn_common.cuh"
 #include "xn_internal.h"
 
@@ -166,20 +168,31 @@ __device__ __forceinline__ int64_t frame_code(const RvqParams &p, int64_t b, int
   return c;
 }
 
-// Sum of the nq codebook rows for access unit u of the frame.
+// Lane q (< nq) holds the address of the row of codebook q that this frame's
+// code selects, null for a bad code (its row adds +0.0). The other lanes read
+// the addresses by shuffle, so each codebook pointer is fetched once per frame.
+template <typename T>
+__device__ __forceinline__ uintptr_t frame_row(const RvqParams &p, int64_t b, int64_t t, int lane) {
+  const int64_t c = frame_code(p, b, t, lane);
+  if (lane >= p.nq || c < 0) return 0;
+  return reinterpret_cast<uintptr_t>(static_cast<const T *>(p.tab.p[lane]) + c * p.dim);
+}
+
+// Sum of the nq codebook rows for access unit u of the frame, in f32 values
+// rounded to T after every add (the reference's T-typed adds in codebook
+// order).
 template <typename T, bool kVector>
-__device__ __forceinline__ void frame_sum(const RvqParams &p, int64_t code_lane, int u,
+__device__ __forceinline__ void frame_sum(const RvqParams &p, uintptr_t row_lane, int u,
                                           float (&acc)[kVector ? Elem<T>::kVec : 1]) {
   constexpr int N = kVector ? Elem<T>::kVec : 1;
   for (int q = 0; q < p.nq; ++q) {
-    const int64_t code = __shfl_sync(0xffffffffu, code_lane, q);
+    const T *row = reinterpret_cast<const T *>(__shfl_sync(0xffffffffu, row_lane, q));
     float v[N];
-    if (code >= 0) {
-      const T *row = static_cast<const T *>(p.tab.p[q]) + code * p.dim + static_cast<int64_t>(u) * N;
+    if (row != nullptr) {
       if constexpr (kVector) {
-        unpack<T>(ld_cached(row), v);
+        unpack<T>(ld_cached(row + static_cast<int64_t>(u) * N), v);
       } else {
-        v[0] = Elem<T>::to_f32(__ldg(row));
+        v[0] = Elem<T>::to_f32(__ldg(row + u));
       }
     } else {
 #pragma unroll
@@ -189,6 +202,38 @@ __device__ __forceinline__ void frame_sum(const RvqParams &p, int64_t code_lane,
     for (int j = 0; j < N; ++j) acc[j] = q == 0 ? v[j] : Elem<T>::round(__fadd_rn(acc[j], v[j]));
   }
 }
+
+// The same sum for 16-bit vector rows, kept packed: each add is one paired
+// bf16x2 / f16x2 add, which rounds the exact sum of two T values once. That is
+// the reference's f32 add followed by rounding to T: f32's 24 bits are at
+// least 2p + 2 for T's p-bit significand (p = 8 or 11), so the double rounding
+// is innocuous. Up to 8 codebook rows are loaded before they are added.
+template <typename T>
+__device__ __forceinline__ uint4 frame_sum_packed(const RvqParams &p, uintptr_t row_lane, int u) {
+  uint4 acc = make_uint4(0u, 0u, 0u, 0u);
+  for (int q0 = 0; q0 < p.nq; q0 += 8) {
+    uint4 v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const uintptr_t a = __shfl_sync(0xffffffffu, row_lane, (q0 + k) & 31);
+      v[k] = make_uint4(0u, 0u, 0u, 0u);
+      if (q0 + k < p.nq && a != 0) v[k] = ld_cached(reinterpret_cast<const T *>(a) + static_cast<int64_t>(u) * 8);
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (q0 + k == 0) {
+        acc = v[k];
+      } else if (q0 + k < p.nq) {
+        acc = make_uint4(t2_add<T>(acc.x, v[k].x), t2_add<T>(acc.y, v[k].y), t2_add<T>(acc.z, v[k].z),
+                         t2_add<T>(acc.w, v[k].w));
+      }
+    }
+  }
+  return acc;
+}
+
+template <typename T, bool kVector>
+constexpr bool kPackedSum = kVector && !std::is_same_v<T, float>;
 
 // [batch, frames, dim] output: one warp per frame.
 template <typename T, bool kVector>
@@ -201,18 +246,23 @@ __global__ void __launch_bounds__(256) rvq_btd_kernel(const RvqParams p) {
   if (frame >= p.batch * p.frames) return;
   const int64_t b = frame / p.frames;
   const int64_t t = frame - b * p.frames;
-  const int64_t code_lane = frame_code(p, b, t, lane);
+  const uintptr_t row_lane = frame_row<T>(p, b, t, lane);
   T *out = static_cast<T *>(p.dst) + frame * p.dim;
   for (int u0 = 0; u0 < p.nvec; u0 += 32) {
     const int u = u0 + lane;
-    float acc[N];
-    // All lanes run frame_sum (it shuffles); only in-range units are stored.
-    frame_sum<T, kVector>(p, code_lane, u < p.nvec ? u : 0, acc);
-    if (u < p.nvec) {
-      if constexpr (kVector) {
-        st_vec(out + static_cast<int64_t>(u) * N, pack<T>(acc));
-      } else {
-        out[u] = Elem<T>::from_f32(acc[0]);
+    // All lanes run the sum (it shuffles); only in-range units are stored.
+    if constexpr (kPackedSum<T, kVector>) {
+      const uint4 sum = frame_sum_packed<T>(p, row_lane, u < p.nvec ? u : 0);
+      if (u < p.nvec) st_vec(out + static_cast<int64_t>(u) * N, sum);
+    } else {
+      float acc[N];
+      frame_sum<T, kVector>(p, row_lane, u < p.nvec ? u : 0, acc);
+      if (u < p.nvec) {
+        if constexpr (kVector) {
+          st_vec(out + static_cast<int64_t>(u) * N, pack<T>(acc));
+        } else {
+          out[u] = Elem<T>::from_f32(acc[0]);
+        }
       }
     }
   }
@@ -236,11 +286,15 @@ __global__ void __launch_bounds__(256) rvq_bct_kernel(const RvqParams p) {
   for (int f = warp; f < 32; f += 8) {
     const int64_t t = t0 + f;
     if (t >= p.frames) break;
-    const int64_t code_lane = frame_code(p, b, t, lane);
+    const uintptr_t row_lane = frame_row<T>(p, b, t, lane);
     for (int u0 = 0; u0 < p.nvec; u0 += 32) {
       const int u = u0 + lane;
       float acc[N];
-      frame_sum<T, kVector>(p, code_lane, u < p.nvec ? u : 0, acc);
+      if constexpr (kPackedSum<T, kVector>) {
+        unpack<T>(frame_sum_packed<T>(p, row_lane, u < p.nvec ? u : 0), acc);
+      } else {
+        frame_sum<T, kVector>(p, row_lane, u < p.nvec ? u : 0, acc);
+      }
       if (u < p.nvec) {
 #pragma unroll
         for (int j = 0; j < N; ++j) tile[f * ld + static_cast<int64_t>(u) * N + j] = acc[j];
@@ -265,12 +319,12 @@ __global__ void __launch_bounds__(256) rvq_bct_wide_kernel(const RvqParams p) {
   if (frame >= p.batch * p.frames) return;
   const int64_t b = frame / p.frames;
   const int64_t t = frame - b * p.frames;
-  const int64_t code_lane = frame_code(p, b, t, lane);
+  const uintptr_t row_lane = frame_row<T>(p, b, t, lane);
   T *out = static_cast<T *>(p.dst) + b * p.dim * p.frames + t;
   for (int u0 = 0; u0 < p.nvec; u0 += 32) {
     const int u = u0 + lane;
     float acc[1];
-    frame_sum<T, false>(p, code_lane, u < p.nvec ? u : 0, acc);
+    frame_sum<T, false>(p, row_lane, u < p.nvec ? u : 0, acc);
     if (u < p.nvec) out[static_cast<int64_t>(u) * p.frames] = Elem<T>::from_f32(acc[0]);
   }
 }
