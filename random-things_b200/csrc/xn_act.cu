@@ -67,6 +67,14 @@ __device__ __forceinline__ float rcp_approx(float x) {
   return y;
 }
 
+// The same reciprocal without the handling of subnormal inputs and results,
+// for arguments known to lie in [1, 3].
+__device__ __forceinline__ float rcp_approx_ftz(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ __nv_bfloat162 silu_bf16x2(__nv_bfloat162 s) {
   const __nv_bfloat162 xb = __hmin2_nan(__hmax2_nan(__hneg2(s), __float2bfloat162_rn(-110.f)),
                                         __float2bfloat162_rn(100.f));
@@ -99,12 +107,50 @@ __device__ __forceinline__ uint4 swiglu_bf16x8(uint4 g, uint4 u) {
                     bf2_bits(__hmul2(silu_bf16x2(bits_bf2(g.w)), bits_bf2(u.w))));
 }
 
+// GELU(erf) for 16-bit T, on element pairs: y = x*0.5*(1 + erf(x/sqrt2)) in
+// f32 as the reference computes it, with erf from
+//   erfc(a) = exp(-a^2) * F(a),  a = min(|z|, 4),
+// F(a) = erfc(a) e^{a^2} a degree-7 polynomial in t = 1 / (1 + a/2) (relative
+// error 2^-22.5 on [0, 4]; coefficients from fit_gelu_erfc.py), t from the
+// hardware reciprocal and exp from the hardware ex2. erf(z) = sign(z) (1 -
+// erfc(a)), so for z < 0 the f32 value 1 + erf is erfc(a) rounded to erf's
+// 2^-24 grid, as the reference's 1 + erff(z) is. At a = 4, 1 - erfc rounds to
+// 1: |z| >= 4 gives erf = +-1, f32's value there (a NaN x stays NaN through
+// x * 0.5). |z| < 2^-10: erf = z * 2/sqrt(pi), which keeps 1 + erf exact for
+// the smallest x, whose f32 products are subnormal. The error of this erf is
+// about 2^-21 relative in erfc and 2^-21 absolute in erf, well inside a 16-bit
+// output's half ulp, so it only matters near a rounding midpoint:
+// test_unary_bf16_exhaustive runs every finite bf16 input against glibc's erff
+// (f32 keeps CUDA's erff).
+__device__ constexpr float kErfcF[8] = {0x1.a02292p-12f, 0x1.1c1feap-2f, 0x1.354df8p-2f, 0x1.bae5c4p-3f,
+                                        0x1.18f908p-3f,  0x1.367d7ep-2f, -0x1.454b7ep-2f, 0x1.4c22eap-4f};
+constexpr float kTwoOverSqrtPi = 0x1.20dd76p+0f;
+
+__device__ __forceinline__ float2 gelu_erf2(float2 x) {
+  const float2 z = __fmul2_rn(x, splat2(kFrac1Sqrt2));
+  const float2 a = make_float2(fminf(fabsf(z.x), 4.f), fminf(fabsf(z.y), 4.f));
+  const float2 u = __ffma2_rn(a, splat2(0.5f), splat2(1.f));
+  const float2 t = make_float2(rcp_approx_ftz(u.x), rcp_approx_ftz(u.y));  // u in [1, 3]
+  float2 q = splat2(kErfcF[7]);
+#pragma unroll
+  for (int i = 6; i >= 0; --i) q = __ffma2_rn(q, t, splat2(kErfcF[i]));
+  const float2 tt = __fmul2_rn(__fmul2_rn(a, a), splat2(-kLog2e));
+  const float2 erfc = __fmul2_rn(make_float2(ex2_approx_ftz(tt.x), ex2_approx_ftz(tt.y)), q);
+  const float2 om = __ffma2_rn(erfc, splat2(-1.f), splat2(1.f));  // 1 - erfc, one rounding
+  const float2 zs = __fmul2_rn(z, splat2(kTwoOverSqrtPi));
+  const float2 erf = make_float2(a.x < 0x1p-10f ? zs.x : copysignf(om.x, z.x),
+                                 a.y < 0x1p-10f ? zs.y : copysignf(om.y, z.y));
+  return __fmul2_rn(__fmul2_rn(x, splat2(0.5f)), __fadd2_rn(splat2(1.f), erf));
+}
+
 template <typename T, int OP>
 __device__ __forceinline__ float unary_op(float x) {
   if constexpr (OP == XN_UNARY_SILU) {
     return silu_t<T>(x);
-  } else {
+  } else if constexpr (std::is_same_v<T, float>) {
     return gelu_erf(x);
+  } else {
+    return gelu_erf2(make_float2(x, x)).x;
   }
 }
 
@@ -133,6 +179,12 @@ __global__ void __launch_bounds__(kBlock) unary_kernel(void *dst, const void *sr
       if (i < nacc) {
         if constexpr (std::is_same_v<T, __nv_bfloat16> && OP == XN_UNARY_SILU) {
           st_vec(d + i * N, silu_bf16x8(raw[u]));
+        } else if constexpr (!std::is_same_v<T, float> && OP == XN_UNARY_GELU_ERF) {
+          float2 v2[N / 2];
+          Pairs<T>::unpack(raw[u], v2);
+#pragma unroll
+          for (int j = 0; j < N / 2; ++j) v2[j] = gelu_erf2(v2[j]);
+          st_vec(d + i * N, Pairs<T>::pack(v2));
         } else {
           float v[N];
           unpack<T>(raw[u], v);
@@ -227,56 +279,69 @@ __global__ void __launch_bounds__(kBlock) swiglu_kernel(void *dst, const void *g
 
 // dst = T(x + T(branch * ls[col])) (or T(x + branch)) over [rows, cols]: the
 // reference's LayerScale::forward (broadcast_mul, cpu_backend.rs:1379-1387)
-// followed by `xs.add` (mimi.rs:1441-1444). grid.x covers a row's columns,
-// grid.y strides over rows.
+// followed by `xs.add` (mimi.rs:1441-1444). Blocks are bx x by threads: bx (a
+// power of two, up to 256) spans a row's accesses, by = 256 / bx rows, so short
+// rows still fill whole blocks. A thread keeps one column, loads its layer
+// scale once and handles kUnroll rows by apart; grid.y strides over row groups.
 template <typename T, bool kVector>
 __global__ void __launch_bounds__(kBlock) residual_kernel(void *dst, const void *x, const void *branch,
-                                                           const void *ls, int64_t rows, int64_t cols) {
+                                                           const void *ls, int64_t rows, int64_t cols,
+                                                           int bx_log2) {
   griddep_wait();
   griddep_release();
   constexpr int N = kVector ? Elem<T>::kVec : 1;
+  const int bx = 1 << bx_log2, by = kBlock >> bx_log2;
   const int64_t cacc = cols / N;
-  const int64_t c0 = static_cast<int64_t>(blockIdx.x) * kBlock * kUnroll + threadIdx.x;
-  for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
-    const T *xr = static_cast<const T *>(x) + r * cols;
-    const T *br = static_cast<const T *>(branch) + r * cols;
-    T *dr = static_cast<T *>(dst) + r * cols;
+  const int64_t c = static_cast<int64_t>(blockIdx.x) * bx + (threadIdx.x & (bx - 1));
+  if (c >= cacc) return;  // no block barrier follows
+  const int ty = threadIdx.x >> bx_log2;
+  const T *xs = static_cast<const T *>(x) + c * N;
+  const T *bs = static_cast<const T *>(branch) + c * N;
+  T *ds = static_cast<T *>(dst) + c * N;
+  float vs[N];
+  if (ls != nullptr) {
+    if constexpr (kVector) {
+      unpack<T>(ld_cached(static_cast<const T *>(ls) + c * N), vs);
+    } else {
+      vs[0] = Elem<T>::to_f32(static_cast<const T *>(ls)[c]);
+    }
+  }
+  const int64_t rstep = static_cast<int64_t>(gridDim.y) * by * kUnroll;
+  for (int64_t r0 = static_cast<int64_t>(blockIdx.y) * by * kUnroll + ty; r0 < rows; r0 += rstep) {
     if constexpr (kVector) {
       uint4 rx[kUnroll], rb[kUnroll];
 #pragma unroll
       for (int k = 0; k < kUnroll; ++k) {
-        const int64_t i = c0 + k * kBlock;
-        if (i < cacc) {
-          rx[k] = ld_stream(xr + i * N);
-          rb[k] = ld_stream(br + i * N);
+        const int64_t r = r0 + static_cast<int64_t>(k) * by;
+        if (r < rows) {
+          rx[k] = ld_stream(xs + r * cols);
+          rb[k] = ld_stream(bs + r * cols);
         }
       }
 #pragma unroll
       for (int k = 0; k < kUnroll; ++k) {
-        const int64_t i = c0 + k * kBlock;
-        if (i < cacc) {
+        const int64_t r = r0 + static_cast<int64_t>(k) * by;
+        if (r < rows) {
           float vx[N], vb[N];
           unpack<T>(rx[k], vx);
           unpack<T>(rb[k], vb);
           if (ls != nullptr) {
-            float vs[N];
-            unpack<T>(ld_cached(static_cast<const T *>(ls) + i * N), vs);
 #pragma unroll
             for (int j = 0; j < N; ++j) vb[j] = Elem<T>::round(__fmul_rn(vb[j], vs[j]));
           }
 #pragma unroll
           for (int j = 0; j < N; ++j) vx[j] = __fadd_rn(vx[j], vb[j]);
-          st_vec(dr + i * N, pack<T>(vx));
+          st_vec(ds + r * cols, pack<T>(vx));
         }
       }
     } else {
 #pragma unroll
       for (int k = 0; k < kUnroll; ++k) {
-        const int64_t i = c0 + k * kBlock;
-        if (i >= cols) break;
-        float b = Elem<T>::to_f32(br[i]);
-        if (ls != nullptr) b = Elem<T>::round(__fmul_rn(b, Elem<T>::to_f32(static_cast<const T *>(ls)[i])));
-        dr[i] = Elem<T>::from_f32(__fadd_rn(Elem<T>::to_f32(xr[i]), b));
+        const int64_t r = r0 + static_cast<int64_t>(k) * by;
+        if (r >= rows) break;
+        float b = Elem<T>::to_f32(bs[r * cols]);
+        if (ls != nullptr) b = Elem<T>::round(__fmul_rn(b, vs[0]));
+        ds[r * cols] = Elem<T>::from_f32(__fadd_rn(Elem<T>::to_f32(xs[r * cols]), b));
       }
     }
   }
@@ -287,15 +352,26 @@ int launch_residual(void *dst, const void *x, const void *branch, const void *ls
                     cudaStream_t st) {
   constexpr int V = Elem<T>::kVec;
   const bool vec = cols % V == 0 && is_aligned16(dst) && is_aligned16(x) && is_aligned16(branch) && is_aligned16(ls);
+  // Without a layer scale the columns do not matter: the contiguous tensor is
+  // reshaped to rows of one block's width (kBlock accesses) when it divides.
+  const int64_t unit = static_cast<int64_t>(kBlock) * (vec ? V : 1);
+  if (ls == nullptr && (rows * cols) % unit == 0) {
+    rows = rows * cols / unit;
+    cols = unit;
+  }
   const int64_t cacc = vec ? cols / V : cols;
-  const int64_t gx = ceil_div(cacc, static_cast<int64_t>(kBlock) * kUnroll);
+  int bx_log2 = 0;
+  while ((int64_t{1} << bx_log2) < cacc && (1 << bx_log2) < kBlock) ++bx_log2;
+  const int64_t bx = int64_t{1} << bx_log2, by = kBlock / bx;
+  const int64_t gx = ceil_div(cacc, bx);
   if (gx > 0x7fffffffLL) return fail(XN_E_INVALID, "xn_residual_add: row too long");
-  const int64_t gy = rows < 65535 ? rows : 65535;
+  int64_t gy = ceil_div(rows, by * kUnroll);
+  if (gy > 65535) gy = 65535;
   dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy));
   if (vec)
-    launch_k(residual_kernel<T, true>, dim3(grid), dim3(kBlock), 0, st, dst, x, branch, ls, rows, cols);
+    launch_k(residual_kernel<T, true>, grid, dim3(kBlock), 0, st, dst, x, branch, ls, rows, cols, bx_log2);
   else
-    launch_k(residual_kernel<T, false>, dim3(grid), dim3(kBlock), 0, st, dst, x, branch, ls, rows, cols);
+    launch_k(residual_kernel<T, false>, grid, dim3(kBlock), 0, st, dst, x, branch, ls, rows, cols, bx_log2);
   return check_launch("xn_residual_add");
 }
 

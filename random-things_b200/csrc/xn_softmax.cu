@@ -227,13 +227,21 @@ __device__ __forceinline__ float softmax_prep(uint4 (&cur)[NV], int lr, int tpr,
 // flush-to-zero form gives the same values with fewer instructions. Otherwise
 // (a row reaching below -86 relative to its max, an infinite input, a NaN)
 // the thread takes the form that keeps subnormals.
-template <typename T, int NV>
-__device__ __forceinline__ float softmax_exp(uint4 (&cur)[NV], float mx, float mn) {
+//
+// kSkip: vectors starting at or past `lim` hold only masked entries; they
+// become +0 without the arithmetic (the same values and sums: exp(-inf) = +0).
+template <typename T, int NV, bool kSkip>
+__device__ __forceinline__ float softmax_exp(uint4 (&cur)[NV], float mx, float mn, int lr, int tpr, int lim) {
+  constexpr int N = Elem<T>::kVec;
   float2 s2 = make_float2(0.f, 0.f);
   if constexpr (std::is_same_v<T, float>) {
     const float2 nmx = splat2(-mx);
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
+      if (kSkip && (lr + k * tpr) * N >= lim) {
+        cur[k] = make_uint4(0u, 0u, 0u, 0u);
+        continue;
+      }
       float2 *x2 = reinterpret_cast<float2 *>(&cur[k]);
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
@@ -261,6 +269,10 @@ __device__ __forceinline__ float softmax_exp(uint4 (&cur)[NV], float mx, float m
     auto run = [&](auto kind) {
 #pragma unroll
       for (int k = 0; k < NV; ++k) {
+        if (kSkip && (lr + k * tpr) * N >= lim) {
+          cur[k] = make_uint4(0u, 0u, 0u, 0u);
+          continue;
+        }
         T2 *w = reinterpret_cast<T2 *>(&cur[k]);
 #pragma unroll
         for (int j = 0; j < Elem<T>::kVec / 2; ++j) {
@@ -279,16 +291,20 @@ __device__ __forceinline__ float softmax_exp(uint4 (&cur)[NV], float mx, float m
 }
 
 // y = T(e / s) for the vectors below nvec, stored to the row at dst_row.
-// s >= 1 for a live row: its maximum contributes exp(0).
-template <typename T, int NV>
-__device__ __forceinline__ void softmax_store(uint4 (&cur)[NV], float s, T *dst_row, int lr, int tpr, int nvec) {
+// s >= 1 for a live row: its maximum contributes exp(0). kSkip: the +0
+// vectors at or past `lim` are stored as they are.
+template <typename T, int NV, bool kSkip>
+__device__ __forceinline__ void softmax_store(uint4 (&cur)[NV], float s, T *dst_row, int lr, int tpr, int nvec,
+                                              int lim) {
   constexpr int N = Elem<T>::kVec;
   const float2 rs = splat2(__frcp_rn(s)), ns = splat2(-s);
 #pragma unroll
   for (int k = 0; k < NV; ++k) {
     const int vi = lr + k * tpr;
     if (vi < nvec) {
-      if constexpr (std::is_same_v<T, float>) {
+      if (kSkip && vi * N >= lim) {
+        // masked: already +0
+      } else if constexpr (std::is_same_v<T, float>) {
         float2 *x2 = reinterpret_cast<float2 *>(&cur[k]);
         x2[0] = div_nonneg2(x2[0], ns, rs);
         x2[1] = div_nonneg2(x2[1], ns, rs);
@@ -363,8 +379,8 @@ __global__ void __launch_bounds__(512, NV >= 8 ? 1 : 2) softmax_pipe_kernel(cons
     load_row(row + step, lim_next, nxt);  // prefetch the next row of this group
     float mn;
     const float mx = group_max<false>(softmax_prep<T, NV>(cur, lr, tpr, lim, p, mn), tpr, red_max);
-    const float s = group_sum<false>(softmax_exp<T, NV>(cur, mx, mn), tpr, red_sum);
-    if (row < p.rows) softmax_store<T, NV>(cur, s, dst + row * p.cols, lr, tpr, p.nvec);
+    const float s = group_sum<false>(softmax_exp<T, NV, kCausal>(cur, mx, mn, lr, tpr, lim), tpr, red_sum);
+    if (row < p.rows) softmax_store<T, NV, kCausal>(cur, s, dst + row * p.cols, lr, tpr, p.nvec, lim);
 #pragma unroll
     for (int k = 0; k < NV; ++k) cur[k] = nxt[k];
     q = qn;
@@ -488,8 +504,10 @@ __global__ void __launch_bounds__(NV >= 8 ? 512 : 1024) softmax_staged_kernel(co
     }
     float mx = red_max[0];
     for (int w = 1; w < warps; ++w) mx = fmaxf(mx, red_max[w]);
-    const float sum = group_sum<false>(softmax_exp<T, NV>(cur, mx, mn), tpr, red_sum);
-    softmax_store<T, NV>(cur, sum, dst + row * p.cols, tid, tpr, p.nvec);
+    // Masked vectors go through the arithmetic here (exp(-inf) = 0): wide
+    // rows are mostly live, and the per-vector skip measured slower.
+    const float sum = group_sum<false>(softmax_exp<T, NV, false>(cur, mx, mn, tid, tpr, lim), tpr, red_sum);
+    softmax_store<T, NV, false>(cur, sum, dst + row * p.cols, tid, tpr, p.nvec, lim);
     if (++s == stages) {
       s = 0;
       parity ^= 1u;
@@ -677,18 +695,34 @@ int launch_softmax(SoftmaxParams p, cudaStream_t st) {
   return check_launch("xn_softmax");
 }
 
-// One warp per (b, i) row writes -inf to columns (offset + i, t2).
+// One warp per (b, i) row writes -inf to columns (offset + i, t2): 16-byte
+// stores over the part of that range that is 16-byte aligned, element stores
+// for the ends.
 template <typename T>
 __global__ void __launch_bounds__(256) causal_mask_kernel(void *dst, int64_t rows, int64_t t1,
                                                           int64_t t2, int64_t offset) {
   griddep_wait();
   griddep_release();
+  constexpr int N = Elem<T>::kVec;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (row >= rows) return;
+  const int lane = threadIdx.x & 31;
   const int64_t first = offset + (row % t1) + 1;
+  if (first >= t2) return;
   T *d = static_cast<T *>(dst) + row * t2;
   const T ninf = Elem<T>::from_f32(-INFINITY);
-  for (int64_t c = first + (threadIdx.x & 31); c < t2; c += 32) d[c] = ninf;
+  // [first, body0): head, [body0, body1): whole aligned vectors, [body1, t2): tail.
+  const int64_t mis = static_cast<int64_t>((reinterpret_cast<uintptr_t>(d + first) & 15u) / sizeof(T));
+  int64_t body0 = mis == 0 ? first : first + (N - mis);
+  if (body0 > t2) body0 = t2;
+  const int64_t body1 = body0 + (t2 - body0) / N * N;
+  if (first + lane < body0) d[first + lane] = ninf;  // the head is shorter than N <= 8 elements
+  uint4 v;
+  T *vt = reinterpret_cast<T *>(&v);
+#pragma unroll
+  for (int j = 0; j < N; ++j) vt[j] = ninf;
+  for (int64_t c = body0 + static_cast<int64_t>(lane) * N; c < body1; c += 32 * N) st_vec(d + c, v);
+  if (body1 + lane < t2) d[body1 + lane] = ninf;  // so is the tail
 }
 
 }  // namespace

@@ -118,7 +118,8 @@ def test_norm_deterministic(xn, cuda):
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
-@pytest.mark.parametrize("rows,cols", [(1000, 512), (7, 100), (3, 1), (70000, 24)])
+@pytest.mark.parametrize("rows,cols", [(1000, 512), (7, 100), (3, 1), (70000, 24), (2048, 256), (513, 64),
+                                       (4, 4104)])
 @pytest.mark.parametrize("with_ls", [True, False])
 def test_residual_add(oracle, xn, cuda, dtype, rows, cols, with_ls):
     """x + LayerScale(branch), bit-exact (mimi.rs:1441-1444)."""
