@@ -157,24 +157,27 @@ __device__ __forceinline__ float unary_op(float x) {
 constexpr int kBlock = 256;
 constexpr int kUnroll = 4;
 
-template <typename T, int OP, bool kVector>
+// kU accesses per thread: kU for large tensors; 1 for tensors smaller
+// than one wave of the kU grid, where the per-thread chain of work, not
+// bandwidth, sets the time.
+template <typename T, int OP, bool kVector, int kU>
 __global__ void __launch_bounds__(kBlock) unary_kernel(void *dst, const void *src, int64_t n) {
   griddep_wait();
   griddep_release();
   constexpr int N = kVector ? Elem<T>::kVec : 1;
   const int64_t nacc = n / N;
-  const int64_t base = static_cast<int64_t>(blockIdx.x) * kBlock * kUnroll + threadIdx.x;
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kBlock * kU + threadIdx.x;
   const T *s = static_cast<const T *>(src);
   T *d = static_cast<T *>(dst);
   if constexpr (kVector) {
-    uint4 raw[kUnroll];
+    uint4 raw[kU];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
+    for (int u = 0; u < kU; ++u) {
       const int64_t i = base + u * kBlock;
       if (i < nacc) raw[u] = ld_stream(s + i * N);
     }
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
+    for (int u = 0; u < kU; ++u) {
       const int64_t i = base + u * kBlock;
       if (i < nacc) {
         if constexpr (std::is_same_v<T, __nv_bfloat16> && OP == XN_UNARY_SILU) {
@@ -200,14 +203,14 @@ __global__ void __launch_bounds__(kBlock) unary_kernel(void *dst, const void *sr
         d[e] = Elem<T>::from_f32(unary_op<T, OP>(Elem<T>::to_f32(s[e])));
     }
   } else {
-    float v[kUnroll];
+    float v[kU];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
+    for (int u = 0; u < kU; ++u) {
       const int64_t i = base + u * kBlock;
       if (i < n) v[u] = Elem<T>::to_f32(s[i]);
     }
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
+    for (int u = 0; u < kU; ++u) {
       const int64_t i = base + u * kBlock;
       if (i < n) d[i] = Elem<T>::from_f32(unary_op<T, OP>(v[u]));
     }
@@ -375,23 +378,33 @@ int launch_residual(void *dst, const void *x, const void *branch, const void *ls
   return check_launch("xn_residual_add");
 }
 
+template <typename T, int kU>
+void launch_unary_u(void *dst, const void *src, int64_t n, int op, bool vec, int64_t grid, cudaStream_t st) {
+  if (op == XN_UNARY_SILU) {
+    if (vec)
+      launch_k(unary_kernel<T, XN_UNARY_SILU, true, kU>, dim3(grid), dim3(kBlock), 0, st, dst, src, n);
+    else
+      launch_k(unary_kernel<T, XN_UNARY_SILU, false, kU>, dim3(grid), dim3(kBlock), 0, st, dst, src, n);
+  } else {
+    if (vec)
+      launch_k(unary_kernel<T, XN_UNARY_GELU_ERF, true, kU>, dim3(grid), dim3(kBlock), 0, st, dst, src, n);
+    else
+      launch_k(unary_kernel<T, XN_UNARY_GELU_ERF, false, kU>, dim3(grid), dim3(kBlock), 0, st, dst, src, n);
+  }
+}
+
 template <typename T>
 int launch_unary(void *dst, const void *src, int64_t n, int op, cudaStream_t st) {
   constexpr int V = Elem<T>::kVec;
   const bool vec = is_aligned16(dst) && is_aligned16(src);
   const int64_t nacc = vec ? n / V : n;
-  const int64_t grid = ceil_div(nacc > 0 ? nacc : 1, static_cast<int64_t>(kBlock) * kUnroll);
-  if (grid > 0x7fffffffLL) return fail(XN_E_INVALID, "xn_unary: too many elements");
-  if (op == XN_UNARY_SILU) {
-    if (vec)
-      launch_k(unary_kernel<T, XN_UNARY_SILU, true>, dim3(grid), dim3(kBlock), 0, st, dst, src, n);
-    else
-      launch_k(unary_kernel<T, XN_UNARY_SILU, false>, dim3(grid), dim3(kBlock), 0, st, dst, src, n);
+  const int64_t per_block = static_cast<int64_t>(kBlock) * kUnroll;
+  if (ceil_div(nacc > 0 ? nacc : 1, per_block) < sm_count()) {
+    launch_unary_u<T, 1>(dst, src, n, op, vec, ceil_div(nacc > 0 ? nacc : 1, kBlock), st);
   } else {
-    if (vec)
-      launch_k(unary_kernel<T, XN_UNARY_GELU_ERF, true>, dim3(grid), dim3(kBlock), 0, st, dst, src, n);
-    else
-      launch_k(unary_kernel<T, XN_UNARY_GELU_ERF, false>, dim3(grid), dim3(kBlock), 0, st, dst, src, n);
+    const int64_t grid = ceil_div(nacc, per_block);
+    if (grid > 0x7fffffffLL) return fail(XN_E_INVALID, "xn_unary: too many elements");
+    launch_unary_u<T, kUnroll>(dst, src, n, op, vec, grid, st);
   }
   return check_launch("xn_unary");
 }
