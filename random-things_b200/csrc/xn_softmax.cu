@@ -75,6 +75,24 @@ struct Pair<__half> {
   __device__ __forceinline__ static T2 low2(T2 v) { return __low2half2(v); }
 };
 
+// Row accesses: U = uint4 (16 bytes, every dtype) or uint32_t (one 16-bit
+// pair, for 16-bit rows of even width whose 16-byte alignment fails).
+template <typename U>
+__device__ __forceinline__ U load_access(const void *p) {
+  if constexpr (sizeof(U) == 16) {
+    return ld_stream(p);
+  } else {
+    U r;
+    asm volatile("ld.global.L1::no_allocate.u32 %0, [%1];" : "=r"(r) : "l"(p));
+    return r;
+  }
+}
+
+template <typename U>
+__device__ __forceinline__ void store_access(void *p, U v) {
+  *reinterpret_cast<U *>(p) = v;
+}
+
 // Scalar rows (widths that are not a multiple of the 16-byte vector, or
 // unaligned pointers): one row per row group, NV elements per thread held in
 // registers. Steps, in the reference's T arithmetic (cpu_backend.rs:667-689):
@@ -144,11 +162,12 @@ __global__ void __launch_bounds__(512) softmax_rows_kernel(const SoftmaxParams p
 // returns the thread's maximum. For 16-bit T, `mn` receives the minimum of the
 // thread's live elements (+inf when it has none), which tells softmax_exp
 // whether any of its exp results can be subnormal.
-template <typename T, int NV>
-__device__ __forceinline__ float softmax_prep(uint4 (&cur)[NV], int lr, int tpr, int lim, const SoftmaxParams &p,
+template <typename T, int NV, typename U>
+__device__ __forceinline__ float softmax_prep(U (&cur)[NV], int lr, int tpr, int lim, const SoftmaxParams &p,
                                               float &mn) {
-  constexpr int N = Elem<T>::kVec;
+  constexpr int N = static_cast<int>(sizeof(U) / sizeof(T));
   if constexpr (std::is_same_v<T, float>) {
+    static_assert(sizeof(U) == 16, "f32 rows use 16-byte accesses");
     mn = -INFINITY;  // not used for f32
     float m = -INFINITY;
     const float2 sc = splat2(p.scale);
@@ -230,16 +249,16 @@ __device__ __forceinline__ float softmax_prep(uint4 (&cur)[NV], int lr, int tpr,
 //
 // kSkip: vectors starting at or past `lim` hold only masked entries; they
 // become +0 without the arithmetic (the same values and sums: exp(-inf) = +0).
-template <typename T, int NV, bool kSkip>
-__device__ __forceinline__ float softmax_exp(uint4 (&cur)[NV], float mx, float mn, int lr, int tpr, int lim) {
-  constexpr int N = Elem<T>::kVec;
+template <typename T, int NV, bool kSkip, typename U>
+__device__ __forceinline__ float softmax_exp(U (&cur)[NV], float mx, float mn, int lr, int tpr, int lim) {
+  constexpr int N = static_cast<int>(sizeof(U) / sizeof(T));
   float2 s2 = make_float2(0.f, 0.f);
   if constexpr (std::is_same_v<T, float>) {
     const float2 nmx = splat2(-mx);
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
       if (kSkip && (lr + k * tpr) * N >= lim) {
-        cur[k] = make_uint4(0u, 0u, 0u, 0u);
+        cur[k] = U{};
         continue;
       }
       float2 *x2 = reinterpret_cast<float2 *>(&cur[k]);
@@ -270,12 +289,12 @@ __device__ __forceinline__ float softmax_exp(uint4 (&cur)[NV], float mx, float m
 #pragma unroll
       for (int k = 0; k < NV; ++k) {
         if (kSkip && (lr + k * tpr) * N >= lim) {
-          cur[k] = make_uint4(0u, 0u, 0u, 0u);
+          cur[k] = U{};
           continue;
         }
         T2 *w = reinterpret_cast<T2 *>(&cur[k]);
 #pragma unroll
-        for (int j = 0; j < Elem<T>::kVec / 2; ++j) {
+        for (int j = 0; j < N / 2; ++j) {
           const T2 e = exp_pair(P::to_f2(__hsub2(w[j], m2)), kind);  // T(exp(T(x - max)))
           s2 = add2_widen<T>(*reinterpret_cast<const uint32_t *>(&e), s2);
           w[j] = e;
@@ -293,10 +312,10 @@ __device__ __forceinline__ float softmax_exp(uint4 (&cur)[NV], float mx, float m
 // y = T(e / s) for the vectors below nvec, stored to the row at dst_row.
 // s >= 1 for a live row: its maximum contributes exp(0). kSkip: the +0
 // vectors at or past `lim` are stored as they are.
-template <typename T, int NV, bool kSkip>
-__device__ __forceinline__ void softmax_store(uint4 (&cur)[NV], float s, T *dst_row, int lr, int tpr, int nvec,
+template <typename T, int NV, bool kSkip, typename U>
+__device__ __forceinline__ void softmax_store(U (&cur)[NV], float s, T *dst_row, int lr, int tpr, int nvec,
                                               int lim) {
-  constexpr int N = Elem<T>::kVec;
+  constexpr int N = static_cast<int>(sizeof(U) / sizeof(T));
   const float2 rs = splat2(__frcp_rn(s)), ns = splat2(-s);
 #pragma unroll
   for (int k = 0; k < NV; ++k) {
@@ -318,7 +337,7 @@ __device__ __forceinline__ void softmax_store(uint4 (&cur)[NV], float s, T *dst_
           w[j] = P::from_f2(q.x, q.y);
         }
       }
-      st_vec(dst_row + vi * N, cur[k]);
+      store_access<U>(dst_row + vi * N, cur[k]);
     }
   }
 }
@@ -329,11 +348,11 @@ __device__ __forceinline__ void softmax_store(uint4 (&cur)[NV], float s, T *dst_
 // through the reductions and the exp / divide work. Arithmetic as
 // softmax_rows_kernel. The loop bound depends only on the block, so blocks
 // whose row groups span several warps keep their __syncthreads uniform.
-template <typename T, int NV, bool kCausal>
-__global__ void __launch_bounds__(512, NV >= 8 ? 1 : 2) softmax_pipe_kernel(const SoftmaxParams p) {
+template <typename T, int NV, bool kCausal, typename U>
+__global__ void __launch_bounds__(512, NV * sizeof(U) >= 128 ? 1 : 2) softmax_pipe_kernel(const SoftmaxParams p) {
   griddep_wait();
   griddep_release();
-  constexpr int N = Elem<T>::kVec;
+  constexpr int N = static_cast<int>(sizeof(U) / sizeof(T));
   // One scratch array per reduction of a row (see group_sum's kReuse).
   __shared__ float red_max[32], red_sum[32];
   const int tpr = p.tpr;
@@ -360,14 +379,14 @@ __global__ void __launch_bounds__(512, NV >= 8 ? 1 : 2) softmax_pipe_kernel(cons
       return cols;
     }
   };
-  auto load_row = [&](int64_t r, int lim, uint4 (&buf)[NV]) {
+  auto load_row = [&](int64_t r, int lim, U (&buf)[NV]) {
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
       const int e0 = (lr + k * tpr) * N;
-      if (e0 < lim) buf[k] = ld_stream(src + r * p.cols + e0);
+      if (e0 < lim) buf[k] = load_access<U>(src + r * p.cols + e0);
     }
   };
-  uint4 cur[NV], nxt[NV];
+  U cur[NV], nxt[NV];
   int64_t row = static_cast<int64_t>(blockIdx.x) * rpb + g;
   int q = kCausal ? static_cast<int>(row % t1) : 0;
   int lim = row_lim(row, q);
@@ -561,26 +580,26 @@ int64_t persistent_grid(K kernel, int block, int64_t needed) {
   return g < needed ? g : needed;
 }
 
-template <typename T, bool kCausal>
+template <typename T, typename U, bool kCausal>
 bool launch_softmax_pipe(const SoftmaxParams &p, int nv, int block, int64_t grid, cudaStream_t st) {
   switch (nv) {
     case 1: {
-      auto k = softmax_pipe_kernel<T, 1, kCausal>;
+      auto k = softmax_pipe_kernel<T, 1, kCausal, U>;
       launch_k(k, dim3(persistent_grid(k, block, grid)), dim3(block), 0, st, p);
       return true;
     }
     case 2: {
-      auto k = softmax_pipe_kernel<T, 2, kCausal>;
+      auto k = softmax_pipe_kernel<T, 2, kCausal, U>;
       launch_k(k, dim3(persistent_grid(k, block, grid)), dim3(block), 0, st, p);
       return true;
     }
     case 4: {
-      auto k = softmax_pipe_kernel<T, 4, kCausal>;
+      auto k = softmax_pipe_kernel<T, 4, kCausal, U>;
       launch_k(k, dim3(persistent_grid(k, block, grid)), dim3(block), 0, st, p);
       return true;
     }
     case 8: {
-      auto k = softmax_pipe_kernel<T, 8, kCausal>;
+      auto k = softmax_pipe_kernel<T, 8, kCausal, U>;
       launch_k(k, dim3(persistent_grid(k, block, grid)), dim3(block), 0, st, p);
       return true;
     }
@@ -589,11 +608,17 @@ bool launch_softmax_pipe(const SoftmaxParams &p, int nv, int block, int64_t grid
   }
 }
 
+// How a row is read: whole 16-byte vectors, 16-bit element pairs (4 bytes), or
+// single elements.
+enum class RowAccess { kScalar, kPair, kVector };
+
 // Returns false when no instantiated kernel has this shape (a dispatcher bug).
-template <typename T, bool kVector, bool kCausal>
+template <typename T, RowAccess kAccess, bool kCausal>
 bool launch_softmax_regs_c(const SoftmaxParams &p, int nv, int block, int64_t grid, cudaStream_t st) {
-  if constexpr (kVector) {
-    return launch_softmax_pipe<T, kCausal>(p, nv, block, grid, st);
+  if constexpr (kAccess == RowAccess::kVector) {
+    return launch_softmax_pipe<T, uint4, kCausal>(p, nv, block, grid, st);
+  } else if constexpr (kAccess == RowAccess::kPair && !std::is_same_v<T, float>) {
+    return launch_softmax_pipe<T, uint32_t, kCausal>(p, nv, block, grid, st);
   } else {
     switch (nv) {
       case 1:
@@ -614,10 +639,10 @@ bool launch_softmax_regs_c(const SoftmaxParams &p, int nv, int block, int64_t gr
   }
 }
 
-template <typename T, bool kVector>
+template <typename T, RowAccess kAccess>
 bool launch_softmax_regs(const SoftmaxParams &p, int nv, int block, int64_t grid, cudaStream_t st) {
-  return p.causal ? launch_softmax_regs_c<T, kVector, true>(p, nv, block, grid, st)
-                  : launch_softmax_regs_c<T, kVector, false>(p, nv, block, grid, st);
+  return p.causal ? launch_softmax_regs_c<T, kAccess, true>(p, nv, block, grid, st)
+                  : launch_softmax_regs_c<T, kAccess, false>(p, nv, block, grid, st);
 }
 
 // Shared-memory-staged rows: 8 vectors per thread (blocks of up to 512
@@ -659,7 +684,12 @@ template <typename T>
 int launch_softmax(SoftmaxParams p, cudaStream_t st) {
   constexpr int V = Elem<T>::kVec;
   const bool vec = p.cols % V == 0 && is_aligned16(p.dst) && is_aligned16(p.src);
-  const int n = vec ? V : 1;
+  // 16-bit rows that miss the 16-byte alignment (widths that are not a multiple
+  // of 8, such as 250 attention scores) but have an even width are read as
+  // element pairs: the same paired arithmetic, 4-byte accesses.
+  const bool pair = !vec && !std::is_same_v<T, float> && p.cols % 2 == 0 &&
+                    (reinterpret_cast<uintptr_t>(p.dst) & 3u) == 0 && (reinterpret_cast<uintptr_t>(p.src) & 3u) == 0;
+  const int n = vec ? V : (pair ? 2 : 1);
   const int64_t nvec = p.cols / n;
   if (vec && nvec >= staged_min_vec<T>() && nvec <= kStagedMaxVec) {
     if (p.causal)
@@ -679,14 +709,18 @@ int launch_softmax(SoftmaxParams p, cudaStream_t st) {
     // vectors sit in one warp and longer ones span half as many warps, with
     // fewer block barriers per row.
     if (vec && nvec > 128) tpr = pow2_ceil(ceil_div(nvec, 8));
+    // Pairs are 4-byte registers: 8 per thread cost little and halve the
+    // reduction steps per element.
+    if (pair) tpr = pow2_ceil(ceil_div(nvec, 8));
     const int nv = static_cast<int>(pow2_ceil(ceil_div(nvec, tpr)));
     const int block = tpr < 256 ? 256 : static_cast<int>(tpr);
     const int64_t grid = ceil_div(p.rows, block / tpr);
     if (grid > 0x7fffffffLL) return fail(XN_E_INVALID, "xn_softmax: too many rows");
     p.tpr = static_cast<int>(tpr);
     p.nvec = static_cast<int>(nvec);
-    const bool launched = vec ? launch_softmax_regs<T, true>(p, nv, block, grid, st)
-                              : launch_softmax_regs<T, false>(p, nv, block, grid, st);
+    const bool launched = vec    ? launch_softmax_regs<T, RowAccess::kVector>(p, nv, block, grid, st)
+                          : pair ? launch_softmax_regs<T, RowAccess::kPair>(p, nv, block, grid, st)
+                                 : launch_softmax_regs<T, RowAccess::kScalar>(p, nv, block, grid, st);
     if (!launched) return fail(XN_E_INVALID, "xn_softmax: internal error, no kernel for %d accesses per thread", nv);
   } else {
     if (p.rows > 0x7fffffffLL) return fail(XN_E_INVALID, "xn_softmax: too many rows");

@@ -127,11 +127,24 @@ class MimiDecoderChain:
         B, T, D = y.shape
         H, hd = cfg.num_heads, cfg.head_dim
         qkv = torch.matmul(y, w[f"layers.{l}.self_attn.in_proj_weight"].t())  # [B, T, 3D]
-        q, k = xn.rope_qk_packed(qkv, H, self.cos, self.sin, offset, interleaved=True)  # [B, T, H, hd]
-        v = qkv[..., 2 * D:].view(B, T, H, hd)
-        scores = torch.matmul(q.transpose(1, 2), k.permute(0, 2, 3, 1))  # [B, H, T, T]
-        probs = xn.attn_softmax(scores, self.scale, offset)
-        ctx = torch.matmul(probs, v.transpose(1, 2))  # [B, H, T, hd]
+        if offset == 0:
+            # One launch splits the packed projection into head-major [B, H, T, hd]
+            # Q and K (rotated, rope_i) and V: the layouts both attention GEMMs take
+            # as they are, where the narrow / transpose views below cost a
+            # contiguous copy of each. (A T-slot ring written from position 0 is
+            # the sequence in order.)
+            k = torch.empty((B, H, T, hd), dtype=qkv.dtype, device=qkv.device)
+            v = torch.empty_like(k)
+            q = xn.kv_append_rope(qkv, H, self.cos, self.sin, k, v, 0)
+            scores = torch.matmul(q, k.transpose(2, 3))  # [B, H, T, T]
+            probs = xn.attn_softmax(scores, self.scale, offset)
+            ctx = torch.matmul(probs, v)  # [B, H, T, hd]
+        else:
+            q, k = xn.rope_qk_packed(qkv, H, self.cos, self.sin, offset, interleaved=True)  # [B, T, H, hd]
+            v = qkv[..., 2 * D:].view(B, T, H, hd)
+            scores = torch.matmul(q.transpose(1, 2), k.permute(0, 2, 3, 1))  # [B, H, T, T]
+            probs = xn.attn_softmax(scores, self.scale, offset)
+            ctx = torch.matmul(probs, v.transpose(1, 2))  # [B, H, T, hd]
         return torch.matmul(ctx.transpose(1, 2).reshape(B, T, D), w[f"layers.{l}.self_attn.out_proj.weight"].t())
 
     def mlp(self, l: int, y: torch.Tensor) -> torch.Tensor:

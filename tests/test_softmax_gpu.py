@@ -13,7 +13,8 @@ DTYPES = ["f32", "bf16", "f16"]
 
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("rows,cols", [(1, 1), (2, 3), (5, 7), (64, 64), (300, 250), (64, 512), (8, 1000),
-                                       (4, 4096), (3, 16384), (2, 20000)])
+                                       (4, 4096), (3, 16384), (2, 20000), (7, 2), (33, 10), (20000, 250),
+                                       (9, 1002), (3, 8194)])
 def test_softmax(oracle, xn, cuda, dtype, rows, cols):
     r = rng(rows * 13 + cols)
     x = to_storage(randn(r, (rows, cols), 2.0), dtype)
@@ -25,7 +26,8 @@ def test_softmax(oracle, xn, cuda, dtype, rows, cols):
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("shape,offset", [((1, 16, 512, 512), 0), ((2, 3, 5, 7), 0), ((2, 3, 5, 7), 2),
                                           ((16, 16, 1, 200), 199), ((4, 8, 64, 96), 32), ((3, 9, 40), 0),
-                                          ((1, 2, 3, 17000), 16990)])
+                                          ((1, 2, 3, 17000), 16990), ((4, 8, 250, 250), 0),
+                                          ((2, 8, 37, 250), 100), ((3, 2, 11, 6), 1)])
 def test_softmax_causal(oracle, xn, cuda, dtype, shape, offset):
     r = rng(sum(shape) + offset)
     x = to_storage(randn(r, shape, 2.0), dtype)
@@ -78,10 +80,11 @@ def test_attn_softmax_scaled(oracle, xn, cuda, dtype, shape, offset, scale):
 
 
 @pytest.mark.parametrize("dtype", ["bf16", "f16"])
-@pytest.mark.parametrize("width", [8, 7])
+@pytest.mark.parametrize("width", [8, 7, 6])
 def test_softmax_exp_every_input(oracle, xn, cuda, dtype, width):
-    """Every non-positive 16-bit value v, through the vector path (rows of 8)
-    and the scalar path (rows of 7): rows [0, v, -inf, ...] have max 0, so
+    """Every non-positive 16-bit value v, through the vector path (rows of 8),
+    the pair path (rows of 6) and the scalar path (rows of 7): rows
+    [0, v, -inf, ...] have max 0, so
     e = T(exp(T(v - 0))) = T(exp(v)) and the row sum 1 + e is the same in any
     order. The outputs then equal the reference's bit for bit exactly when
     every T(exp(v)) does; the test reports how many of the 2^15 inputs differ."""
@@ -100,7 +103,7 @@ def test_softmax_exp_every_input(oracle, xn, cuda, dtype, width):
     diff = np.nonzero(np.any(got != ref, axis=1))[0]
     print(f"{dtype}: {diff.size} of {n} inputs differ")
     assert diff.size == 0, f"first differing inputs: {[hex(int(b)) for b in v[diff[:8]]]}"
-    if width == 8:
+    if width in (8, 6):
         # The same rows with the -inf columns masked by the fused causal mask
         # (one query row per slice, offset 1: columns >= 2 are not read)
         # instead of held in the data. A thread whose live values stay within
