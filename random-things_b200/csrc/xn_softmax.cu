@@ -61,6 +61,11 @@ struct Pair<__nv_bfloat16> {
   }
   // Both halves set to the low element.
   __device__ __forceinline__ static T2 low2(T2 v) { return __low2bfloat162(v); }
+  __device__ __forceinline__ static T2 high2(T2 v) { return __high2bfloat162(v); }
+  // Keeps the high element, sets the low one to -inf.
+  __device__ __forceinline__ static T2 mask_low(T2 v) {
+    return __halves2bfloat162(__float2bfloat16(-INFINITY), __high2bfloat16(v));
+  }
 };
 template <>
 struct Pair<__half> {
@@ -73,6 +78,10 @@ struct Pair<__half> {
     return __halves2half2(__low2half(v), __float2half(-INFINITY));
   }
   __device__ __forceinline__ static T2 low2(T2 v) { return __low2half2(v); }
+  __device__ __forceinline__ static T2 high2(T2 v) { return __high2half2(v); }
+  __device__ __forceinline__ static T2 mask_low(T2 v) {
+    return __halves2half2(__float2half(-INFINITY), __high2half(v));
+  }
 };
 
 // Row accesses: U = uint4 (16 bytes, every dtype) or uint32_t (one 16-bit
@@ -158,14 +167,18 @@ __global__ void __launch_bounds__(512) softmax_rows_kernel(const SoftmaxParams p
 // run as paired bf16x2 / f16x2 instructions, which round exactly once as the
 // reference's T operations do.
 
-// [x = T(x * scale)] on the live elements, -inf at and past `lim`, in place;
-// returns the thread's maximum. For 16-bit T, `mn` receives the minimum of the
+// [x = T(x * scale)] on the live elements, -inf elsewhere, in place; returns
+// the thread's maximum. Live elements are the row positions [0, lim); with
+// kWin the accesses cover an aligned window around the row and row position 0
+// sits at window position `lo` (elements before it belong to the previous
+// row), otherwise lo = 0. For 16-bit T, `mn` receives the minimum of the
 // thread's live elements (+inf when it has none), which tells softmax_exp
 // whether any of its exp results can be subnormal.
-template <typename T, int NV, typename U>
+template <typename T, int NV, typename U, bool kWin = false>
 __device__ __forceinline__ float softmax_prep(U (&cur)[NV], int lr, int tpr, int lim, const SoftmaxParams &p,
-                                              float &mn) {
+                                              float &mn, int lo = 0) {
   constexpr int N = static_cast<int>(sizeof(U) / sizeof(T));
+  const int lo_ = kWin ? lo : 0;
   if constexpr (std::is_same_v<T, float>) {
     static_assert(sizeof(U) == 16, "f32 rows use 16-byte accesses");
     mn = -INFINITY;  // not used for f32
@@ -173,18 +186,20 @@ __device__ __forceinline__ float softmax_prep(U (&cur)[NV], int lr, int tpr, int
     const float2 sc = splat2(p.scale);
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
-      const int e0 = (lr + k * tpr) * N;
+      const int a0 = (lr + k * tpr) * N - lo_;  // row position of the access's first element
       float2 *x2 = reinterpret_cast<float2 *>(&cur[k]);
       float *x = reinterpret_cast<float *>(&cur[k]);
-      if (e0 + N <= lim) {
+      if (kWin && a0 >= lim) {  // past the row (the window's spare accesses) or masked
+        x2[0] = x2[1] = splat2(-INFINITY);
+      } else if ((!kWin || a0 >= 0) && a0 + N <= lim) {
         if (p.scaled) {
           x2[0] = __fmul2_rn(x2[0], sc);
           x2[1] = __fmul2_rn(x2[1], sc);
         }
-      } else {  // the vector holding the row end, or padding: -inf past it
+      } else {  // an access holding a row end, or padding: -inf outside [0, lim)
 #pragma unroll
         for (int j = 0; j < N; ++j) {
-          if (e0 + j < lim) {
+          if ((!kWin || a0 + j >= 0) && a0 + j < lim) {
             if (p.scaled) x[j] = __fmul_rn(x[j], p.scale);
           } else {
             x[j] = -INFINITY;
@@ -202,24 +217,33 @@ __device__ __forceinline__ float softmax_prep(U (&cur)[NV], int lr, int tpr, int
     const T2 sc2 = P::splat(p.scale);
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
-      const int e0 = (lr + k * tpr) * N;
+      const int a0 = (lr + k * tpr) * N - lo_;
       T2 *w = reinterpret_cast<T2 *>(&cur[k]);
-      if (e0 + N <= lim) {
+      if (kWin && a0 >= lim) {  // past the row (the window's spare accesses) or masked
+#pragma unroll
+        for (int j = 0; j < W; ++j) w[j] = P::neg_inf();
+      } else if ((!kWin || a0 >= 0) && a0 + N <= lim) {
 #pragma unroll
         for (int j = 0; j < W; ++j) {
           if (p.scaled) w[j] = __hmul2(w[j], sc2);
           mn2 = __hmin2(mn2, w[j]);
         }
-      } else {  // the vector holding the row end, or padding: -inf past it
+      } else {  // an access holding a row end, or padding: -inf outside [0, lim)
 #pragma unroll
         for (int j = 0; j < W; ++j) {
-          if (e0 + 2 * j + 1 < lim) {
+          const int ra = a0 + 2 * j;  // row positions of the pair's elements: ra, ra + 1
+          const bool la = (!kWin || ra >= 0) && ra < lim, lb = (!kWin || ra + 1 >= 0) && ra + 1 < lim;
+          if (la && lb) {
             if (p.scaled) w[j] = __hmul2(w[j], sc2);
             mn2 = __hmin2(mn2, w[j]);
-          } else if (e0 + 2 * j < lim) {
+          } else if (la) {
             if (p.scaled) w[j] = __hmul2(w[j], sc2);
             mn2 = __hmin2(mn2, P::low2(w[j]));
             w[j] = P::mask_high(w[j]);
+          } else if (kWin && lb) {
+            if (p.scaled) w[j] = __hmul2(w[j], sc2);
+            mn2 = __hmin2(mn2, P::high2(w[j]));
+            w[j] = P::mask_low(w[j]);
           } else {
             w[j] = P::neg_inf();
           }
@@ -249,15 +273,17 @@ __device__ __forceinline__ float softmax_prep(U (&cur)[NV], int lr, int tpr, int
 //
 // kSkip: vectors starting at or past `lim` hold only masked entries; they
 // become +0 without the arithmetic (the same values and sums: exp(-inf) = +0).
-template <typename T, int NV, bool kSkip, typename U>
-__device__ __forceinline__ float softmax_exp(U (&cur)[NV], float mx, float mn, int lr, int tpr, int lim) {
+template <typename T, int NV, bool kSkip, typename U, bool kWin = false>
+__device__ __forceinline__ float softmax_exp(U (&cur)[NV], float mx, float mn, int lr, int tpr, int lim,
+                                             int lo = 0) {
   constexpr int N = static_cast<int>(sizeof(U) / sizeof(T));
+  const int lo_ = kWin ? lo : 0;
   float2 s2 = make_float2(0.f, 0.f);
   if constexpr (std::is_same_v<T, float>) {
     const float2 nmx = splat2(-mx);
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
-      if (kSkip && (lr + k * tpr) * N >= lim) {
+      if (kSkip && (lr + k * tpr) * N - lo_ >= lim) {
         cur[k] = U{};
         continue;
       }
@@ -288,7 +314,7 @@ __device__ __forceinline__ float softmax_exp(U (&cur)[NV], float mx, float mn, i
     auto run = [&](auto kind) {
 #pragma unroll
       for (int k = 0; k < NV; ++k) {
-        if (kSkip && (lr + k * tpr) * N >= lim) {
+        if (kSkip && (lr + k * tpr) * N - lo_ >= lim) {
           cur[k] = U{};
           continue;
         }
@@ -309,19 +335,23 @@ __device__ __forceinline__ float softmax_exp(U (&cur)[NV], float mx, float mn, i
   return __fadd_rn(s2.x, s2.y);
 }
 
-// y = T(e / s) for the vectors below nvec, stored to the row at dst_row.
+// y = T(e / s) for the accesses below nvec, stored to the row at dst_row.
 // s >= 1 for a live row: its maximum contributes exp(0). kSkip: the +0
-// vectors at or past `lim` are stored as they are.
-template <typename T, int NV, bool kSkip, typename U>
+// accesses at or past `lim` are stored as they are. kWin: dst_row points at
+// the window start; accesses that reach outside the row's `cols` elements
+// store only the row's own elements.
+template <typename T, int NV, bool kSkip, typename U, bool kWin = false>
 __device__ __forceinline__ void softmax_store(U (&cur)[NV], float s, T *dst_row, int lr, int tpr, int nvec,
-                                              int lim) {
+                                              int lim, int lo = 0, int cols = 0) {
   constexpr int N = static_cast<int>(sizeof(U) / sizeof(T));
+  const int lo_ = kWin ? lo : 0;
   const float2 rs = splat2(__frcp_rn(s)), ns = splat2(-s);
 #pragma unroll
   for (int k = 0; k < NV; ++k) {
     const int vi = lr + k * tpr;
     if (vi < nvec) {
-      if (kSkip && vi * N >= lim) {
+      const int a0 = vi * N - lo_;
+      if (kSkip && a0 >= lim) {
         // masked: already +0
       } else if constexpr (std::is_same_v<T, float>) {
         float2 *x2 = reinterpret_cast<float2 *>(&cur[k]);
@@ -337,7 +367,14 @@ __device__ __forceinline__ void softmax_store(U (&cur)[NV], float s, T *dst_row,
           w[j] = P::from_f2(q.x, q.y);
         }
       }
-      store_access<U>(dst_row + vi * N, cur[k]);
+      if (!kWin || (a0 >= 0 && a0 + N <= cols)) {
+        store_access<U>(dst_row + vi * N, cur[k]);
+      } else {
+        const T *el = reinterpret_cast<const T *>(&cur[k]);
+#pragma unroll
+        for (int j = 0; j < N; ++j)
+          if (a0 + j >= 0 && a0 + j < cols) dst_row[vi * N + j] = el[j];
+      }
     }
   }
 }
@@ -348,7 +385,7 @@ __device__ __forceinline__ void softmax_store(U (&cur)[NV], float s, T *dst_row,
 // through the reductions and the exp / divide work. Arithmetic as
 // softmax_rows_kernel. The loop bound depends only on the block, so blocks
 // whose row groups span several warps keep their __syncthreads uniform.
-template <typename T, int NV, bool kCausal, typename U>
+template <typename T, int NV, bool kCausal, typename U, bool kWin>
 __global__ void __launch_bounds__(512, NV * sizeof(U) >= 128 ? 1 : 2) softmax_pipe_kernel(const SoftmaxParams p) {
   griddep_wait();
   griddep_release();
@@ -370,6 +407,12 @@ __global__ void __launch_bounds__(512, NV * sizeof(U) >= 128 ? 1 : 2) softmax_pi
   const int t1 = kCausal ? static_cast<int>(p.t1) : 1;
   const int q_step = kCausal ? static_cast<int>(step % t1) : 0;
   const int off = kCausal ? static_cast<int>(p.offset < p.cols ? p.offset : p.cols) : 0;
+  // kWin: rows of a width that is not a multiple of N, read through the
+  // 16-byte-aligned window around each row. The row starting at element
+  // row * cols sits at window position lo = (row * cols) % N, carried along
+  // the walk like q. Every loaded 16-byte block holds an element of the
+  // tensor, so none reaches past the pages it occupies.
+  const int lo_step = kWin ? static_cast<int>((step % N) * (p.cols % N) % N) : 0;
   auto row_lim = [&](int64_t r, int q) -> int {
     if (r >= p.rows) return 0;
     if constexpr (kCausal) {
@@ -379,30 +422,47 @@ __global__ void __launch_bounds__(512, NV * sizeof(U) >= 128 ? 1 : 2) softmax_pi
       return cols;
     }
   };
-  auto load_row = [&](int64_t r, int lim, U (&buf)[NV]) {
+  // lim = 0 marks a row past the end: nothing is loaded (with a window, e0 -
+  // lo < 0 would otherwise admit its first access).
+  auto load_row = [&](int64_t r, int lim, int lo, U (&buf)[NV]) {
+    if (lim == 0) return;
+    const T *w = src + r * p.cols - lo;
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
       const int e0 = (lr + k * tpr) * N;
-      if (e0 < lim) buf[k] = load_access<U>(src + r * p.cols + e0);
+      if (e0 - lo < lim) buf[k] = load_access<U>(w + e0);
     }
   };
   U cur[NV], nxt[NV];
   int64_t row = static_cast<int64_t>(blockIdx.x) * rpb + g;
   int q = kCausal ? static_cast<int>(row % t1) : 0;
+  int lo = kWin ? static_cast<int>((row % N) * (p.cols % N) % N) : 0;
   int lim = row_lim(row, q);
-  load_row(row, lim, cur);
+  load_row(row, lim, lo, cur);
   for (int64_t base = static_cast<int64_t>(blockIdx.x) * rpb; base < p.rows; base += step, row += step) {
     int qn = q + q_step;
     if (qn >= t1) qn -= t1;
+    int lon = lo + lo_step;
+    if (lon >= N) lon -= N;
     const int lim_next = row_lim(row + step, qn);
-    load_row(row + step, lim_next, nxt);  // prefetch the next row of this group
+    load_row(row + step, lim_next, lon, nxt);  // prefetch the next row of this group
     float mn;
-    const float mx = group_max<false>(softmax_prep<T, NV>(cur, lr, tpr, lim, p, mn), tpr, red_max);
-    const float s = group_sum<false>(softmax_exp<T, NV, kCausal>(cur, mx, mn, lr, tpr, lim), tpr, red_sum);
-    if (row < p.rows) softmax_store<T, NV, kCausal>(cur, s, dst + row * p.cols, lr, tpr, p.nvec, lim);
+    const float mx = group_max<false>(softmax_prep<T, NV, U, kWin>(cur, lr, tpr, lim, p, mn, lo), tpr, red_max);
+    // Window rows skip the arithmetic of their spare accesses like masked ones.
+    const float s = group_sum<false>(softmax_exp<T, NV, kCausal || kWin, U, kWin>(cur, mx, mn, lr, tpr, lim, lo),
+                                     tpr, red_sum);
+    if (row < p.rows) {
+      if constexpr (kWin) {
+        softmax_store<T, NV, true, U, true>(cur, s, dst + row * p.cols - lo, lr, tpr, (lo + cols + N - 1) / N, lim,
+                                            lo, cols);
+      } else {
+        softmax_store<T, NV, kCausal, U>(cur, s, dst + row * p.cols, lr, tpr, p.nvec, lim);
+      }
+    }
 #pragma unroll
     for (int k = 0; k < NV; ++k) cur[k] = nxt[k];
     q = qn;
+    lo = lon;
     lim = lim_next;
   }
 }
@@ -580,26 +640,26 @@ int64_t persistent_grid(K kernel, int block, int64_t needed) {
   return g < needed ? g : needed;
 }
 
-template <typename T, typename U, bool kCausal>
+template <typename T, typename U, bool kCausal, bool kWin = false>
 bool launch_softmax_pipe(const SoftmaxParams &p, int nv, int block, int64_t grid, cudaStream_t st) {
   switch (nv) {
     case 1: {
-      auto k = softmax_pipe_kernel<T, 1, kCausal, U>;
+      auto k = softmax_pipe_kernel<T, 1, kCausal, U, kWin>;
       launch_k(k, dim3(persistent_grid(k, block, grid)), dim3(block), 0, st, p);
       return true;
     }
     case 2: {
-      auto k = softmax_pipe_kernel<T, 2, kCausal, U>;
+      auto k = softmax_pipe_kernel<T, 2, kCausal, U, kWin>;
       launch_k(k, dim3(persistent_grid(k, block, grid)), dim3(block), 0, st, p);
       return true;
     }
     case 4: {
-      auto k = softmax_pipe_kernel<T, 4, kCausal, U>;
+      auto k = softmax_pipe_kernel<T, 4, kCausal, U, kWin>;
       launch_k(k, dim3(persistent_grid(k, block, grid)), dim3(block), 0, st, p);
       return true;
     }
     case 8: {
-      auto k = softmax_pipe_kernel<T, 8, kCausal, U>;
+      auto k = softmax_pipe_kernel<T, 8, kCausal, U, kWin>;
       launch_k(k, dim3(persistent_grid(k, block, grid)), dim3(block), 0, st, p);
       return true;
     }
@@ -608,15 +668,18 @@ bool launch_softmax_pipe(const SoftmaxParams &p, int nv, int block, int64_t grid
   }
 }
 
-// How a row is read: whole 16-byte vectors, 16-bit element pairs (4 bytes), or
-// single elements.
-enum class RowAccess { kScalar, kPair, kVector };
+// How a row is read: whole 16-byte vectors, 16-byte vectors of the aligned
+// window around a row whose width is not a multiple of the vector, 16-bit
+// element pairs (4 bytes), or single elements.
+enum class RowAccess { kScalar, kPair, kWindow, kVector };
 
 // Returns false when no instantiated kernel has this shape (a dispatcher bug).
 template <typename T, RowAccess kAccess, bool kCausal>
 bool launch_softmax_regs_c(const SoftmaxParams &p, int nv, int block, int64_t grid, cudaStream_t st) {
   if constexpr (kAccess == RowAccess::kVector) {
     return launch_softmax_pipe<T, uint4, kCausal>(p, nv, block, grid, st);
+  } else if constexpr (kAccess == RowAccess::kWindow) {
+    return launch_softmax_pipe<T, uint4, kCausal, true>(p, nv, block, grid, st);
   } else if constexpr (kAccess == RowAccess::kPair && !std::is_same_v<T, float>) {
     return launch_softmax_pipe<T, uint32_t, kCausal>(p, nv, block, grid, st);
   } else {
@@ -684,13 +747,18 @@ template <typename T>
 int launch_softmax(SoftmaxParams p, cudaStream_t st) {
   constexpr int V = Elem<T>::kVec;
   const bool vec = p.cols % V == 0 && is_aligned16(p.dst) && is_aligned16(p.src);
-  // 16-bit rows that miss the 16-byte alignment (widths that are not a multiple
-  // of 8, such as 250 attention scores) but have an even width are read as
-  // element pairs: the same paired arithmetic, 4-byte accesses.
-  const bool pair = !vec && !std::is_same_v<T, float> && p.cols % 2 == 0 &&
+  // Rows whose width is not a multiple of the vector (such as 250 attention
+  // scores) in 16-byte-aligned tensors: 16-byte accesses over the aligned
+  // window around each row, one access more than a vector row.
+  const bool win = !vec && is_aligned16(p.dst) && is_aligned16(p.src) && p.cols >= V;
+  // 16-bit rows of even width in tensors aligned to 4 bytes only: element
+  // pairs, the same paired arithmetic with 4-byte accesses.
+  const bool pair = !vec && !win && !std::is_same_v<T, float> && p.cols % 2 == 0 &&
                     (reinterpret_cast<uintptr_t>(p.dst) & 3u) == 0 && (reinterpret_cast<uintptr_t>(p.src) & 3u) == 0;
-  const int n = vec ? V : (pair ? 2 : 1);
-  const int64_t nvec = p.cols / n;
+  const int n = (vec || win) ? V : (pair ? 2 : 1);
+  // A window row spans up to ceil((V - 1 + cols) / V) vectors (its first
+  // element at window position V - 1 at worst).
+  const int64_t nvec = win ? (p.cols + 2 * V - 2) / V : p.cols / n;
   if (vec && nvec >= staged_min_vec<T>() && nvec <= kStagedMaxVec) {
     if (p.causal)
       launch_softmax_staged<T, true>(p, nvec, st);
@@ -708,7 +776,7 @@ int launch_softmax(SoftmaxParams p, cudaStream_t st) {
     // vectors per thread (the 128-register shape), so rows of up to 256
     // vectors sit in one warp and longer ones span half as many warps, with
     // fewer block barriers per row.
-    if (vec && nvec > 128) tpr = pow2_ceil(ceil_div(nvec, 8));
+    if ((vec || win) && nvec > 128) tpr = pow2_ceil(ceil_div(nvec, 8));
     // Pairs are 4-byte registers: 8 per thread cost little and halve the
     // reduction steps per element.
     if (pair) tpr = pow2_ceil(ceil_div(nvec, 8));
@@ -719,6 +787,7 @@ int launch_softmax(SoftmaxParams p, cudaStream_t st) {
     p.tpr = static_cast<int>(tpr);
     p.nvec = static_cast<int>(nvec);
     const bool launched = vec    ? launch_softmax_regs<T, RowAccess::kVector>(p, nv, block, grid, st)
+                          : win  ? launch_softmax_regs<T, RowAccess::kWindow>(p, nv, block, grid, st)
                           : pair ? launch_softmax_regs<T, RowAccess::kPair>(p, nv, block, grid, st)
                                  : launch_softmax_regs<T, RowAccess::kScalar>(p, nv, block, grid, st);
     if (!launched) return fail(XN_E_INVALID, "xn_softmax: internal error, no kernel for %d accesses per thread", nv);

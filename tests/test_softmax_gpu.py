@@ -80,10 +80,11 @@ def test_attn_softmax_scaled(oracle, xn, cuda, dtype, shape, offset, scale):
 
 
 @pytest.mark.parametrize("dtype", ["bf16", "f16"])
-@pytest.mark.parametrize("width", [8, 7, 6])
+@pytest.mark.parametrize("width", [8, 7, 6, 10])
 def test_softmax_exp_every_input(oracle, xn, cuda, dtype, width):
     """Every non-positive 16-bit value v, through the vector path (rows of 8),
-    the pair path (rows of 6) and the scalar path (rows of 7): rows
+    the window path (rows of 10, starting at every offset within a 16-byte
+    vector), the pair path (rows of 6) and the scalar path (rows of 7): rows
     [0, v, -inf, ...] have max 0, so
     e = T(exp(T(v - 0))) = T(exp(v)) and the row sum 1 + e is the same in any
     order. The outputs then equal the reference's bit for bit exactly when
@@ -103,7 +104,7 @@ def test_softmax_exp_every_input(oracle, xn, cuda, dtype, width):
     diff = np.nonzero(np.any(got != ref, axis=1))[0]
     print(f"{dtype}: {diff.size} of {n} inputs differ")
     assert diff.size == 0, f"first differing inputs: {[hex(int(b)) for b in v[diff[:8]]]}"
-    if width in (8, 6):
+    if width in (8, 6, 10):
         # The same rows with the -inf columns masked by the fused causal mask
         # (one query row per slice, offset 1: columns >= 2 are not read)
         # instead of held in the data. A thread whose live values stay within
@@ -118,7 +119,8 @@ def test_softmax_exp_every_input(oracle, xn, cuda, dtype, width):
 
 
 @pytest.mark.parametrize("dtype,rows,cols", [("bf16", 6000, 4096), ("bf16", 13500, 2048), ("f16", 3000, 8192),
-                                             ("bf16", 700, 32768), ("f32", 1100, 16384), ("f32", 5000, 1024)])
+                                             ("bf16", 700, 32768), ("f32", 1100, 16384), ("f32", 5000, 1024),
+                                             ("bf16", 30000, 250), ("f32", 30000, 250), ("f16", 4000, 1003)])
 def test_softmax_many_rows_per_block(oracle, xn, cuda, dtype, rows, cols):
     """Enough rows that every block of the persistent kernels walks several:
     each shared-memory stage buffer of the staged kernel is refilled more than
