@@ -494,7 +494,7 @@ def sweep(torch, xn, device, widths, rows_list, dtypes, reps: int, mem_cap_gb: f
     flush_clean = torch.zeros(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
     out = []
     for dname in dtypes:
-        dt = {"f32": torch.float32, "bf16": torch.bfloat16}[dname]
+        dt = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}[dname]
         s = 4 if dname == "f32" else 2
         for op in ops:
             for cols in widths:
@@ -777,7 +777,7 @@ def main() -> int:
     ap.add_argument("--sweep", action="store_true", help="run the per-op bandwidth sweep instead (JSON per point)")
     ap.add_argument("--sweep-widths", default="256,1024,4096,16384")
     ap.add_argument("--sweep-rows", default="1024,16384,262144,1048576")
-    ap.add_argument("--sweep-dtypes", default="f32,bf16")
+    ap.add_argument("--sweep-dtypes", default="f32,bf16", help="comma-separated subset of f32, bf16, f16")
     ap.add_argument("--sweep-mem-gb", type=float, default=48.0)
     ap.add_argument("--sweep-ops", default=",".join(SWEEP_OPS),
                     help="comma-separated subset of " + ",".join(SWEEP_OPS + SWEEP_EXTRA_OPS))
