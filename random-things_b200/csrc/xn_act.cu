@@ -157,9 +157,9 @@ __device__ __forceinline__ float unary_op(float x) {
 constexpr int kBlock = 256;
 constexpr int kUnroll = 4;
 
-// kU accesses per thread: kU for large tensors; 1 for tensors smaller
-// than one wave of the kU grid, where the per-thread chain of work, not
-// bandwidth, sets the time.
+// kU accesses per thread: kUnroll for large tensors; 1 for tensors whose
+// one-access grid fits in one wave (8 blocks per SM), where the per-thread
+// chain of work, not bandwidth, sets the time.
 template <typename T, int OP, bool kVector, int kU>
 __global__ void __launch_bounds__(kBlock) unary_kernel(void *dst, const void *src, int64_t n) {
   griddep_wait();
@@ -399,7 +399,7 @@ int launch_unary(void *dst, const void *src, int64_t n, int op, cudaStream_t st)
   const bool vec = is_aligned16(dst) && is_aligned16(src);
   const int64_t nacc = vec ? n / V : n;
   const int64_t per_block = static_cast<int64_t>(kBlock) * kUnroll;
-  if (ceil_div(nacc > 0 ? nacc : 1, per_block) < sm_count()) {
+  if (ceil_div(nacc > 0 ? nacc : 1, static_cast<int64_t>(kBlock)) <= static_cast<int64_t>(sm_count()) * 8) {
     launch_unary_u<T, 1>(dst, src, n, op, vec, ceil_div(nacc > 0 ? nacc : 1, kBlock), st);
   } else {
     const int64_t grid = ceil_div(nacc, per_block);
