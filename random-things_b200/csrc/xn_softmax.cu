@@ -189,7 +189,7 @@ __device__ __forceinline__ float softmax_prep(U (&cur)[NV], int lr, int tpr, int
       const int a0 = (lr + k * tpr) * N - lo_;  // row position of the access's first element
       float2 *x2 = reinterpret_cast<float2 *>(&cur[k]);
       float *x = reinterpret_cast<float *>(&cur[k]);
-      if (kWin && a0 >= lim) {  // past the row (the window's spare accesses) or masked
+      if (a0 >= lim) {  // masked, padding, or past the row (a window's spare accesses)
         x2[0] = x2[1] = splat2(-INFINITY);
       } else if ((!kWin || a0 >= 0) && a0 + N <= lim) {
         if (p.scaled) {
@@ -219,7 +219,7 @@ __device__ __forceinline__ float softmax_prep(U (&cur)[NV], int lr, int tpr, int
     for (int k = 0; k < NV; ++k) {
       const int a0 = (lr + k * tpr) * N - lo_;
       T2 *w = reinterpret_cast<T2 *>(&cur[k]);
-      if (kWin && a0 >= lim) {  // past the row (the window's spare accesses) or masked
+      if (a0 >= lim) {  // masked, padding, or past the row (a window's spare accesses)
 #pragma unroll
         for (int j = 0; j < W; ++j) w[j] = P::neg_inf();
       } else if ((!kWin || a0 >= 0) && a0 + N <= lim) {
@@ -483,7 +483,7 @@ __global__ void __launch_bounds__(512, NV * sizeof(U) >= 128 ? 1 : 2) softmax_pi
 constexpr int kMaxStages = 4;
 constexpr uint32_t kStageWaitLimit = 1u << 22;
 
-template <typename T, int NV, bool kCausal>
+template <typename T, int NV, bool kCausal, bool kSkip>
 __global__ void __launch_bounds__(NV >= 8 ? 512 : 1024) softmax_staged_kernel(const SoftmaxParams p, int stages,
                                                                               int stage_bytes) {
   griddep_wait();
@@ -583,10 +583,11 @@ __global__ void __launch_bounds__(NV >= 8 ? 512 : 1024) softmax_staged_kernel(co
     }
     float mx = red_max[0];
     for (int w = 1; w < warps; ++w) mx = fmaxf(mx, red_max[w]);
-    // Masked vectors go through the arithmetic here (exp(-inf) = 0): wide
-    // rows are mostly live, and the per-vector skip measured slower.
-    const float sum = group_sum<false>(softmax_exp<T, NV, false>(cur, mx, mn, tid, tpr, lim), tpr, red_sum);
-    softmax_store<T, NV, false>(cur, sum, dst + row * p.cols, tid, tpr, p.nvec, lim);
+    // kSkip: masked vectors skip the arithmetic (they become +0 directly). It
+    // pays off when rows are mostly masked and costs about 5% when they are
+    // mostly live; the launcher picks it from the mask's average live share.
+    const float sum = group_sum<false>(softmax_exp<T, NV, kSkip>(cur, mx, mn, tid, tpr, lim), tpr, red_sum);
+    softmax_store<T, NV, kSkip>(cur, sum, dst + row * p.cols, tid, tpr, p.nvec, lim);
     if (++s == stages) {
       s = 0;
       parity ^= 1u;
@@ -710,7 +711,7 @@ bool launch_softmax_regs(const SoftmaxParams &p, int nv, int block, int64_t grid
 
 // Shared-memory-staged rows: 8 vectors per thread (blocks of up to 512
 // threads), two stage buffers. Used, as measured on B200, for 16-bit rows of
-// 512 to 4096 vectors (4096 to 32768 elements) and f32 rows of 2049 to 4096
+// 256 to 4096 vectors (2048 to 32768 elements) and f32 rows of 2049 to 4096
 // vectors (8196 to 16384 elements); narrower rows run as fast or faster in the
 // register-prefetching kernel, and 4096 vectors (64 KB) is the widest row the
 // 512 threads hold.
@@ -723,12 +724,12 @@ static_assert(kStages <= kMaxStages && kStages * kStagedMaxVec * 16 <= 200 * 102
 
 template <typename T>
 constexpr int64_t staged_min_vec() {
-  return std::is_same_v<T, float> ? 2049 : 512;
+  return std::is_same_v<T, float> ? 2049 : 256;
 }
 
-template <typename T, bool kCausal>
+template <typename T, bool kCausal, bool kSkip>
 void launch_softmax_staged(SoftmaxParams p, int64_t nvec, cudaStream_t st) {
-  auto kernel = softmax_staged_kernel<T, kStagedNv, kCausal>;
+  auto kernel = softmax_staged_kernel<T, kStagedNv, kCausal, kSkip>;
   const int block = static_cast<int>(ceil_div(ceil_div(nvec, kStagedNv), 32) * 32);
   const int stage_bytes = static_cast<int>(ceil_div(nvec * 16, 128) * 128);
   const size_t smem = static_cast<size_t>(kStages) * stage_bytes;
@@ -760,10 +761,16 @@ int launch_softmax(SoftmaxParams p, cudaStream_t st) {
   // element at window position V - 1 at worst).
   const int64_t nvec = win ? (p.cols + 2 * V - 2) / V : p.cols / n;
   if (vec && nvec >= staged_min_vec<T>() && nvec <= kStagedMaxVec) {
-    if (p.causal)
-      launch_softmax_staged<T, true>(p, nvec, st);
+    // Causal rows hold offset + q + 1 live columns, q = 0 .. t1 - 1: skip the
+    // masked vectors when fewer than 3/4 of the columns are live on average
+    // (square prefill masks are half live).
+    const bool mostly_masked = p.causal && 4 * (2 * p.offset + p.t1 + 1) < 3 * 2 * p.cols;
+    if (!p.causal)
+      launch_softmax_staged<T, false, false>(p, nvec, st);
+    else if (mostly_masked)
+      launch_softmax_staged<T, true, true>(p, nvec, st);
     else
-      launch_softmax_staged<T, false>(p, nvec, st);
+      launch_softmax_staged<T, true, false>(p, nvec, st);
     return check_launch("xn_softmax");
   }
   // exp needs more registers than the norms: groups of up to 512 threads with

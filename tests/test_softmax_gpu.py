@@ -136,6 +136,19 @@ def test_softmax_many_rows_per_block(oracle, xn, cuda, dtype, rows, cols):
     assert np.array_equal(from_device(X, dtype), from_device(Y, dtype))
 
 
+@pytest.mark.parametrize("dtype,shape,offset", [("bf16", (2, 2, 2048, 2048), 0), ("f16", (1, 3, 300, 4096), 7),
+                                                ("f32", (1, 2, 1024, 9000), 0)])
+def test_softmax_causal_mostly_masked(oracle, xn, cuda, dtype, shape, offset):
+    """Wide causal rows with fewer than 3/4 of their columns live on average
+    (square prefill masks): the shared-memory-staged kernel then skips the
+    arithmetic of masked vectors."""
+    r = rng(sum(shape) + offset)
+    x = to_storage(randn(r, shape, 2.0), dtype)
+    ref = oracle.softmax_causal(x, offset, dtype)
+    Y = from_device(xn.softmax_causal(to_device(x, dtype, cuda), offset), dtype)
+    assert_close(Y, ref, dtype, f"softmax_causal {dtype} {shape} off={offset}")
+
+
 @pytest.mark.parametrize("dtype", ["bf16", "f32"])
 def test_softmax_causal_many_rows(oracle, xn, cuda, dtype):
     """Causal rows of varying length (offset + i + 1 of 4096 columns, most of
