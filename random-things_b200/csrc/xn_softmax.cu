@@ -17,6 +17,8 @@
 // a three-pass kernel.
 #include <math.h>
 
+#include <cooperative_groups.h>
+
 #include <type_traits>
 
 #include "xn_common.cuh"
@@ -596,6 +598,67 @@ __global__ void __launch_bounds__(NV >= 8 ? 512 : 1024) softmax_staged_kernel(co
   }
 }
 
+// Vector rows wider than the staged kernel's 64 KB: one thread-block cluster
+// of up to kMaxCluster blocks per row (grid.x = rows * cluster size). Block
+// rank r holds vectors [r * per, (r + 1) * per) of the row in registers
+// (per = blockDim.x * NV), so the row crosses HBM once. Each block reduces its
+// part, writes the partial max (then sum) into a slot of every block's shared
+// memory through distributed shared memory, and after a cluster barrier
+// combines the slots in rank order (deterministic). Arithmetic as
+// softmax_pipe_kernel. Every thread reaches both cluster barriers, and after
+// the second one blocks read only their own shared memory, so a block may
+// exit while the others finish. (A persistent form that walks rows measured
+// slower: each row's cluster barriers, which release prior memory accesses,
+// then wait for the previous row's global stores.)
+constexpr int kMaxCluster = 8;
+constexpr int kClusterThreads = 512;
+constexpr int kClusterNv = 4;
+
+template <typename T, int NV, bool kCausal>
+__global__ void __launch_bounds__(kClusterThreads, 2) softmax_cluster_kernel(const SoftmaxParams p) {
+  griddep_wait();
+  griddep_release();
+  namespace cg = cooperative_groups;
+  constexpr int N = Elem<T>::kVec;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int csize = static_cast<int>(cluster.num_blocks());
+  const int rank = static_cast<int>(cluster.block_rank());
+  __shared__ float red_max[32], red_sum[32];
+  __shared__ float cmax[kMaxCluster], csum[kMaxCluster];
+  const int tid = threadIdx.x, tpr = blockDim.x;
+  const int64_t row = blockIdx.x / csize;
+  const int v0 = rank * tpr * NV;  // first vector of this block
+  const int cols = static_cast<int>(p.cols);
+  int lim = cols;
+  if constexpr (kCausal) {
+    const int64_t l = (p.offset < p.cols ? p.offset : p.cols) + row % p.t1 + 1;
+    lim = l < cols ? static_cast<int>(l) : cols;
+  }
+  const T *src = static_cast<const T *>(p.src) + row * p.cols;
+  uint4 cur[NV];
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int e0 = (v0 + tid + k * tpr) * N;
+    if (e0 < lim) cur[k] = ld_stream(src + e0);
+  }
+  float mn;
+  const float m = group_max<false>(softmax_prep<T, NV>(cur, v0 + tid, tpr, lim, p, mn), tpr, red_max);
+  if (tid == 0) {
+    for (int r = 0; r < csize; ++r) *cluster.map_shared_rank(&cmax[rank], r) = m;
+  }
+  cluster.sync();
+  float mx = cmax[0];
+  for (int r = 1; r < csize; ++r) mx = fmaxf(mx, cmax[r]);
+  const float s = group_sum<false>(softmax_exp<T, NV, kCausal>(cur, mx, mn, v0 + tid, tpr, lim), tpr, red_sum);
+  if (tid == 0) {
+    for (int r = 0; r < csize; ++r) *cluster.map_shared_rank(&csum[rank], r) = s;
+  }
+  cluster.sync();
+  float sum = csum[0];
+  for (int r = 1; r < csize; ++r) sum = __fadd_rn(sum, csum[r]);
+  softmax_store<T, NV, kCausal>(cur, sum, static_cast<T *>(p.dst) + row * p.cols, v0 + tid, tpr, p.nvec, lim);
+}
+
 // Rows wider than the register budget: one block per row, three passes; the
 // second pass writes T(exp(...)) to dst and the third rescales it in place.
 template <typename T>
@@ -744,6 +807,27 @@ void launch_softmax_staged(SoftmaxParams p, int64_t nvec, cudaStream_t st) {
   launch_k(kernel, dim3(static_cast<unsigned>(grid)), dim3(block), smem, st, p, kStages, stage_bytes);
 }
 
+// One cluster of `csize` blocks per row, launched with programmatic dependent
+// launch allowed as launch_k does.
+template <auto kKernel>
+void launch_softmax_cluster(const SoftmaxParams &p, int csize, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(p.rows * csize));
+  cfg.blockDim = dim3(kClusterThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(csize);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  cudaLaunchKernelEx(&cfg, kKernel, p);
+}
+
 template <typename T>
 int launch_softmax(SoftmaxParams p, cudaStream_t st) {
   constexpr int V = Elem<T>::kVec;
@@ -798,6 +882,15 @@ int launch_softmax(SoftmaxParams p, cudaStream_t st) {
                           : pair ? launch_softmax_regs<T, RowAccess::kPair>(p, nv, block, grid, st)
                                  : launch_softmax_regs<T, RowAccess::kScalar>(p, nv, block, grid, st);
     if (!launched) return fail(XN_E_INVALID, "xn_softmax: internal error, no kernel for %d accesses per thread", nv);
+  } else if (vec && nvec <= static_cast<int64_t>(kMaxCluster) * kClusterThreads * kClusterNv) {
+    int csize = 2;
+    while (static_cast<int64_t>(csize) * kClusterThreads * kClusterNv < nvec) csize *= 2;
+    if (p.rows * csize > 0x7fffffffLL) return fail(XN_E_INVALID, "xn_softmax: too many rows");
+    p.nvec = static_cast<int>(nvec);
+    if (p.causal)
+      launch_softmax_cluster<softmax_cluster_kernel<T, kClusterNv, true>>(p, csize, st);
+    else
+      launch_softmax_cluster<softmax_cluster_kernel<T, kClusterNv, false>>(p, csize, st);
   } else {
     if (p.rows > 0x7fffffffLL) return fail(XN_E_INVALID, "xn_softmax: too many rows");
     launch_k(softmax_loop_kernel<T>, dim3(static_cast<unsigned>(p.rows)), dim3(1024), 0, st, p);
