@@ -143,7 +143,9 @@ def test_every_kernel_waits_for_its_predecessor_first():
     """Launches allow programmatic dependent launch, so a kernel may start
     while the previous kernel of the stream drains. Every kernel must
     therefore begin with griddep_wait() (nothing read before it), and every
-    launch must go through launch_k (no bare <<<...>>> launches)."""
+    launch must go through launch_k or another cudaLaunchKernelEx launcher that
+    sets the same attribute (the softmax's cluster launch); no bare <<<...>>>
+    launches."""
     import re
     from pathlib import Path
 
@@ -152,6 +154,8 @@ def test_every_kernel_waits_for_its_predecessor_first():
     for f in sorted(csrc.glob("*.cu")):
         src = f.read_text()
         assert "<<<" not in src, f"{f.name}: bare <<<>>> launch"
+        if "cudaLaunchKernelEx" in src:
+            assert "cudaLaunchAttributeProgrammaticStreamSerialization" in src, f"{f.name}: launch without PDL"
         for m in re.finditer(r"__global__", src):
             body = src[src.index("{", m.end()) + 1:].lstrip()
             assert body.startswith("griddep_wait();"), f"{f.name}: kernel at offset {m.start()} does not wait first"
