@@ -276,6 +276,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
   // Phase 1: scores T(T(q.k) * T(scale)), -inf where masked.
   const float scale_t = Elem<T>::round(p.scale);
   float m = -INFINITY;
+#pragma unroll 2
   for (int64_t j = tid; j < kv_len; j += kAttnThreads) {
     float s = -INFINITY;
     if (j < nvis) {

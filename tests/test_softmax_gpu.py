@@ -49,8 +49,11 @@ def test_softmax_widest_rows(oracle, xn, cuda, dtype, rows, cols):
     r = rng(rows + cols)
     x = to_storage(randn(r, (rows, cols), 2.0), dtype)
     ref = oracle.softmax(x, dtype)
-    got = from_device(xn.softmax(to_device(x, dtype, cuda)), dtype)
-    assert_softmax_close(got, ref, dtype, cols, f"softmax {dtype} {rows}x{cols}")
+    X = to_device(x, dtype, cuda)
+    Y = xn.softmax(X)
+    assert_softmax_close(from_device(Y, dtype), ref, dtype, cols, f"softmax {dtype} {rows}x{cols}")
+    xn.softmax_(X, X)  # in place (dst == src), bit for bit the same
+    assert np.array_equal(from_device(X, dtype), from_device(Y, dtype))
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
