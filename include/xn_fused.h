@@ -201,7 +201,9 @@ XN_API int xn_swiglu(void *dst, const void *gate, const void *up, int64_t rows, 
  * replaces the Backend::apply_causality_mask that precedes it
  * (backend.rs:150-156, cpu_backend.rs:647-665; callers mimi.rs:1365-1368,
  * llama.rs:201-202). rows = bh * t1; row r is query (r % t1) and its columns
- * j > offset + (r % t1) give exactly 0 (they are not read).
+ * j > offset + (r % t1) give exactly 0 (they are not read). dst may equal src
+ * (in place). Any width and alignment; 16-byte-aligned tensors run the vector
+ * kernels, also for widths that are not a multiple of the vector.
  */
 XN_API int xn_softmax(void *dst, const void *src, int64_t rows, int64_t cols,
                int causal, int64_t t1, int64_t offset, int dtype, void *stream);
