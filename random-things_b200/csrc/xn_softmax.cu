@@ -176,7 +176,10 @@ __global__ void __launch_bounds__(512) softmax_rows_kernel(const SoftmaxParams p
 // row), otherwise lo = 0. For 16-bit T, `mn` receives the minimum of the
 // thread's live elements (+inf when it has none), which tells softmax_exp
 // whether any of its exp results can be subnormal.
-template <typename T, int NV, typename U, bool kWin = false>
+// kDead: accesses wholly past `lim` (common with a causal mask or a window)
+// are set to -inf at once; otherwise the rare padding access takes the
+// per-element path, which keeps the check off the common path.
+template <typename T, int NV, typename U, bool kWin = false, bool kDead = false>
 __device__ __forceinline__ float softmax_prep(U (&cur)[NV], int lr, int tpr, int lim, const SoftmaxParams &p,
                                               float &mn, int lo = 0) {
   constexpr int N = static_cast<int>(sizeof(U) / sizeof(T));
@@ -191,7 +194,7 @@ __device__ __forceinline__ float softmax_prep(U (&cur)[NV], int lr, int tpr, int
       const int a0 = (lr + k * tpr) * N - lo_;  // row position of the access's first element
       float2 *x2 = reinterpret_cast<float2 *>(&cur[k]);
       float *x = reinterpret_cast<float *>(&cur[k]);
-      if (a0 >= lim) {  // masked, padding, or past the row (a window's spare accesses)
+      if (kDead && a0 >= lim) {  // masked, or past the row (a window's spare accesses)
         x2[0] = x2[1] = splat2(-INFINITY);
       } else if ((!kWin || a0 >= 0) && a0 + N <= lim) {
         if (p.scaled) {
@@ -221,7 +224,7 @@ __device__ __forceinline__ float softmax_prep(U (&cur)[NV], int lr, int tpr, int
     for (int k = 0; k < NV; ++k) {
       const int a0 = (lr + k * tpr) * N - lo_;
       T2 *w = reinterpret_cast<T2 *>(&cur[k]);
-      if (a0 >= lim) {  // masked, padding, or past the row (a window's spare accesses)
+      if (kDead && a0 >= lim) {  // masked, or past the row (a window's spare accesses)
 #pragma unroll
         for (int j = 0; j < W; ++j) w[j] = P::neg_inf();
       } else if ((!kWin || a0 >= 0) && a0 + N <= lim) {
@@ -424,10 +427,11 @@ __global__ void __launch_bounds__(512, NV * sizeof(U) >= 128 ? 1 : 2) softmax_pi
       return cols;
     }
   };
-  // lim = 0 marks a row past the end: nothing is loaded (with a window, e0 -
-  // lo < 0 would otherwise admit its first access).
+  // lim = 0 marks a row past the end: nothing is loaded (e0 < lim already
+  // excludes every access without a window; with one, e0 - lo < 0 would admit
+  // the first).
   auto load_row = [&](int64_t r, int lim, int lo, U (&buf)[NV]) {
-    if (lim == 0) return;
+    if (kWin && lim == 0) return;
     const T *w = src + r * p.cols - lo;
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
@@ -449,7 +453,8 @@ __global__ void __launch_bounds__(512, NV * sizeof(U) >= 128 ? 1 : 2) softmax_pi
     const int lim_next = row_lim(row + step, qn);
     load_row(row + step, lim_next, lon, nxt);  // prefetch the next row of this group
     float mn;
-    const float mx = group_max<false>(softmax_prep<T, NV, U, kWin>(cur, lr, tpr, lim, p, mn, lo), tpr, red_max);
+    const float mx =
+        group_max<false>(softmax_prep<T, NV, U, kWin, kCausal || kWin>(cur, lr, tpr, lim, p, mn, lo), tpr, red_max);
     // Window rows skip the arithmetic of their spare accesses like masked ones.
     const float s = group_sum<false>(softmax_exp<T, NV, kCausal || kWin, U, kWin>(cur, mx, mn, lr, tpr, lim, lo),
                                      tpr, red_sum);
@@ -552,7 +557,7 @@ __global__ void __launch_bounds__(NV >= 8 ? 512 : 1024) softmax_staged_kernel(co
       if (vi * N < lim) cur[k] = buf[vi];
     }
     float mn;
-    float m = softmax_prep<T, NV>(cur, tid, tpr, lim, p, mn);
+    float m = softmax_prep<T, NV, uint4, false, kSkip>(cur, tid, tpr, lim, p, mn);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     if ((tid & 31) == 0) red_max[tid >> 5] = m;
@@ -642,7 +647,8 @@ __global__ void __launch_bounds__(kClusterThreads, 2) softmax_cluster_kernel(con
     if (e0 < lim) cur[k] = ld_stream(src + e0);
   }
   float mn;
-  const float m = group_max<false>(softmax_prep<T, NV>(cur, v0 + tid, tpr, lim, p, mn), tpr, red_max);
+  const float m =
+      group_max<false>(softmax_prep<T, NV, uint4, false, kCausal>(cur, v0 + tid, tpr, lim, p, mn), tpr, red_max);
   if (tid == 0) {
     for (int r = 0; r < csize; ++r) *cluster.map_shared_rank(&cmax[rank], r) = m;
   }
