@@ -19,13 +19,6 @@ namespace {
 // f32 value of std::f32::consts::FRAC_1_SQRT_2.
 constexpr float kFrac1Sqrt2 = 0.707106781186547524400844362104849039f;
 
-template <typename T>
-__device__ __forceinline__ float silu_t(float s) {
-  // (T::zero() - s).exp(), then T::one() + e, then s / (...), each rounded to T.
-  const float e = Elem<T>::round(expf(Elem<T>::round(__fsub_rn(0.f, s))));
-  return __fdiv_rn(s, Elem<T>::round(__fadd_rn(1.f, e)));
-}
-
 __device__ __forceinline__ float gelu_erf(float x) {
   const float erf_val = erff(__fmul_rn(x, kFrac1Sqrt2));
   return __fmul_rn(__fmul_rn(x, 0.5f), __fadd_rn(1.f, erf_val));
@@ -73,6 +66,73 @@ __device__ __forceinline__ float rcp_approx_ftz(float x) {
   float y;
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// T(s / d) for f16 values s and d >= 1 (SiLU's d = T(1 + e)), without the
+// IEEE division routine. q0 = s * rcp(d), refined once with the exact
+// remainder: q1 = q0 + (s - d q0) * rcp(d) is s / d rounded once to f32 (up
+// to a term of the square of the reciprocal's error), so within 2^-24 of s / d
+// relative. Over every finite f16 s and its d, a quotient that is not an f32
+// value is at least 2^-22.78 (relative) from an f16 rounding midpoint, so q1
+// rounds to the f16 value of the IEEE f32 quotient; an f32-exact quotient
+// comes out exact. copysign restores the sign of zero quotients (s = -0).
+// Where the remainder step meets an infinity (s = +inf, or d = inf) it gives
+// NaN, and q0 is then the IEEE quotient (s / inf = -0 for finite s < 0, inf / 1,
+// -inf / inf = NaN).
+__device__ __forceinline__ float div_f16_by_d(float s, float d) {
+  const float r = rcp_approx(d);
+  const float q0 = __fmul_rn(s, r);
+  const float rem = __fmaf_rn(-d, q0, s);
+  const float q1 = copysignf(__fmaf_rn(rem, r, q0), q0);
+  return isnan(q1) ? q0 : q1;
+}
+
+template <typename T>
+__device__ __forceinline__ float silu_t(float s) {
+  // (T::zero() - s).exp(), then T::one() + e, then s / (...), each rounded to T.
+  const float e = Elem<T>::round(expf(Elem<T>::round(__fsub_rn(0.f, s))));
+  const float d = Elem<T>::round(__fadd_rn(1.f, e));
+  if constexpr (std::is_same_v<T, __half>) {
+    return div_f16_by_d(s, d);
+  } else {
+    return __fdiv_rn(s, d);
+  }
+}
+
+// silu_t<__half> on an element pair, same results bit for bit: -s by a sign
+// flip (exp(-0) = exp(+0), so the sign of 0 - s does not matter), exp from
+// CUDA's expf, and the f16 additions as f16x2 instructions: 1 + e in f32 is
+// exact for e >= 2^-13 and below 1 + 2^-11 (which rounds to 1) otherwise, so
+// its f16 rounding is the f16x2 sum's. The division is div_f16_by_d on f32
+// pairs.
+__device__ __forceinline__ __half2 silu_f16x2(__half2 s) {
+  const float2 x = __half22float2(__hneg2(s));
+  const __half2 e = __floats2half2_rn(expf(x.x), expf(x.y));
+  const __half2 d = __hadd2(__float2half2_rn(1.f), e);
+  const float2 sf = __half22float2(s), df = __half22float2(d);
+  const float2 r = make_float2(rcp_approx(df.x), rcp_approx(df.y));
+  const float2 q0 = __fmul2_rn(sf, r);
+  const float2 rem = __ffma2_rn(make_float2(-df.x, -df.y), q0, sf);
+  const float2 q1 = __ffma2_rn(rem, r, q0);
+  const float y0 = copysignf(q1.x, q0.x), y1 = copysignf(q1.y, q0.y);
+  return __floats2half2_rn(isnan(y0) ? q0.x : y0, isnan(y1) ? q0.y : y1);
+}
+
+__device__ __forceinline__ uint32_t h2_bits(__half2 v) { return *reinterpret_cast<uint32_t *>(&v); }
+__device__ __forceinline__ __half2 bits_h2(uint32_t w) { return *reinterpret_cast<__half2 *>(&w); }
+
+__device__ __forceinline__ uint4 silu_f16x8(uint4 v) {
+  return make_uint4(h2_bits(silu_f16x2(bits_h2(v.x))), h2_bits(silu_f16x2(bits_h2(v.y))),
+                    h2_bits(silu_f16x2(bits_h2(v.z))), h2_bits(silu_f16x2(bits_h2(v.w))));
+}
+
+// T(T(silu(g)) * u): a product of two f16 values is exact in f32, so the
+// f16x2 multiply rounds as the reference's f32 product rounded to f16 does.
+__device__ __forceinline__ uint4 swiglu_f16x8(uint4 g, uint4 u) {
+  return make_uint4(h2_bits(__hmul2(silu_f16x2(bits_h2(g.x)), bits_h2(u.x))),
+                    h2_bits(__hmul2(silu_f16x2(bits_h2(g.y)), bits_h2(u.y))),
+                    h2_bits(__hmul2(silu_f16x2(bits_h2(g.z)), bits_h2(u.z))),
+                    h2_bits(__hmul2(silu_f16x2(bits_h2(g.w)), bits_h2(u.w))));
 }
 
 __device__ __forceinline__ __nv_bfloat162 silu_bf16x2(__nv_bfloat162 s) {
@@ -182,6 +242,8 @@ __global__ void __launch_bounds__(kBlock) unary_kernel(void *dst, const void *sr
       if (i < nacc) {
         if constexpr (std::is_same_v<T, __nv_bfloat16> && OP == XN_UNARY_SILU) {
           st_vec(d + i * N, silu_bf16x8(raw[u]));
+        } else if constexpr (std::is_same_v<T, __half> && OP == XN_UNARY_SILU) {
+          st_vec(d + i * N, silu_f16x8(raw[u]));
         } else if constexpr (!std::is_same_v<T, float> && OP == XN_UNARY_GELU_ERF) {
           float2 v2[N / 2];
           Pairs<T>::unpack(raw[u], v2);
@@ -251,6 +313,8 @@ __global__ void __launch_bounds__(kBlock) swiglu_kernel(void *dst, const void *g
         if (i < cacc) {
           if constexpr (std::is_same_v<T, __nv_bfloat16>) {
             st_vec(dr + i * N, swiglu_bf16x8(rg[k], ru[k]));
+          } else if constexpr (std::is_same_v<T, __half>) {
+            st_vec(dr + i * N, swiglu_f16x8(rg[k], ru[k]));
           } else {
             float vg[N], vu[N];
             unpack<T>(rg[k], vg);

@@ -46,6 +46,18 @@ int sm_count();
 // True unless the environment sets XN_PDL=0 (read once per process).
 bool pdl_enabled();
 
+// Grid of a persistent kernel: as many blocks of `block` threads (and `smem`
+// bytes of dynamic shared memory) as are resident on the GPU at once, never
+// more than `needed`.
+template <typename K>
+int64_t persistent_grid(K kernel, int block, int64_t needed, size_t smem = 0) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, block, smem) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  const int64_t g = static_cast<int64_t>(per_sm) * sm_count();
+  return g < needed ? g : needed;
+}
+
 // Launches `kernel` on `stream` with programmatic dependent launch allowed
 // (cudaLaunchAttributeProgrammaticStreamSerialization): the kernel's blocks
 // may be scheduled while the previous kernel of the stream drains. Every

@@ -699,17 +699,6 @@ __global__ void __launch_bounds__(1024) softmax_loop_kernel(const SoftmaxParams 
     dst[base + c] = Elem<T>::from_f32(__fdiv_rn(Elem<T>::to_f32(dst[base + c]), s));
 }
 
-// Persistent grid for the prefetching kernel: as many blocks as fit on the GPU
-// at once (never more than there are row-group rows).
-template <typename K>
-int64_t persistent_grid(K kernel, int block, int64_t needed) {
-  int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, block, 0) != cudaSuccess || per_sm < 1)
-    per_sm = 1;
-  const int64_t g = static_cast<int64_t>(per_sm) * sm_count();
-  return g < needed ? g : needed;
-}
-
 template <typename T, typename U, bool kCausal, bool kWin = false>
 bool launch_softmax_pipe(const SoftmaxParams &p, int nv, int block, int64_t grid, cudaStream_t st) {
   switch (nv) {
@@ -904,34 +893,38 @@ int launch_softmax(SoftmaxParams p, cudaStream_t st) {
   return check_launch("xn_softmax");
 }
 
-// One warp per (b, i) row writes -inf to columns (offset + i, t2): 16-byte
-// stores over the part of that range that is 16-byte aligned, element stores
-// for the ends.
+// One warp per row i of a slice writes -inf to columns (offset + i, t2):
+// 16-byte stores over the part of that range that is 16-byte aligned, element
+// stores for the ends. Only the mrows = min(t1, t2 - offset - 1) rows of a
+// slice that hold a masked column get a warp (grid.x, 8 per block); grid.y
+// covers the bh slices (striding past 65535), so no thread divides by t1 and
+// the blocks, in launch order, walk the tensor in memory order.
 template <typename T>
-__global__ void __launch_bounds__(256) causal_mask_kernel(void *dst, int64_t rows, int64_t t1,
-                                                          int64_t t2, int64_t offset) {
+__global__ void __launch_bounds__(256) causal_mask_kernel(void *dst, int64_t bh, int64_t t1, int64_t t2,
+                                                          int64_t offset, int64_t mrows) {
   griddep_wait();
   griddep_release();
   constexpr int N = Elem<T>::kVec;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (row >= rows) return;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (i >= mrows) return;
   const int lane = threadIdx.x & 31;
-  const int64_t first = offset + (row % t1) + 1;
-  if (first >= t2) return;
-  T *d = static_cast<T *>(dst) + row * t2;
+  const int64_t first = offset + i + 1;  // < t2, as i < mrows
   const T ninf = Elem<T>::from_f32(-INFINITY);
-  // [first, body0): head, [body0, body1): whole aligned vectors, [body1, t2): tail.
-  const int64_t mis = static_cast<int64_t>((reinterpret_cast<uintptr_t>(d + first) & 15u) / sizeof(T));
-  int64_t body0 = mis == 0 ? first : first + (N - mis);
-  if (body0 > t2) body0 = t2;
-  const int64_t body1 = body0 + (t2 - body0) / N * N;
-  if (first + lane < body0) d[first + lane] = ninf;  // the head is shorter than N <= 8 elements
   uint4 v;
   T *vt = reinterpret_cast<T *>(&v);
 #pragma unroll
   for (int j = 0; j < N; ++j) vt[j] = ninf;
-  for (int64_t c = body0 + static_cast<int64_t>(lane) * N; c < body1; c += 32 * N) st_vec(d + c, v);
-  if (body1 + lane < t2) d[body1 + lane] = ninf;  // so is the tail
+  for (int64_t b = blockIdx.y; b < bh; b += gridDim.y) {
+    T *d = static_cast<T *>(dst) + (b * t1 + i) * t2;
+    // [first, body0): head, [body0, body1): whole aligned vectors, [body1, t2): tail.
+    const int64_t mis = static_cast<int64_t>((reinterpret_cast<uintptr_t>(d + first) & 15u) / sizeof(T));
+    int64_t body0 = mis == 0 ? first : first + (N - mis);
+    if (body0 > t2) body0 = t2;
+    const int64_t body1 = body0 + (t2 - body0) / N * N;
+    if (first + lane < body0) d[first + lane] = ninf;  // the head is shorter than N <= 8 elements
+    for (int64_t c = body0 + static_cast<int64_t>(lane) * N; c < body1; c += 32 * N) st_vec(d + c, v);
+    if (body1 + lane < t2) d[body1 + lane] = ninf;  // so is the tail
+  }
 }
 
 }  // namespace
@@ -975,12 +968,16 @@ int xn_causality_mask(void *dst, int64_t bh, int64_t t1, int64_t t2, int64_t off
   using namespace xn;
   if (!is_float_dtype(dtype)) return fail(XN_E_DTYPE, "xn_causality_mask: unsupported dtype %d", dtype);
   if (bh < 0 || t1 < 0 || t2 < 0 || offset < 0) return fail(XN_E_INVALID, "xn_causality_mask: negative size");
-  const int64_t rows = bh * t1;
-  if (rows == 0 || t2 == 0) return ok();
+  if (bh == 0 || t1 == 0 || t2 == 0) return ok();
   if (dst == nullptr) return fail(XN_E_INVALID, "xn_causality_mask: null dst");
-  const int64_t grid = ceil_div(rows, 8);
-  if (grid > 0x7fffffffLL) return fail(XN_E_INVALID, "xn_causality_mask: too many rows");
-  XN_DISPATCH_FLOAT(dtype, launch_k(causal_mask_kernel<T>, dim3(grid), dim3(256), 0, as_stream(stream), dst, rows, t1, t2, offset);
+  // Rows i of a slice with a masked column: offset + i + 1 < t2.
+  const int64_t mrows = t2 - offset - 1 < t1 ? t2 - offset - 1 : t1;
+  if (mrows <= 0) return ok();
+  const int64_t gx = ceil_div(mrows, 8);
+  if (gx > 0x7fffffffLL) return fail(XN_E_INVALID, "xn_causality_mask: too many rows");
+  const int64_t gy = bh < 65535 ? bh : 65535;
+  const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy));
+  XN_DISPATCH_FLOAT(dtype, launch_k(causal_mask_kernel<T>, grid, dim3(256), 0, as_stream(stream), dst, bh, t1, t2, offset, mrows);
                     return check_launch("xn_causality_mask"));
   return fail(XN_E_DTYPE, "xn_causality_mask: unsupported dtype %d", dtype);
 }

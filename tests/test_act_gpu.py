@@ -104,6 +104,37 @@ def test_unary_bf16_exhaustive(oracle, xn, cuda, op):
     assert stats["exact_frac"] > 0.999, stats
 
 
+def test_silu_f16_exhaustive(oracle, xn, cuda):
+    """Every finite f16 input: the f16 SiLU divides without the IEEE division
+    routine (a reciprocal refined by the exact remainder), exact by the
+    quotients' distance from f16 rounding midpoints; differences left are
+    CUDA's expf against glibc's in T(exp(-s))."""
+    bits = np.arange(0x10000, dtype=np.uint32).astype(np.uint16)
+    x = bits[((bits >> 10) & 0x1F) != 0x1F]
+    ref = oracle.unary(x, "silu", "f16")
+    got = from_device(xn.silu(to_device(x, "f16", cuda)), "f16")
+    stats = assert_close(got, ref, "f16", "silu f16 exhaustive")
+    print(f"silu f16: {int(np.sum(got != ref))} of {x.size} inputs differ")
+    assert stats["exact_frac"] > 0.9995, stats
+    # Signed zeros and the quotients past exp's overflow (s <= -11.09: s / inf = -0).
+    z = got[(x == 0x8000) | (x == 0x0000)]
+    assert set(z.tolist()) == {0x8000, 0x0000}
+    neg_big = storage_to_f32(x, "f16") < -11.5
+    assert np.all(got[neg_big] == 0x8000)
+
+
+def test_swiglu_f16_all_gates(oracle, xn, cuda):
+    """Every finite f16 gate value against random up values."""
+    bits = np.arange(0x10000, dtype=np.uint32).astype(np.uint16)
+    g = bits[((bits >> 10) & 0x1F) != 0x1F]
+    u = to_storage(randn(rng(13), g.size, 2.0), "f16")
+    ref = oracle.swiglu(g, u, "f16")
+    got = from_device(xn.swiglu(to_device(g, "f16", cuda), to_device(u, "f16", cuda)), "f16")
+    stats = assert_close(got, ref, "f16", "swiglu f16 all gates")
+    print(f"swiglu f16: {int(np.sum(got != ref))} of {g.size} gates differ")
+    assert stats["exact_frac"] > 0.9995, stats
+
+
 def test_swiglu_bf16_all_gates(oracle, xn, cuda):
     """Every finite bf16 gate value against random up values."""
     bits = np.arange(0x10000, dtype=np.uint32).astype(np.uint16)
