@@ -102,6 +102,12 @@ __device__ __forceinline__ uint4 opaque(uint4 v) {
   return v;
 }
 
+// The j-th 32-bit word of a 16-byte vector (j a compile-time constant after
+// unrolling).
+__device__ __forceinline__ uint32_t u4_word(const uint4 &v, int j) {
+  return j == 0 ? v.x : (j == 1 ? v.y : (j == 2 ? v.z : v.w));
+}
+
 // Unpack / pack 16 bytes as kVec values of T widened to f32.
 template <typename T>
 __device__ __forceinline__ void unpack(const uint4 &v, float (&f)[Elem<T>::kVec]);

@@ -138,7 +138,13 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : 1) norm_rows
 // and mask, and the residual prologue on packed T pairs (residual_vec). The
 // results per element are the same as the scalar forms: only the grouping of
 // the row sums differs (two interleaved partial sums per thread).
-template <typename T, int NV, bool kLN, int kMaxBlock, bool kBranch>
+// kMix (16-bit LayerNorm): the sums with row elements use the mixed-precision
+// add on the stored elements instead of widening them first (fewer
+// instructions; the same values). Chosen for row groups of 8 or more threads:
+// with 4-thread groups (rows of 32 vectors) the shorter instruction stream
+// reaches the per-vector weight loads sooner and waits on them, which measured
+// slower.
+template <typename T, int NV, bool kLN, int kMaxBlock, bool kBranch, bool kMix = false>
 __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : (kMaxBlock == 512 ? 2 : 1))
     norm_vec_kernel(const NormParams p) {
   griddep_wait();
@@ -209,7 +215,59 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : (kMaxBlock =
   // 2) Row statistics in f32, then 3) the epilogue dst = T(norm(h) * w (+ b)).
   const float cols_f = __ll2float_rn(p.cols);
   uint4 *dst = reinterpret_cast<uint4 *>(static_cast<T *>(p.dst) + base);
-  if constexpr (kLN) {
+  if constexpr (kLN && kMix && !std::is_same_v<T, float>) {
+    // kMix: every f32 sum with a row element takes the element as it is
+    // stored (sm_100's mixed-precision add, add2_widen), the same values as
+    // widening it first; only the weight is widened.
+    float2 s2 = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+#pragma unroll
+      for (int j = 0; j < KP; ++j) s2 = add2_widen<T>(u4_word(h[k], j), s2);
+    }
+    const float mean = __fdiv_rn(group_sum<false>(__fadd_rn(s2.x, s2.y), tpr, red_a), cols_f);
+    const float2 nmean = splat2(-mean);
+    float2 v2 = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      if (lr + k * tpr < p.nvec) {
+        const uint4 hk = opaque(h[k]);
+#pragma unroll
+        for (int j = 0; j < KP; ++j) {
+          const float2 d = add2_widen<T>(u4_word(hk, j), nmean);
+          v2 = __ffma2_rn(d, d, v2);
+        }
+      }
+    }
+    const float var = __fdiv_rn(group_sum<false>(__fadd_rn(v2.x, v2.y), tpr, red_b), cols_f);
+    const float2 inv = splat2(__fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(var, p.eps))));
+    const float2 nshift = splat2(p.remove_mean ? -mean : -0.f);  // -0: x + (-0) == x
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int vi = lr + k * tpr;
+      if (active && vi < p.nvec) {
+        const uint4 hk = opaque(h[k]);
+        float2 x[KP], w[KP];
+        if (wp != nullptr) {
+          P::unpack(kPre ? wpre[k] : ld_cached(wp + vi * N), w);
+        } else {
+#pragma unroll
+          for (int j = 0; j < KP; ++j) w[j] = splat2(1.f);
+        }
+#pragma unroll
+        for (int j = 0; j < KP; ++j) x[j] = __fmul2_rn(__fmul2_rn(add2_widen<T>(u4_word(hk, j), nshift), inv), w[j]);
+        if (bp != nullptr) {
+          const uint4 bv = kPre ? bpre[k] : ld_cached(bp + vi * N);
+#pragma unroll
+          for (int j = 0; j < KP; ++j) x[j] = add2_widen<T>(u4_word(bv, j), x[j]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < KP; ++j) x[j] = __fadd2_rn(x[j], splat2(0.f));
+        }
+        st_vec(dst + vi, P::pack(x));
+      }
+    }
+  } else if constexpr (kLN) {
     float2 s2 = make_float2(0.f, 0.f);
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
@@ -368,6 +426,12 @@ constexpr int kMaxNv = (kBranch || kMaxBlock > 512) ? 4 : 8;
 template <typename T, bool kVector, int NV, bool kLN, int kMaxBlock, bool kBranch>
 void launch_nv(const NormParams &p, int block, int64_t grid, cudaStream_t st) {
   if constexpr (kVector) {
+    if constexpr (kLN && !kBranch && !std::is_same_v<T, float>) {
+      if (p.tpr >= 8) {
+        launch_k(norm_vec_kernel<T, NV, kLN, kMaxBlock, kBranch, true>, dim3(grid), dim3(block), 0, st, p);
+        return;
+      }
+    }
     launch_k(norm_vec_kernel<T, NV, kLN, kMaxBlock, kBranch>, dim3(grid), dim3(block), 0, st, p);
   } else {
     launch_k(norm_rows_kernel<T, NV, kLN, kMaxBlock, kBranch>, dim3(grid), dim3(block), 0, st, p);
