@@ -536,6 +536,30 @@ __device__ __forceinline__ float2 add2_widen<__half>(uint32_t w, float2 c) {
   return d;
 }
 
+// c + lo*lo, c + hi*hi for a packed 16-bit pair (lo, hi), each rounded once to
+// f32: sm_100's mixed-precision fma on the stored halves, the same values as
+// __ffma2_rn(x, x, c) on the widened pair.
+template <typename T>
+__device__ __forceinline__ float2 sq_add2_widen(uint32_t w, float2 c);
+
+template <>
+__device__ __forceinline__ float2 sq_add2_widen<__nv_bfloat16>(uint32_t w, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\tfma.rn.f32.bf16 %0, lo, lo, %3;\n\tfma.rn.f32.bf16 %1, hi, hi, %4;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "r"(w), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+template <>
+__device__ __forceinline__ float2 sq_add2_widen<__half>(uint32_t w, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\tfma.rn.f32.f16 %0, lo, lo, %3;\n\tfma.rn.f32.f16 %1, hi, hi, %4;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "r"(w), "f"(c.x), "f"(c.y));
+  return d;
+}
+
 // div_by on an element pair, for dividends that are never -0 (exp results):
 // with x = +0 every step is +0, so the sign fix-up is not needed. nd = -d,
 // r = __frcp_rn(d) in both lanes.

@@ -138,9 +138,10 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : 1) norm_rows
 // and mask, and the residual prologue on packed T pairs (residual_vec). The
 // results per element are the same as the scalar forms: only the grouping of
 // the row sums differs (two interleaved partial sums per thread).
-// kMix (16-bit LayerNorm): the sums with row elements use the mixed-precision
-// add on the stored elements instead of widening them first (fewer
-// instructions; the same values). Chosen for row groups of 8 or more threads:
+// kMix (16-bit rows; LayerNorm without a residual branch, RMSNorm with or
+// without): the sums with row elements use the mixed-precision add / fma on
+// the stored elements instead of widening them first (fewer instructions; the
+// same values). Chosen for row groups of 8 or more threads:
 // with 4-thread groups (rows of 32 vectors) the shorter instruction stream
 // reaches the per-vector weight loads sooner and waits on them, which measured
 // slower.
@@ -320,6 +321,45 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : (kMaxBlock =
         st_vec(dst + vi, P::pack(x));
       }
     }
+  } else if constexpr (kMix && !std::is_same_v<T, float>) {
+    // kMix: the squares summed straight from the stored elements (sm_100's
+    // mixed-precision fma, sq_add2_widen: the same values), and div_by's
+    // quotient steps with the remainder's sign flipped: nrem = m*q0 - x is
+    // exactly -(x - m*q0), so q0 - nrem*r is the same value, and where x = +-0
+    // the zeros combine to the sign of x, so no copysign fix-up is needed
+    // (m = inf: 0 in m's place, q0 = x * 0 as in neg_divisor).
+    float2 s2 = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+#pragma unroll
+      for (int j = 0; j < KP; ++j) s2 = sq_add2_widen<T>(u4_word(h[k], j), s2);
+    }
+    const float s = group_sum<false>(__fadd_rn(s2.x, s2.y), tpr, red_a);
+    const float m = __fsqrt_rn(__fadd_rn(__fdiv_rn(s, cols_f), p.eps));
+    const float r = __frcp_rn(m);
+    const float2 pm2 = splat2(isinf(m) ? 0.f : m), r2 = splat2(r);
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int vi = lr + k * tpr;
+      if (active && vi < p.nvec) {
+        float2 x[KP], w[KP];
+        P::unpack(opaque(h[k]), x);
+        if (wp != nullptr) {
+          P::unpack(kPre ? wpre[k] : ld_cached(wp + vi * N), w);
+        } else {
+#pragma unroll
+          for (int j = 0; j < KP; ++j) w[j] = splat2(1.f);
+        }
+#pragma unroll
+        for (int j = 0; j < KP; ++j) {
+          const float2 q0 = __fmul2_rn(x[j], r2);
+          const float2 nrem = __ffma2_rn(pm2, q0, make_float2(-x[j].x, -x[j].y));
+          const float2 q = __ffma2_rn(make_float2(-nrem.x, -nrem.y), r2, q0);
+          x[j] = __fmul2_rn(q, w[j]);
+        }
+        st_vec(dst + vi, P::pack(x));
+      }
+    }
   } else {
     float2 s2 = make_float2(0.f, 0.f);
 #pragma unroll
@@ -426,7 +466,7 @@ constexpr int kMaxNv = (kBranch || kMaxBlock > 512) ? 4 : 8;
 template <typename T, bool kVector, int NV, bool kLN, int kMaxBlock, bool kBranch>
 void launch_nv(const NormParams &p, int block, int64_t grid, cudaStream_t st) {
   if constexpr (kVector) {
-    if constexpr (kLN && !kBranch && !std::is_same_v<T, float>) {
+    if constexpr ((!kLN || !kBranch) && !std::is_same_v<T, float>) {
       if (p.tpr >= 8) {
         launch_k(norm_vec_kernel<T, NV, kLN, kMaxBlock, kBranch, true>, dim3(grid), dim3(block), 0, st, p);
         return;
