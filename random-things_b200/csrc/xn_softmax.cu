@@ -899,31 +899,35 @@ int launch_softmax(SoftmaxParams p, cudaStream_t st) {
 // slice that hold a masked column get a warp (grid.x, 8 per block); grid.y
 // covers the bh slices (striding past 65535), so no thread divides by t1 and
 // the blocks, in launch order, walk the tensor in memory order.
-template <typename T>
+// I: the index type within a row and a slice, int when t1, t2 and the offset
+// are below 2^30 (then first + 32 * N and every other index stay below 2^31),
+// else int64_t; the row's base pointer is always formed in 64 bits.
+template <typename T, typename I>
 __global__ void __launch_bounds__(256) causal_mask_kernel(void *dst, int64_t bh, int64_t t1, int64_t t2,
                                                           int64_t offset, int64_t mrows) {
   griddep_wait();
   griddep_release();
   constexpr int N = Elem<T>::kVec;
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (i >= mrows) return;
+  const I i = static_cast<I>(blockIdx.x) * 8 + static_cast<I>(threadIdx.x >> 5);
+  if (i >= static_cast<I>(mrows)) return;
   const int lane = threadIdx.x & 31;
-  const int64_t first = offset + i + 1;  // < t2, as i < mrows
+  const I w = static_cast<I>(t2);
+  const I first = static_cast<I>(offset) + i + 1;  // < t2, as i < mrows
   const T ninf = Elem<T>::from_f32(-INFINITY);
   uint4 v;
   T *vt = reinterpret_cast<T *>(&v);
 #pragma unroll
   for (int j = 0; j < N; ++j) vt[j] = ninf;
   for (int64_t b = blockIdx.y; b < bh; b += gridDim.y) {
-    T *d = static_cast<T *>(dst) + (b * t1 + i) * t2;
+    T *d = static_cast<T *>(dst) + (b * t1 + static_cast<int64_t>(i)) * t2;
     // [first, body0): head, [body0, body1): whole aligned vectors, [body1, t2): tail.
-    const int64_t mis = static_cast<int64_t>((reinterpret_cast<uintptr_t>(d + first) & 15u) / sizeof(T));
-    int64_t body0 = mis == 0 ? first : first + (N - mis);
-    if (body0 > t2) body0 = t2;
-    const int64_t body1 = body0 + (t2 - body0) / N * N;
+    const I mis = static_cast<I>((reinterpret_cast<uintptr_t>(d + first) & 15u) / sizeof(T));
+    I body0 = mis == 0 ? first : first + (N - mis);
+    if (body0 > w) body0 = w;
+    const I body1 = body0 + ((w - body0) & ~static_cast<I>(N - 1));  // w - body0 >= 0
     if (first + lane < body0) d[first + lane] = ninf;  // the head is shorter than N <= 8 elements
-    for (int64_t c = body0 + static_cast<int64_t>(lane) * N; c < body1; c += 32 * N) st_vec(d + c, v);
-    if (body1 + lane < t2) d[body1 + lane] = ninf;  // so is the tail
+    for (I c = body0 + static_cast<I>(lane) * N; c < body1; c += 32 * N) st_vec(d + c, v);
+    if (body1 + lane < w) d[body1 + lane] = ninf;  // so is the tail
   }
 }
 
@@ -977,7 +981,9 @@ int xn_causality_mask(void *dst, int64_t bh, int64_t t1, int64_t t2, int64_t off
   if (gx > 0x7fffffffLL) return fail(XN_E_INVALID, "xn_causality_mask: too many rows");
   const int64_t gy = bh < 65535 ? bh : 65535;
   const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy));
-  XN_DISPATCH_FLOAT(dtype, launch_k(causal_mask_kernel<T>, grid, dim3(256), 0, as_stream(stream), dst, bh, t1, t2, offset, mrows);
+  const bool narrow = t1 < (int64_t{1} << 30) && t2 < (int64_t{1} << 30) && offset < (int64_t{1} << 30);
+  XN_DISPATCH_FLOAT(dtype, if (narrow) launch_k(causal_mask_kernel<T, int>, grid, dim3(256), 0, as_stream(stream), dst, bh, t1, t2, offset, mrows);
+                    else launch_k(causal_mask_kernel<T, int64_t>, grid, dim3(256), 0, as_stream(stream), dst, bh, t1, t2, offset, mrows);
                     return check_launch("xn_causality_mask"));
   return fail(XN_E_DTYPE, "xn_causality_mask: unsupported dtype %d", dtype);
 }
