@@ -21,6 +21,7 @@ def _rows(dtype, cols):
     x[4, :] = 3.0e19  # finite; squares overflow f32 (sum of squares = inf)
     x[4, ::3] = -2.0e20
     x[5, :] = 0.0
+    x[5, ::2] = -0.0  # signed zeros: x / m keeps the sign of x
     x[6, 0] = 1.0e30
     return to_storage(x, dtype)
 
@@ -46,9 +47,13 @@ def test_norms_and_softmax_special_values(oracle, xn, cuda, dtype, cols):
         (xn.layer_norm(X, W, B, 1e-5), oracle.layer_norm(x, w, b, 1e-5, dtype), "layer_norm"),
         (xn.softmax(X), oracle.softmax(x, dtype), "softmax"),
     ]:
-        g, r = _same_nonfinite(from_device(got, dtype), ref, dtype)
+        full = from_device(got, dtype)
+        g, r = _same_nonfinite(full, ref, dtype)
         if g.size:
             assert_close(g, r, dtype, f"{what} finite part")
+        # The row of signed zeros, bit for bit (+0 and -0 differ in storage).
+        assert np.array_equal(full[5].view(np.uint32 if dtype == "f32" else np.uint16),
+                              ref[5].view(np.uint32 if dtype == "f32" else np.uint16)), f"{what}: signed zeros"
 
 
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
