@@ -712,6 +712,13 @@ bool launch_softmax_pipe(const SoftmaxParams &p, int nv, int block, int64_t grid
       launch_k(k, dim3(persistent_grid(k, block, grid)), dim3(block), 0, st, p);
       return true;
     }
+    case 3:
+      if constexpr (kWin) {
+        auto k = softmax_pipe_kernel<T, 3, kCausal, U, kWin>;
+        launch_k(k, dim3(persistent_grid(k, block, grid)), dim3(block), 0, st, p);
+        return true;
+      }
+      return false;
     case 4: {
       auto k = softmax_pipe_kernel<T, 4, kCausal, U, kWin>;
       launch_k(k, dim3(persistent_grid(k, block, grid)), dim3(block), 0, st, p);
@@ -866,7 +873,12 @@ int launch_softmax(SoftmaxParams p, cudaStream_t st) {
     // Pairs are 4-byte registers: 8 per thread cost little and halve the
     // reduction steps per element.
     if (pair) tpr = pow2_ceil(ceil_div(nvec, 8));
-    const int nv = static_cast<int>(pow2_ceil(ceil_div(nvec, tpr)));
+    int nv = static_cast<int>(pow2_ceil(ceil_div(nvec, tpr)));
+    // Window rows of 17-24 vectors per 8, 33-48 per 16 threads (Mimi's 250
+    // attention columns: 33): 3 accesses per thread instead of 4. Every access
+    // slot is issued whether or not a lane holds data in it, so the fourth,
+    // empty in every lane, would cost as much as a live one.
+    if (win && ceil_div(nvec, tpr) == 3) nv = 3;
     const int block = tpr < 256 ? 256 : static_cast<int>(tpr);
     const int64_t grid = ceil_div(p.rows, block / tpr);
     if (grid > 0x7fffffffLL) return fail(XN_E_INVALID, "xn_softmax: too many rows");
