@@ -498,6 +498,12 @@ bool launch_regs_b(NormParams p, int nv, int block, int64_t grid, cudaStream_t s
         return true;
       }
       return false;
+    case 6:
+      if constexpr (cap >= 8 && kVector) {
+        launch_nv<T, kVector, 6, kLN, kMaxBlock, kBranch>(p, block, grid, st);
+        return true;
+      }
+      return false;
     case 8:
       if constexpr (cap >= 8) {
         launch_nv<T, kVector, 8, kLN, kMaxBlock, kBranch>(p, block, grid, st);
@@ -559,7 +565,11 @@ int launch_norm(NormParams p, cudaStream_t st, const char *op) {
     while (tpr < 256 && tpr < nvec && p.rows * tpr * 2 <= 65536) tpr *= 2;
   }
   if (tpr > 0) {
-    const int nv = static_cast<int>(pow2_ceil(ceil_div(nvec, tpr)));
+    int nv = static_cast<int>(pow2_ceil(ceil_div(nvec, tpr)));
+    // 5 or 6 accesses per thread (rows of 1536, 2560, 3072 or 5120 16-bit
+    // columns): 6 instead of 8. Every access slot is issued whether or not a
+    // lane holds data in it, so empty slots cost as much as full ones.
+    if (vec && nv == 8 && ceil_div(nvec, tpr) <= 6) nv = 6;
     const int block = tpr < 256 ? 256 : static_cast<int>(tpr);
     const int64_t rpb = block / tpr;
     const int64_t grid = ceil_div(p.rows, rpb);

@@ -391,7 +391,7 @@ __device__ __forceinline__ void softmax_store(U (&cur)[NV], float s, T *dst_row,
 // softmax_rows_kernel. The loop bound depends only on the block, so blocks
 // whose row groups span several warps keep their __syncthreads uniform.
 template <typename T, int NV, bool kCausal, typename U, bool kWin>
-__global__ void __launch_bounds__(512, NV * sizeof(U) >= 128 ? 1 : 2) softmax_pipe_kernel(const SoftmaxParams p) {
+__global__ void __launch_bounds__(512, NV * sizeof(U) >= 80 ? 1 : 2) softmax_pipe_kernel(const SoftmaxParams p) {
   griddep_wait();
   griddep_release();
   constexpr int N = static_cast<int>(sizeof(U) / sizeof(T));
@@ -713,7 +713,7 @@ bool launch_softmax_pipe(const SoftmaxParams &p, int nv, int block, int64_t grid
       return true;
     }
     case 3:
-      if constexpr (kWin) {
+      if constexpr (sizeof(U) == 16) {
         auto k = softmax_pipe_kernel<T, 3, kCausal, U, kWin>;
         launch_k(k, dim3(persistent_grid(k, block, grid)), dim3(block), 0, st, p);
         return true;
@@ -724,6 +724,20 @@ bool launch_softmax_pipe(const SoftmaxParams &p, int nv, int block, int64_t grid
       launch_k(k, dim3(persistent_grid(k, block, grid)), dim3(block), 0, st, p);
       return true;
     }
+    case 5:
+      if constexpr (sizeof(U) == 16) {
+        auto k = softmax_pipe_kernel<T, 5, kCausal, U, kWin>;
+        launch_k(k, dim3(persistent_grid(k, block, grid)), dim3(block), 0, st, p);
+        return true;
+      }
+      return false;
+    case 6:
+      if constexpr (sizeof(U) == 16) {
+        auto k = softmax_pipe_kernel<T, 6, kCausal, U, kWin>;
+        launch_k(k, dim3(persistent_grid(k, block, grid)), dim3(block), 0, st, p);
+        return true;
+      }
+      return false;
     case 8: {
       auto k = softmax_pipe_kernel<T, 8, kCausal, U, kWin>;
       launch_k(k, dim3(persistent_grid(k, block, grid)), dim3(block), 0, st, p);
@@ -792,10 +806,10 @@ constexpr int64_t staged_min_vec() {
   return std::is_same_v<T, float> ? 2049 : 256;
 }
 
-template <typename T, bool kCausal, bool kSkip>
-void launch_softmax_staged(SoftmaxParams p, int64_t nvec, cudaStream_t st) {
-  auto kernel = softmax_staged_kernel<T, kStagedNv, kCausal, kSkip>;
-  const int block = static_cast<int>(ceil_div(ceil_div(nvec, kStagedNv), 32) * 32);
+template <typename T, bool kCausal, bool kSkip, int NV>
+void launch_softmax_staged_nv(SoftmaxParams p, int64_t nvec, cudaStream_t st) {
+  auto kernel = softmax_staged_kernel<T, NV, kCausal, kSkip>;
+  const int block = static_cast<int>(ceil_div(ceil_div(nvec, NV), 32) * 32);
   const int stage_bytes = static_cast<int>(ceil_div(nvec * 16, 128) * 128);
   const size_t smem = static_cast<size_t>(kStages) * stage_bytes;
   cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -807,6 +821,23 @@ void launch_softmax_staged(SoftmaxParams p, int64_t nvec, cudaStream_t st) {
   p.tpr = block;
   p.nvec = static_cast<int>(nvec);
   launch_k(kernel, dim3(static_cast<unsigned>(grid)), dim3(block), smem, st, p, kStages, stage_bytes);
+}
+
+// Accesses per thread: the fewest access slots (threads rounded up to whole
+// warps, times accesses per thread) among 8, 6 and 5, preferring 8. Every slot
+// is issued whether or not it holds data, so rows of 320, 384 or 640 vectors
+// (2560, 3072 and 5120 16-bit columns) take 5, 6 and 5 per thread with no
+// empty slot instead of 8 with 37, 25 and 17% of them empty.
+template <typename T, bool kCausal, bool kSkip>
+void launch_softmax_staged(SoftmaxParams p, int64_t nvec, cudaStream_t st) {
+  auto slots = [nvec](int nv) { return ceil_div(ceil_div(nvec, nv), 32) * 32 * nv; };
+  const int64_t s8 = slots(kStagedNv), s6 = slots(6), s5 = slots(5);
+  if (s5 < s8 && s5 < s6 && ceil_div(nvec, 5) <= 512)
+    launch_softmax_staged_nv<T, kCausal, kSkip, 5>(p, nvec, st);
+  else if (s6 < s8 && ceil_div(nvec, 6) <= 512)
+    launch_softmax_staged_nv<T, kCausal, kSkip, 6>(p, nvec, st);
+  else
+    launch_softmax_staged_nv<T, kCausal, kSkip, kStagedNv>(p, nvec, st);
 }
 
 // One cluster of `csize` blocks per row, launched with programmatic dependent
@@ -874,11 +905,16 @@ int launch_softmax(SoftmaxParams p, cudaStream_t st) {
     // reduction steps per element.
     if (pair) tpr = pow2_ceil(ceil_div(nvec, 8));
     int nv = static_cast<int>(pow2_ceil(ceil_div(nvec, tpr)));
-    // Window rows of 17-24 vectors per 8, 33-48 per 16 threads (Mimi's 250
-    // attention columns: 33): 3 accesses per thread instead of 4. Every access
-    // slot is issued whether or not a lane holds data in it, so the fourth,
-    // empty in every lane, would cost as much as a live one.
-    if (win && ceil_div(nvec, tpr) == 3) nv = 3;
+    // Rows of 17-24 vectors per 8, 33-48 per 16, 65-96 per 32 threads (Mimi's
+    // 250 attention columns through the window: 33; 768 16-bit columns: 96):
+    // 3 accesses per thread instead of 4. Every access slot is issued whether
+    // or not a lane holds data in it, so the fourth, empty in every lane,
+    // would cost as much as a live one.
+    if ((vec || win) && ceil_div(nvec, tpr) == 3) nv = 3;
+    // Likewise 5 or 6 vectors per thread (rows of 1536 16-bit columns, of 768,
+    // 1280, 1536, 2560, 3072 or 5120 f32 columns) take 5 or 6 slots instead
+    // of 8.
+    if ((vec || win) && nv == 8 && ceil_div(nvec, tpr) <= 6) nv = static_cast<int>(ceil_div(nvec, tpr));
     const int block = tpr < 256 ? 256 : static_cast<int>(tpr);
     const int64_t grid = ceil_div(p.rows, block / tpr);
     if (grid > 0x7fffffffLL) return fail(XN_E_INVALID, "xn_softmax: too many rows");
