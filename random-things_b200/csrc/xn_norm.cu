@@ -492,6 +492,12 @@ bool launch_regs_b(NormParams p, int nv, int block, int64_t grid, cudaStream_t s
         return true;
       }
       return false;
+    case 3:
+      if constexpr (cap >= 4 && kVector) {
+        launch_nv<T, kVector, 3, kLN, kMaxBlock, kBranch>(p, block, grid, st);
+        return true;
+      }
+      return false;
     case 4:
       if constexpr (cap >= 4) {
         launch_nv<T, kVector, 4, kLN, kMaxBlock, kBranch>(p, block, grid, st);
@@ -567,9 +573,12 @@ int launch_norm(NormParams p, cudaStream_t st, const char *op) {
   if (tpr > 0) {
     int nv = static_cast<int>(pow2_ceil(ceil_div(nvec, tpr)));
     // 5 or 6 accesses per thread (rows of 1536, 2560, 3072 or 5120 16-bit
-    // columns): 6 instead of 8. Every access slot is issued whether or not a
-    // lane holds data in it, so empty slots cost as much as full ones.
+    // columns): 6 instead of 8, and 3 instead of 4 (with a residual branch,
+    // rows of 768, 1536 or 3072 16-bit columns). Every access slot is issued
+    // whether or not a lane holds data in it, so empty slots cost as much as
+    // full ones.
     if (vec && nv == 8 && ceil_div(nvec, tpr) <= 6) nv = 6;
+    if (vec && nv == 4 && ceil_div(nvec, tpr) == 3) nv = 3;
     const int block = tpr < 256 ? 256 : static_cast<int>(tpr);
     const int64_t rpb = block / tpr;
     const int64_t grid = ceil_div(p.rows, rpb);
