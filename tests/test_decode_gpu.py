@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 import torch
 
-from helpers import assert_close, from_device, randn, rng, to_device, to_storage
+from helpers import assert_close, attention_abs_bound, from_device, randn, rng, storage_to_f32, to_device, to_storage
 
 pytestmark = pytest.mark.gpu
 
@@ -80,7 +80,11 @@ def _stream(oracle, xn, cuda, dtype, *, b, h, d, cap, context, steps, mask, seed
         kv_len = kk.shape[2]
         mask_offset = kv_len - t if mask == "relative" else total
         ref = oracle.attention_step(q, kk, vv, scale, mask_offset, dtype).reshape(b, t, h * d)
-        yield from_device(O, dtype), ref
+        # The reference's probabilities, for the weighted sum's allowance.
+        scores = oracle.scale(oracle.matmul(q, kk, dtype, trans_rhs=True), scale, dtype)
+        probs = oracle.softmax(oracle.apply_causality_mask(scores, mask_offset, dtype), dtype)
+        allow = attention_abs_bound(storage_to_f32(probs, dtype), storage_to_f32(vv, dtype)).reshape(b, t, h * d)
+        yield from_device(O, dtype), ref, allow
         total += t
 
 
@@ -91,27 +95,27 @@ def test_attention_decode_stream(oracle, xn, cuda, dtype, mask, d):
     """Single-token steps and chunks, past the context so the cache trims and
     the ring wraps (cap 24 > context 20)."""
     steps = [3, 1, 1, 4, 1, 2, 1, 1, 5, 1, 1, 1, 2, 1]
-    for n, (got, ref) in enumerate(_stream(oracle, xn, cuda, dtype, b=2, h=3, d=d, cap=24, context=20, steps=steps,
-                                           mask=mask, seed=d)):
-        assert_close(got, ref, dtype, f"step {n}")
+    for n, (got, ref, allow) in enumerate(_stream(oracle, xn, cuda, dtype, b=2, h=3, d=d, cap=24, context=20,
+                                                  steps=steps, mask=mask, seed=d)):
+        assert_close(got, ref, dtype, f"attention_decode {dtype} d={d} step {n}", extra_abs=allow)
 
 
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
 def test_attention_decode_config3_shapes(oracle, xn, cuda, dtype):
     """Benchmark config 3 shapes (B=16, 16 heads of 64) over the first steps and
     a step at a long context (t=1 per step, pos = step - 1)."""
-    for n, (got, ref) in enumerate(_stream(oracle, xn, cuda, dtype, b=16, h=16, d=64, cap=256, context=256,
-                                           steps=[1] * 6, mask="relative", seed=3)):
-        assert_close(got, ref, dtype, f"step {n}")
+    for n, (got, ref, allow) in enumerate(_stream(oracle, xn, cuda, dtype, b=16, h=16, d=64, cap=256, context=256,
+                                                  steps=[1] * 6, mask="relative", seed=3)):
+        assert_close(got, ref, dtype, f"attention_decode {dtype} config3 step {n}", extra_abs=allow)
 
 
 def test_attention_decode_device_position_matches_host(oracle, xn, cuda):
     """Reading the position from device memory (graph-capturable) gives the
     same results as passing it from the host."""
     steps = [2, 1, 1, 3, 1, 1, 1]
-    host = [g for g, _ in _stream(oracle, xn, cuda, "bf16", b=2, h=4, d=64, cap=8, context=6, steps=steps,
+    host = [g for g, _, _ in _stream(oracle, xn, cuda, "bf16", b=2, h=4, d=64, cap=8, context=6, steps=steps,
                                   mask="relative", seed=11)]
-    dev = [g for g, _ in _stream(oracle, xn, cuda, "bf16", b=2, h=4, d=64, cap=8, context=6, steps=steps,
+    dev = [g for g, _, _ in _stream(oracle, xn, cuda, "bf16", b=2, h=4, d=64, cap=8, context=6, steps=steps,
                                  mask="relative", seed=11, use_total_dev=True)]
     for a, c in zip(host, dev):
         assert np.array_equal(a, c)
