@@ -279,8 +279,20 @@ XN_API int xn_rvq_decode_sum(void *dst, const void *const *tables, int64_t n_q,
 enum {
   XN_MASK_RELATIVE = 0,  /* key j visible to query i iff j <= i + kv_len - t
                             (pocket_tts/src/transformer.rs:35-52) */
-  XN_MASK_ABSOLUTE = 1   /* iff j <= total + i: apply_causality_mask(offset) on
-                            the trimmed cache (mimi-rs/src/models/mimi.rs:1364) */
+  XN_MASK_ABSOLUTE = 1,  /* iff j <= total + i: apply_causality_mask(offset) on
+                            the trimmed cache with offset = the absolute position
+                            (pocket_tts/src/mimi_transformer.rs:114-145) */
+  XN_MASK_CACHE_LEN = 2  /* mimi-rs StreamingTransformer::forward
+                            (mimi-rs/src/models/mimi.rs:1476-1487): offset = the
+                            cache's length before the step, min(total, context),
+                            used as the RoPE position of the new rows (rope_i at
+                            offset, :1350-1351) and as the mask offset (:1364).
+                            The visible keys are those of XN_MASK_ABSOLUTE; only
+                            the rotation differs once the context is full. In
+                            xn_attention_decode (no rotation) it equals
+                            XN_MASK_ABSOLUTE; xn_kv_append_rope rotates at
+                            `total`, so a caller of this mode uses the fused
+                            xn_decode_attention_step. */
 };
 
 /*

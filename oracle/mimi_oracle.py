@@ -61,6 +61,20 @@ def _bmm(a: np.ndarray, b: np.ndarray, dtype: str) -> np.ndarray:
     return to_storage(np.matmul(storage_to_f32(a, dtype), storage_to_f32(b, dtype)), dtype)
 
 
+def rvq_ref(oracle, cfg, w: dict, codes: np.ndarray, dtype: str) -> np.ndarray:
+    """SplitResidualVectorQuantizer::decode (mimi-rs/src/models/mimi.rs:1858-1868):
+    rvq_first on codebook 0 and rvq_rest on the others, each a gather-sum
+    (:1627-1744) and a 1x1 projection (:1796-1806), added in T. codes
+    [B, n_q, T] -> [B, T, D]."""
+    books = [w[f"quantizer.codebook.{i}"] for i in range(cfg.n_q)]
+    first = oracle.rvq_decode(books[:1], np.ascontiguousarray(codes[:, :1]), dtype, "btd")
+    x = _mm(first, w["quantizer.rvq_first.output_proj"], dtype)
+    if cfg.n_q > 1:
+        rest = oracle.rvq_decode(books[1:], np.ascontiguousarray(codes[:, 1:]), dtype, "btd")
+        x = oracle.binary(x, _mm(rest, w["quantizer.rvq_rest.output_proj"], dtype), "add", dtype)
+    return x
+
+
 def chain_ref(oracle, cfg, w: dict, cos: np.ndarray, sin: np.ndarray, codes: np.ndarray, dtype: str,
               scale: float) -> np.ndarray:
     # `oracle` is the xn_oracle module (passed explicitly so callers control its build).
@@ -69,13 +83,7 @@ def chain_ref(oracle, cfg, w: dict, cos: np.ndarray, sin: np.ndarray, codes: np.
     B, _, T = codes.shape
     D, H = cfg.d_model, cfg.num_heads
     hd = D // H
-    # SplitResidualVectorQuantizer::decode: rvq_first + rvq_rest, each with its projection.
-    books = [w[f"quantizer.codebook.{i}"] for i in range(cfg.n_q)]
-    first = oracle.rvq_decode(books[:1], np.ascontiguousarray(codes[:, :1]), dtype, "btd")
-    x = _mm(first, w["quantizer.rvq_first.output_proj"], dtype)
-    if cfg.n_q > 1:
-        rest = oracle.rvq_decode(books[1:], np.ascontiguousarray(codes[:, 1:]), dtype, "btd")
-        x = oracle.binary(x, _mm(rest, w["quantizer.rvq_rest.output_proj"], dtype), "add", dtype)
+    x = rvq_ref(oracle, cfg, w, codes, dtype)
     scale_row = to_storage(np.full(T, scale, dtype=np.float32), dtype)
     for l in range(cfg.num_layers):
         p = f"layers.{l}."
@@ -104,30 +112,43 @@ def chain_ref(oracle, cfg, w: dict, cos: np.ndarray, sin: np.ndarray, codes: np.
 
 
 def stream_ref(oracle, cfg, w: dict, cos: np.ndarray, sin: np.ndarray, xs: list, dtype: str, scale: float,
-               context: int, act: str = "gelu_erf", mask: str = "absolute") -> list:
-    """The streaming decoder transformer (pocket_tts/src/mimi_transformer.rs:
-    StreamingTransformerLayer::forward with MimiStreamingMultiheadAttention;
-    mimi-rs/src/models/mimi.rs:1317-1445) over a stream of step inputs
+               context: int, act: str = "gelu_erf", mask: str = "absolute", codes: bool = False) -> list:
+    """The streaming decoder transformer over a stream of step inputs
     xs[s] = [B, t_s, D]: per layer a cat-then-trim KV cache of `context`
-    positions, rope_i at the absolute position, the attention op sequence with
-    apply_causality_mask(offset) ("absolute") or the additive causal mask
-    ("relative", pocket_tts/src/transformer.rs:35-52), LayerNorm / LayerScale /
-    residual adds and the MLP (`act` = gelu_erf as Pocket, or silu). Returns
-    the per-step outputs."""
+    positions, rope_i, the attention op sequence, LayerNorm / LayerScale /
+    residual adds and the MLP (`act` = gelu_erf as Mimi and Pocket, or silu).
+    Returns the per-step outputs.
+
+    mask selects the position bookkeeping:
+      * "absolute": Pocket's MimiStreamingMultiheadAttention
+        (pocket_tts/src/mimi_transformer.rs:114-145): RoPE and
+        apply_causality_mask at the absolute position (absolute_offset);
+      * "relative": the same with the additive causal mask
+        (pocket_tts/src/transformer.rs:35-52), key j visible to query i iff
+        j <= i + kv_len - t;
+      * "cache_len": mimi-rs's StreamingTransformer::forward
+        (mimi-rs/src/models/mimi.rs:1476-1487, 1317-1371): offset = the layer-0
+        cache's length before the step (min(total, context)), the RoPE position
+        and apply_causality_mask offset of every layer.
+    codes=True: each xs[s] is a [B, n_q, t_s] code tensor, decoded by rvq_ref
+    first (Mimi::decode_step, mimi.rs:2059-2071, without the conv upsample)."""
     L, D, H = cfg.num_layers, cfg.d_model, cfg.num_heads
     caches = [oracle.KvCacheRef(context) for _ in range(L)]
     total, outs = 0, []
     wide = _Widened(dtype)
     for x in xs:
+        if codes:
+            x = rvq_ref(oracle, cfg, w, x, dtype)
         B, T, _ = x.shape
+        pos = caches[0].current_seq_len() if mask == "cache_len" else total
         for l in range(L):
             p = f"layers.{l}."
             y = oracle.layer_norm(x, w[p + "norm1.weight"], w[p + "norm1.bias"], cfg.eps, dtype)
             q, k, v = oracle.split_qkv(_mm(y, w[p + "self_attn.in_proj_weight"], dtype, wide), H)
-            q = oracle.rope(q, cos, sin, total, dtype, interleaved=True)
-            k = oracle.rope(k, cos, sin, total, dtype, interleaved=True)
+            q = oracle.rope(q, cos, sin, pos, dtype, interleaved=True)
+            k = oracle.rope(k, cos, sin, pos, dtype, interleaved=True)
             kk, vv = caches[l].append(k, v)
-            offset = total if mask == "absolute" else kk.shape[2] - T
+            offset = kk.shape[2] - T if mask == "relative" else pos
             a = oracle.attention_step(q, kk, vv, scale, offset, dtype).reshape(B, T, D)
             attn = _mm(a, w[p + "self_attn.out_proj.weight"], dtype, wide)
             x = oracle.residual_prologue(x, attn, w[p + "layer_scale_1.scale"], dtype)

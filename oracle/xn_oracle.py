@@ -292,6 +292,10 @@ class KvCacheRef:
         self.k = self.v = None
         self.max_seq_len = max_seq_len
 
+    def current_seq_len(self) -> int:
+        """KvCache::current_seq_len (mimi-rs/src/models/mimi.rs:1115-1120)."""
+        return 0 if self.k is None else self.k.shape[2]
+
     def append(self, k, v):
         if self.k is None:
             nk, nv = k, v

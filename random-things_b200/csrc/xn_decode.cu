@@ -192,7 +192,13 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
   const int64_t n = total + p.t;
   const int64_t kv_len = n < p.context ? n : p.context;
   const int64_t first = n - kv_len;  // position of logical key 0
-  const int64_t last_visible = p.mask_mode == XN_MASK_ABSOLUTE ? total + i : i + kv_len - p.t;
+  // XN_MASK_CACHE_LEN shows the keys of XN_MASK_ABSOLUTE: its offset
+  // min(total, context) differs from total only when total >= context, and then
+  // every one of the kv_len <= context keys is visible under either offset.
+  const int64_t last_visible = p.mask_mode != XN_MASK_RELATIVE ? total + i : i + kv_len - p.t;
+  // Position of query / new row i2 in the RoPE tables: total + i2, or the
+  // cache's length before the step + i2 (XN_MASK_CACHE_LEN).
+  const int64_t rope0 = p.mask_mode == XN_MASK_CACHE_LEN && total > p.context ? p.context : total;
   const int64_t nvis = last_visible + 1 < kv_len ? last_visible + 1 : kv_len;
   // Logical key j sits at slot (first + j) % cap; j < kv_len <= cap, so one
   // conditional subtraction replaces the per-key division.
@@ -209,7 +215,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
   const int tid = threadIdx.x;
 
   if constexpr (kFused) {
-    if (total < 0 || total + p.t > p.max_pos) {  // device position past the tables
+    if (total < 0 || rope0 + p.t > p.max_pos) {  // device position past the tables
       if (tid == 0 && p.err_flag != nullptr) atomicOr(p.err_flag, 1);
       return;  // uniform over the block, before any barrier
     }
@@ -228,11 +234,11 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
         which = 0;
         i2 = i;
       }
-      const int64_t pos = total + i2;
+      const int64_t pos = total + i2;  // ring position
       const T *src = static_cast<const T *>(p.qkv) + ((bi * p.t + i2) * 3 + which) * p.h * D + hh * D;
       T *dst = which == 1 ? kw + (pos % p.cap) * D : vw + (pos % p.cap) * D;
-      const T *cs = static_cast<const T *>(p.cos) + pos * half;
-      const T *sn = static_cast<const T *>(p.sin) + pos * half;
+      const T *cs = static_cast<const T *>(p.cos) + (rope0 + i2) * half;
+      const T *sn = static_cast<const T *>(p.sin) + (rope0 + i2) * half;
       if constexpr (kInterleaved) {
         const int e = c * V;
         uint4 y = ld_stream(src + e);
@@ -438,7 +444,7 @@ int xn_attention_decode(void *out, const void *q, const void *k_cache, const voi
     return fail(XN_E_INVALID, "%s: need 0 < context <= cap and context <= %d (context=%lld cap=%lld)", op,
                 kMaxContext, (long long)context, (long long)cap);
   if (t > cap) return fail(XN_E_INVALID, "%s: t=%lld exceeds cap=%lld", op, (long long)t, (long long)cap);
-  if (mask_mode != XN_MASK_RELATIVE && mask_mode != XN_MASK_ABSOLUTE)
+  if (mask_mode != XN_MASK_RELATIVE && mask_mode != XN_MASK_ABSOLUTE && mask_mode != XN_MASK_CACHE_LEN)
     return fail(XN_E_INVALID, "%s: unknown mask mode %d", op, mask_mode);
   if (total_dev == nullptr && total < 0) return fail(XN_E_INVALID, "%s: negative position %lld", op, (long long)total);
   if (b * h > 0x7fffffffLL || t > 65535) return fail(XN_E_INVALID, "%s: grid too large (b*h=%lld, t=%lld)", op, (long long)(b * h), (long long)t);
@@ -465,12 +471,14 @@ int xn_decode_attention_step(void *out, void *k_cache, void *v_cache, const void
     return fail(XN_E_INVALID, "%s: need 0 < context <= cap and context <= %d (context=%lld cap=%lld)", op,
                 kMaxContext, (long long)context, (long long)cap);
   if (t > cap) return fail(XN_E_INVALID, "%s: t=%lld new positions exceed cap=%lld", op, (long long)t, (long long)cap);
-  if (mask_mode != XN_MASK_RELATIVE && mask_mode != XN_MASK_ABSOLUTE)
+  if (mask_mode != XN_MASK_RELATIVE && mask_mode != XN_MASK_ABSOLUTE && mask_mode != XN_MASK_CACHE_LEN)
     return fail(XN_E_INVALID, "%s: unknown mask mode %d", op, mask_mode);
   if (total_dev == nullptr) {
     if (total < 0) return fail(XN_E_INVALID, "%s: negative position %lld", op, (long long)total);
-    if (total + t > max_pos)
-      return fail(XN_E_RANGE, "%s: pos %lld + t %lld exceeds the %lld rows of cos/sin", op, (long long)total,
+    // The rows rotate at total + i, or at min(total, context) + i (XN_MASK_CACHE_LEN).
+    const int64_t rope0 = mask_mode == XN_MASK_CACHE_LEN && total > context ? context : total;
+    if (rope0 + t > max_pos)
+      return fail(XN_E_RANGE, "%s: pos %lld + t %lld exceeds the %lld rows of cos/sin", op, (long long)rope0,
                   (long long)t, (long long)max_pos);
   }
   if (b * h > 0x7fffffffLL || t > 65535) return fail(XN_E_INVALID, "%s: grid too large (b*h=%lld, t=%lld)", op, (long long)(b * h), (long long)t);

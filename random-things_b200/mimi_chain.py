@@ -107,6 +107,14 @@ class MimiDecoderChain:
         # StreamingMultiheadAttention: T::from_f32(1 / sqrt(head_dim)) (mimi.rs:1361).
         self.scale = float(torch.tensor(1.0 / math.sqrt(cfg.head_dim), dtype=torch.float32).to(dtype).float())
         self.books = [weights[f"quantizer.codebook.{i}"] for i in range(cfg.n_q)]
+        # When a list, every op's inputs and outputs are appended to it as
+        # (name, layer, tensor copy): the tests check each fused op on the
+        # exact inputs it received (GEMM outputs included).
+        self.trace: list | None = None
+
+    def _rec(self, name: str, layer: int, t: torch.Tensor) -> None:
+        if self.trace is not None:
+            self.trace.append((name, layer, t.detach().clone()))
 
     # -- RVQ ---------------------------------------------------------------
     def rvq_decode(self, codes: torch.Tensor) -> torch.Tensor:
@@ -116,8 +124,10 @@ class MimiDecoderChain:
         w = self.w
         first = xn.rvq_decode_sum(self.books[:1], codes[:, :1].contiguous(), out_layout="btd")
         x = torch.matmul(first, w["quantizer.rvq_first.output_proj"].t())
+        self._rec("rvq_first", -1, first)
         if self.cfg.n_q > 1:
             rest = xn.rvq_decode_sum(self.books[1:], codes[:, 1:].contiguous(), out_layout="btd")
+            self._rec("rvq_rest", -1, rest)
             x = x + torch.matmul(rest, w["quantizer.rvq_rest.output_proj"].t())
         return x
 
@@ -139,6 +149,8 @@ class MimiDecoderChain:
             scores = torch.matmul(q, k.transpose(2, 3))  # [B, H, T, T]
             probs = xn.attn_softmax(scores, self.scale, offset)
             ctx = torch.matmul(probs, v)  # [B, H, T, hd]
+            for name, t in (("qkv", qkv), ("q", q), ("k", k), ("v", v), ("scores", scores), ("probs", probs)):
+                self._rec(name, l, t)
         else:
             q, k = xn.rope_qk_packed(qkv, H, self.cos, self.sin, offset, interleaved=True)  # [B, T, H, hd]
             v = qkv[..., 2 * D:].view(B, T, H, hd)
@@ -150,7 +162,9 @@ class MimiDecoderChain:
     def mlp(self, l: int, y: torch.Tensor) -> torch.Tensor:
         w = self.w
         h = torch.matmul(y, w[f"layers.{l}.linear1.weight"].t())
+        self._rec("h_pre", l, h)
         xn.unary_(h, h, "gelu_erf")
+        self._rec("h", l, h)
         return torch.matmul(h, w[f"layers.{l}.linear2.weight"].t())
 
     def transformer(self, x: torch.Tensor, offset: int = 0) -> torch.Tensor:
@@ -160,20 +174,27 @@ class MimiDecoderChain:
         eps = cfg.eps
         resid = x
         y = xn.layer_norm(resid, w["layers.0.norm1.weight"], w["layers.0.norm1.bias"], eps)
+        self._rec("x", 0, resid)
+        self._rec("y", 0, y)
         for l in range(cfg.num_layers):
             p = f"layers.{l}."
             attn = self.attention(l, y, offset)
             # xs = xs + ls1 * attn ; norm2(xs)
             y2, resid = xn.layer_norm_residual(resid, attn, w[p + "norm2.weight"], w[p + "norm2.bias"], eps,
                                                layer_scale=w[p + "layer_scale_1.scale"])
+            for name, t in (("attn", attn), ("y2", y2), ("resid_mid", resid)):
+                self._rec(name, l, t)
             m = self.mlp(l, y2)
+            self._rec("m", l, m)
             if l + 1 < cfg.num_layers:
                 # xs = xs + ls2 * mlp ; next layer's norm1(xs)
                 q = f"layers.{l + 1}."
                 y, resid = xn.layer_norm_residual(resid, m, w[q + "norm1.weight"], w[q + "norm1.bias"], eps,
                                                   layer_scale=w[p + "layer_scale_2.scale"])
+                self._rec("y", l + 1, y)
             else:
                 resid = xn.residual_add(resid, m, w[p + "layer_scale_2.scale"])
+            self._rec("resid", l, resid)
         return resid
 
     def decode(self, codes: torch.Tensor) -> torch.Tensor:
@@ -215,6 +236,12 @@ class StreamingDecoderChain:
         self.total = 0
         self.total_dev = torch.zeros(1, dtype=torch.int64, device=dev)
         self.graph = None
+        # As MimiDecoderChain.trace (eager steps only; None while capturing).
+        self.trace: list | None = None
+
+    def _rec(self, name: str, layer: int, t: torch.Tensor) -> None:
+        if self.trace is not None:
+            self.trace.append((name, layer, t.detach().clone()))
 
     def reset(self) -> None:
         """Forget the stream (the caches' contents are overwritten as it refills)."""
@@ -226,6 +253,8 @@ class StreamingDecoderChain:
         H = cfg.num_heads
         resid = x
         y = xn.layer_norm(resid, w["layers.0.norm1.weight"], w["layers.0.norm1.bias"], eps)
+        self._rec("x", 0, resid)
+        self._rec("y", 0, y)
         for l in range(cfg.num_layers):
             p = f"layers.{l}."
             qkv = torch.matmul(y, w[p + "self_attn.in_proj_weight"].t())
@@ -235,28 +264,41 @@ class StreamingDecoderChain:
             y2, resid = xn.layer_norm_residual(resid, attn, w[p + "norm2.weight"], w[p + "norm2.bias"], eps,
                                                layer_scale=w[p + "layer_scale_1.scale"])
             h = torch.matmul(y2, w[p + "linear1.weight"].t())
+            self._rec("h_pre", l, h)
             xn.unary_(h, h, self.act)
             m = torch.matmul(h, w[p + "linear2.weight"].t())
+            for name, t in (("qkv", qkv), ("a", a), ("attn", attn), ("y2", y2), ("resid_mid", resid), ("h", h),
+                            ("m", m)):
+                self._rec(name, l, t)
             if l + 1 < cfg.num_layers:
                 q_ = f"layers.{l + 1}."
                 y, resid = xn.layer_norm_residual(resid, m, w[q_ + "norm1.weight"], w[q_ + "norm1.bias"], eps,
                                                   layer_scale=w[p + "layer_scale_2.scale"])
+                self._rec("y", l + 1, y)
             else:
                 resid = xn.residual_add(resid, m, w[p + "layer_scale_2.scale"])
+            self._rec("resid", l, resid)
         return resid
+
+    def _frames(self, x: torch.Tensor) -> int:
+        """New positions in a step input (x [B, t, D])."""
+        return x.shape[1]
+
+    def _static_input(self, t: int) -> torch.Tensor:
+        """The graph's input buffer for steps of t frames."""
+        return torch.zeros((self.batch, t, self.cfg.d_model), dtype=self.k[0].dtype, device=self.total_dev.device)
 
     def step(self, x: torch.Tensor) -> torch.Tensor:
         """One eager step on x [B, t, D] with the host-side position."""
         out = self._layers(x, self.total, None)
-        self.total += x.shape[1]
+        self.total += self._frames(x)
         self.total_dev.fill_(self.total)
         return out
 
     def capture(self, t: int = 1) -> None:
         """Records one step of t frames (reading the device position) as a CUDA graph."""
-        cfg = self.cfg
         dev = self.total_dev.device
-        self.x_static = torch.zeros((self.batch, t, cfg.d_model), dtype=self.k[0].dtype, device=dev)
+        self.x_static = self._static_input(t)
         saved = self.total_dev.clone()
         stream = torch.cuda.Stream(dev)
         stream.wait_stream(torch.cuda.current_stream(dev))
@@ -278,3 +320,35 @@ class StreamingDecoderChain:
         self.graph.replay()
         self.total += self.graph_t
         return self.out_static
+
+
+class MimiStreamingDecoder(StreamingDecoderChain):
+    """Mimi::decode_step (mimi-rs/src/models/mimi.rs:2059-2071) on the fused
+    ops, without its conv stages (the transposed-conv upsample and the SEANet
+    decoder): each step takes the codes of t frames [B, n_q, t] (int64),
+    decodes them with the two RVQ gather-sums and their 1x1 projections
+    (SplitResidualVectorQuantizer::decode, :1858-1868), and runs one step of
+    the decoder transformer (Transformer::step -> StreamingTransformer::forward,
+    :1560-1571, 1476-1483) with mimi-rs's position bookkeeping: every layer's
+    offset is the layer-0 cache's length before the step, min(total,
+    context), used as the rope_i position and the causal-mask offset; caches
+    keep the last `context` (250) positions as ring buffers. GELU(erf) MLP.
+    `capture(t)` records the whole step (RVQ + all layers + the position
+    advance) as one CUDA graph over a static codes buffer."""
+
+    def __init__(self, cfg: MimiChainConfig, weights: dict[str, torch.Tensor], cos: torch.Tensor,
+                 sin: torch.Tensor, batch: int, context: int | None = None):
+        super().__init__(cfg, weights, cos, sin, batch, act="gelu_erf", mask="cache_len", context=context)
+        self.rvq = MimiDecoderChain(cfg, weights, cos, sin)
+
+    def _layers(self, codes: torch.Tensor, total: int | None, total_dev: torch.Tensor | None) -> torch.Tensor:
+        self.rvq.trace = self.trace
+        x = self.rvq.rvq_decode(codes)
+        self.rvq.trace = None
+        return super()._layers(x, total, total_dev)
+
+    def _frames(self, codes: torch.Tensor) -> int:
+        return codes.shape[2]
+
+    def _static_input(self, t: int) -> torch.Tensor:
+        return torch.zeros((self.batch, self.cfg.n_q, t), dtype=torch.int64, device=self.total_dev.device)

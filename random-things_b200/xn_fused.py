@@ -26,7 +26,8 @@ XN_OK, XN_E_INVALID, XN_E_DTYPE, XN_E_RANGE, XN_E_CUDA = 0, 1, 2, 3, 4
 XN_UNARY_SILU, XN_UNARY_GELU_ERF = 0, 1
 XN_LAYOUT_BHTD, XN_LAYOUT_BTHD = 0, 1
 XN_RVQ_MAX_CODEBOOKS = 32
-XN_MASK_RELATIVE, XN_MASK_ABSOLUTE = 0, 1
+XN_MASK_RELATIVE, XN_MASK_ABSOLUTE, XN_MASK_CACHE_LEN = 0, 1, 2
+MASK_MODES = {"relative": XN_MASK_RELATIVE, "absolute": XN_MASK_ABSOLUTE, "cache_len": XN_MASK_CACHE_LEN}
 
 # Same codes as `enum DType` (mimi-rs/src/dtype.rs:4-10).
 DTYPE_CODES = {
@@ -683,8 +684,7 @@ def attention_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     _check_same_shape(k_cache.shape, v_cache.shape, f"{op} caches")
     if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
         raise XnError(f"{op}: caches must be contiguous")
-    modes = {"relative": XN_MASK_RELATIVE, "absolute": XN_MASK_ABSOLUTE}
-    if mask not in modes:
+    if mask not in MASK_MODES:
         raise XnError(f"{op}: unknown mask mode {mask!r}")
     tot, tdev = _total_args(total, total_dev, op)
     if out is None:
@@ -694,7 +694,7 @@ def attention_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     _dev(q, k_cache, v_cache, out)
     _same_dtype(q, k_cache, v_cache, out)
     _call("xn_attention_decode", _p(out), _p(q), _p(k_cache), _p(v_cache), b, h, t, d, tot, tdev,
-          k_cache.shape[2], int(context), modes[mask], float(scale), _dtype_code(q), _stream(q))
+          k_cache.shape[2], int(context), MASK_MODES[mask], float(scale), _dtype_code(q), _stream(q))
     return out
 
 
@@ -705,7 +705,10 @@ def decode_attention_step(qkv: torch.Tensor, heads: int, cos: torch.Tensor, sin:
                           out: torch.Tensor | None = None) -> torch.Tensor:
     """kv_append_rope followed by attention_decode in one launch (q stays on
     chip): the step's attention output [B, T, H*D] from the packed projection
-    qkv [B, T, 3*H*D], with the caches updated as kv_append_rope does."""
+    qkv [B, T, 3*H*D], with the caches updated as kv_append_rope does.
+    mask "cache_len" is mimi-rs's StreamingTransformer (mimi.rs:1476-1487):
+    the new rows rotate at the cache's length before the step,
+    min(total, context), which is also the mask offset."""
     op = "decode_attention_step"
     if qkv.dim() != 3 or not qkv.is_contiguous():
         raise XnError(f"{op}: expected a contiguous [B, T, 3*H*D] projection, got {tuple(qkv.shape)}")
@@ -722,12 +725,13 @@ def decode_attention_step(qkv: torch.Tensor, heads: int, cos: torch.Tensor, sin:
     max_pos, d_over_2 = cos.shape
     if d_over_2 * 2 != d:
         raise XnError(f"{op} requires even d dimension, got d={d}")
-    modes = {"relative": XN_MASK_RELATIVE, "absolute": XN_MASK_ABSOLUTE}
-    if mask not in modes:
+    if mask not in MASK_MODES:
         raise XnError(f"{op}: unknown mask mode {mask!r}")
     tot, tdev = _total_args(total, total_dev, op)
-    if tdev is None and tot + t > max_pos:
-        raise XnError(f"{op} position out of range, pos={tot} + t={t} > max_pos={max_pos}", XN_E_RANGE)
+    # The new rows rotate at total + i, or at min(total, context) + i ("cache_len").
+    rope0 = min(tot, int(context)) if mask == "cache_len" else tot
+    if tdev is None and rope0 + t > max_pos:
+        raise XnError(f"{op} position out of range, pos={rope0} + t={t} > max_pos={max_pos}", XN_E_RANGE)
     if out is None:
         out = torch.empty((b, t, heads * d), dtype=qkv.dtype, device=qkv.device)
     elif out.numel() != b * t * heads * d or not out.is_contiguous():
@@ -739,7 +743,7 @@ def decode_attention_step(qkv: torch.Tensor, heads: int, cos: torch.Tensor, sin:
         if err_flag.dtype != torch.int32:
             raise XnError(f"{op}: err_flag must be an int32 CUDA tensor")
     _call("xn_decode_attention_step", _p(out), _p(k_cache), _p(v_cache), _p(qkv), _p(cos), _p(sin), b, heads, t,
-          d, tot, tdev, max_pos, k_cache.shape[2], int(context), modes[mask], float(scale), int(interleaved),
+          d, tot, tdev, max_pos, k_cache.shape[2], int(context), MASK_MODES[mask], float(scale), int(interleaved),
           _dtype_code(qkv), _p(err_flag), _stream(qkv))
     return out
 
