@@ -344,8 +344,10 @@ def mimi_rate(torch, device, steps: int, batch: int = 4, frames: int = 250) -> d
     return {"frames_per_s": round(n / (ms * 1e-3), 1), "ms_per_decode": round(ms, 4),
             "e2e_frames_per_s": round(n / (ms_e2e * 1e-3), 1), "batch": batch, "frames": frames,
             "dtype": "bf16", "layers": cfg.num_layers, "d_model": cfg.d_model, "codebooks": cfg.n_q,
-            "what": "RVQ decode (8 x 2048 x 256) + 8-layer decoder transformer (LN, RoPE, causal softmax, GELU "
-                    "fused ops; GEMMs on cuBLAS), one CUDA graph; seeded synthetic weights"}
+            "what": "whole-sequence (non-streaming) decode, Mimi::decode's path without the conv stages: RVQ decode "
+                    "(8 x 2048 x 256) + 8-layer decoder transformer over all 250 frames at once (LN, RoPE, causal "
+                    "softmax, GELU fused ops; GEMMs on cuBLAS), one CUDA graph; not the reference's streaming "
+                    "realtime loop, which is mimi_stream_decode; seeded synthetic weights"}
 
 
 def gather_context(torch, xn, device, reps: int = 7) -> list:
@@ -387,6 +389,237 @@ def gather_context(torch, xn, device, reps: int = 7) -> list:
             dict(after="write flush + clean read", **timed(lambda: (wflush.zero_(), rflush.sum()))),
             dict(after="swiglu (the step's last op)", **timed(lambda: xn.swiglu_(act, gate, up))),
             dict(after="swiglu + clean read", **timed(lambda: (xn.swiglu_(act, gate, up), rflush.sum())))]
+
+
+# ---------------------------------------------------------------------------
+# Benchmark config 1: the CPU-runnable f32 micro-pipeline, timed on the GPU.
+# ---------------------------------------------------------------------------
+C1 = dict(tokens=512, hidden=2048, heads=16, head_dim=128, inter=5632, theta=10000.0, eps=1e-5)
+
+
+def l2_flusher(torch, device):
+    """Returns flush(): writes 256 MB (> the 126 MB L2), then reads another
+    256 MB buffer, so the L2 holds only clean lines of the second buffer and a
+    launch timed after it pays for no write-back of the flush."""
+    wbuf = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+    rbuf = torch.zeros(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+
+    def flush():
+        wbuf.zero_()
+        rbuf.sum()
+    return flush
+
+
+def time_flushed(torch, fn, flush, reps: int) -> float:
+    """Median CUDA-event time (ms) of fn() over `reps` launches, each after an
+    L2 flush and a fixed GPU spin (so host launch latency never falls between
+    the two events)."""
+    times = []
+    for _ in range(reps):
+        flush()
+        torch.cuda._sleep(1_000_000)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    return statistics.median(times)
+
+
+def config1_rate(torch, xn, device, reps: int = 20) -> dict:
+    """Benchmark config 1 (f32, seeded): x ~ N(0,1) [1, 512, 2048] -> RMSNorm
+    (eps 1e-5, weight ~ N(1, 0.02)); RoPE (theta 1e4, half-split) on Q / K
+    [1, 512, 16, 128] ~ N(0,1) at positions 0..511 ([B, T, H, D], no
+    transposes); SwiGLU on gate / up [1, 512, 5632] ~ N(0,1); causal softmax
+    over [1, 16, 512, 512] logits ~ N(0, 4). Each op is timed alone after an
+    L2 flush (every input is smaller than the L2), then the four ops as one
+    CUDA graph after a flush. The reference CPU backend's own path for these
+    ops is cpu_backend.rs:359-392, 667-709."""
+    c = C1
+    g = torch.Generator(device=device).manual_seed(11)
+    T, H, NH, D, I = c["tokens"], c["hidden"], c["heads"], c["head_dim"], c["inter"]
+
+    def rnd(*shape, std=1.0, mean=0.0):
+        t = torch.empty(shape, dtype=torch.float32, device=device)
+        return t.normal_(mean, std, generator=g)
+
+    x, w = rnd(1, T, H), rnd(H, std=0.02, mean=1.0)
+    y = torch.empty_like(x)
+    q, k = rnd(1, T, NH, D), rnd(1, T, NH, D)
+    qo, ko = torch.empty_like(q), torch.empty_like(k)
+    half = D // 2
+    inv = 1.0 / (c["theta"] ** (torch.arange(half, dtype=torch.float32) * 2.0 / D))
+    ang = torch.arange(T, dtype=torch.float32)[:, None] * inv[None, :]
+    cos, sin = ang.cos().to(device), ang.sin().to(device)
+    gate, up = rnd(1, T, I), rnd(1, T, I)
+    act = torch.empty_like(gate)
+    logits = rnd(1, NH, T, T, std=2.0)
+    probs = torch.empty_like(logits)
+    s = 4
+    live = NH * T * (T + 1) // 2  # unmasked logits: row i reads i + 1 of them
+    ops = {
+        "rms_norm": (lambda: xn.rms_norm_(y, x, w, c["eps"]), 2 * T * H * s + H * s),
+        "rope_qk": (lambda: xn.rope_qk(q, k, cos, sin, 0, layout="bthd", out=(qo, ko)),
+                    2 * 2 * T * NH * D * s + 2 * T * half * s),
+        "swiglu": (lambda: xn.swiglu_(act, gate, up), 3 * T * I * s),
+        "softmax_causal": (lambda: xn.softmax_causal_(probs, logits, 0), (live + NH * T * T) * s),
+    }
+    flush = l2_flusher(torch, device)
+    peak, _ = measured_peak()
+    for fn, _ in ops.values():
+        fn()
+    out = {}
+    for name, (fn, nbytes) in ops.items():
+        ms = time_flushed(torch, fn, flush, reps)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"us": round(ms * 1e3, 2), "bytes": nbytes, "gbs": round(gbs, 1), "frac": round(gbs / peak, 3)}
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    stream = torch.cuda.Stream(device)
+    stream.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(stream):
+        for fn, _ in ops.values():
+            fn()
+    torch.cuda.current_stream(device).wait_stream(stream)
+    torch.cuda.synchronize()
+    with torch.cuda.graph(graph, stream=stream):
+        for fn, _ in ops.values():
+            fn()
+    ms = time_flushed(torch, graph.replay, flush, reps)
+    total = sum(b for _, b in ops.values())
+    del graph
+    return {"per_op": out, "pipeline_us": round(ms * 1e3, 2), "pipeline_bytes": total,
+            "pipeline_gbs": round(total / (ms * 1e-3) / 1e9, 1),
+            "pipeline_frac": round(total / (ms * 1e-3) / 1e9 / peak, 3),
+            "what": "benchmark config 1, f32: RMSNorm [512, 2048], RoPE half-split on Q/K [1, 512, 16, 128] (BTHD), "
+                    "SwiGLU [512, 5632], causal softmax [1, 16, 512, 512]; each op after an L2 flush (inputs are "
+                    "smaller than L2), median of launches; pipeline = the four ops as one CUDA graph after a flush; "
+                    "causal softmax bytes = unmasked reads + all writes"}
+
+
+# ---------------------------------------------------------------------------
+# Mimi streaming decode (benchmark config 2 shapes, frame by frame).
+# ---------------------------------------------------------------------------
+def mimi_stream_rate(torch, device, steps: int, batch: int = 4) -> dict:
+    """Mimi::decode_step without its conv stages (mimi_chain.MimiStreamingDecoder):
+    per step the codes of one frame [B, 8, 1] -> RVQ decode (8 x 2048 x 256)
+    -> one step of the 8-layer decoder transformer (context-250 ring KV
+    caches, offset = min(frames seen, 250)), one captured CUDA graph per step.
+    `steps` frames from an empty cache (past 250, so the steady state with a
+    full context is included); frames/s = batch x steps / time. End to end:
+    each step's codes copied from pinned host memory and its output read back."""
+    import mimi_chain as mc
+
+    cfg = mc.MimiChainConfig()
+    w = mc.synthetic_weights(cfg, torch.bfloat16, device, seed=7)
+    cos, sin = mc.rope_tables(cfg, torch.bfloat16, device)
+    dec = mc.MimiStreamingDecoder(cfg, w, cos, sin, batch, context=cfg.context)
+    g = torch.Generator(device=device).manual_seed(12)
+    codes = torch.randint(0, cfg.bins, (steps, batch, cfg.n_q, 1), dtype=torch.int64, device=device, generator=g)
+    dec.capture(1)
+    for s in range(3):
+        dec.step_graph(codes[s])
+    torch.cuda.synchronize()
+    dec.reset()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for s in range(steps):
+        dec.step_graph(codes[s])
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / steps
+    codes_h = codes.cpu().pin_memory()
+    out_h = torch.empty(dec.out_static.shape, dtype=torch.bfloat16, pin_memory=True)
+    dec.reset()
+    torch.cuda.synchronize()
+    e0.record()
+    for s in range(steps):
+        dec.x_static.copy_(codes_h[s], non_blocking=True)
+        dec.graph.replay()
+        out_h.copy_(dec.out_static, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    us_e2e = e0.elapsed_time(e1) * 1e3 / steps
+    del dec
+    return {"us_per_step": round(us, 2), "frames_per_s": round(batch / (us * 1e-6), 1),
+            "e2e_us_per_step": round(us_e2e, 2), "e2e_frames_per_s": round(batch / (us_e2e * 1e-6), 1),
+            "batch": batch, "steps": steps, "context": cfg.context, "dtype": "bf16", "layers": cfg.num_layers,
+            "h2d_bytes_per_step": batch * cfg.n_q * 8, "d2h_bytes_per_step": batch * cfg.d_model * 2,
+            "what": "Mimi::decode_step without the conv upsample / SEANet decoder: RVQ decode of one frame + one "
+                    "step of the 8-layer decoder transformer with context-250 ring KV caches (fused LN/residual, "
+                    "KV append + RoPE + decode attention, GELU; GEMMs on cuBLAS), one CUDA graph per step; the "
+                    "reference's streaming realtime loop (mimi-rs/examples/mimi.rs:220-235) at batch 4; seeded "
+                    "synthetic weights"}
+
+
+def cpu_mimi_stream_rate(steps: int = 3, batch: int = 4) -> dict:
+    """The reference streaming op sequence of mimi_stream_rate on the CPU oracle
+    (oracle ops single-threaded, numpy f32 GEMMs rounded to bf16): mean time
+    per step of the steps after a warm-up step."""
+    import numpy as np
+
+    import mimi_chain as mc
+    import mimi_oracle
+    import xn_oracle
+    import torch
+
+    cfg = mc.MimiChainConfig()
+    w = {k: mimi_oracle.to_storage(v.float().numpy(), "bf16")
+         for k, v in mc.synthetic_weights(cfg, torch.float32, "cpu", seed=7).items()}
+    cos, sin = (mimi_oracle.to_storage(t.float().numpy(), "bf16") for t in mc.rope_tables(cfg, torch.float32, "cpu"))
+    r = np.random.default_rng(12)
+    codes = [r.integers(0, cfg.bins, size=(batch, cfg.n_q, 1), dtype=np.int64) for _ in range(steps + 1)]
+    with _oracle_threads(xn_oracle, 1):
+        t0 = time.perf_counter()
+        mimi_oracle.stream_ref(xn_oracle, cfg, w, cos, sin, codes[:1], "bf16", 0.125, cfg.context,
+                               mask="cache_len", codes=True)
+        t1 = time.perf_counter()
+        mimi_oracle.stream_ref(xn_oracle, cfg, w, cos, sin, codes, "bf16", 0.125, cfg.context, mask="cache_len",
+                               codes=True)
+        t2 = time.perf_counter()
+    us = ((t2 - t1) - (t1 - t0)) / steps * 1e6
+    return {"us_per_step": round(us, 1), "frames_per_s": round(batch / (us * 1e-6), 1),
+            "sample": f"steps 2..{steps + 1} of a stream at batch {batch}, bf16, oracle ops single-threaded + "
+                      f"numpy f32 GEMMs on {os.cpu_count()} BLAS threads"}
+
+
+def cpu_config1_rate(reps: int = 3) -> dict:
+    """Benchmark config 1 on the CPU oracle (row-parallel ops on every host
+    core, unary/binary single-threaded as the reference): per-op and
+    pipeline time."""
+    import numpy as np
+
+    import xn_oracle as o
+
+    o.build()
+    threads = os.cpu_count() or 1
+    c = C1
+    r = np.random.default_rng(11)
+    T, H, NH, D, I = c["tokens"], c["hidden"], c["heads"], c["head_dim"], c["inter"]
+    f = lambda *shape, std=1.0, mean=0.0: (r.standard_normal(shape, dtype=np.float32) * np.float32(std)  # noqa: E731
+                                          + np.float32(mean)).astype(np.float32)
+    x, w = f(1, T, H), f(H, std=0.02, mean=1.0)
+    q = np.ascontiguousarray(np.transpose(f(1, T, NH, D), (0, 2, 1, 3)))  # the reference rotates [B, H, T, D]
+    k = np.ascontiguousarray(np.transpose(f(1, T, NH, D), (0, 2, 1, 3)))
+    cos, sin = o.rope_tables(D, T, c["theta"], "f32", "llama")
+    gate, up, logits = f(1, T, I), f(1, T, I), f(1, NH, T, T, std=2.0)
+    ops = {"rms_norm": lambda: o.rms_norm(x, w, c["eps"], "f32"),
+           "rope_qk": lambda: (o.rope(q, cos, sin, 0, "f32"), o.rope(k, cos, sin, 0, "f32")),
+           "swiglu": lambda: o.swiglu(gate, up, "f32"),
+           "softmax_causal": lambda: o.softmax_causal(logits, 0, "f32")}
+    o.set_num_threads(threads)
+    out = {}
+    for name, fn in ops.items():
+        fn()
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        out[name] = {"us": round(statistics.median(ts) * 1e6, 1)}
+    return {"per_op": out, "pipeline_us": round(sum(v["us"] for v in out.values()), 1), "cores": threads,
+            "sample": "the whole config-1 pipeline (it is CPU-sized), median of 3 runs per op"}
 
 
 DECODE_CFG = dict(d_model=1024, num_heads=16, num_layers=6, dim_feedforward=4096)
@@ -485,13 +718,16 @@ SWEEP_EXTRA_OPS = ["silu", "gelu_erf", "residual_add", "softmax_causal", "causal
 RVQ_BINS, RVQ_BOOKS = 2048, 8
 
 
-def sweep(torch, xn, device, widths, rows_list, dtypes, reps: int, mem_cap_gb: float, ops=SWEEP_OPS) -> list[dict]:
-    # L2 flush before every timed launch: write 256 MB (> the 126 MB L2), then
-    # read another 256 MB buffer, so the L2 holds only clean lines of the
-    # second buffer and the timed launch pays for no write-back of the flush.
-    # Events are created per launch inside the loop below.
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
-    flush_clean = torch.zeros(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+def sweep(torch, xn, device, widths, rows_list, dtypes, reps: int, mem_cap_gb: float, ops=SWEEP_OPS,
+          world: int = 1, rank: int = 0) -> list[dict]:
+    """Each point: `rows` x `cols` of one op. With world > 1 (torchrun), the
+    rows are sharded across the ranks (xn_shard_rows; causal ops by whole
+    1024-query slices), every rank times its shard after a barrier, and a
+    point's time is the max over ranks of each launch (strong scaling: the
+    GB/s are the whole point's bytes over that time)."""
+    import torch.distributed as dist
+
+    flush = l2_flusher(torch, device)
     out = []
     for dname in dtypes:
         dt = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}[dname]
@@ -502,15 +738,29 @@ def sweep(torch, xn, device, widths, rows_list, dtypes, reps: int, mem_cap_gb: f
                     n_tensors = {"rms_norm_residual": 4, "layer_norm": 2, "rope": 2, "swiglu": 3, "softmax": 2,
                                  "embedding_gather": 1, "silu": 2, "gelu_erf": 2, "residual_add": 3,
                                  "softmax_causal": 2, "causal_mask": 1, "rvq_decode": 1}[op]
-                    need = n_tensors * rows * cols * s + (32768 * cols * s if op == "embedding_gather" else 0) + \
-                        (RVQ_BOOKS * (RVQ_BINS * cols * s + rows * 8) if op == "rvq_decode" else 0)
-                    point = {"op": op, "dtype": dname, "rows": rows, "cols": cols}
+                    point = {"op": op, "dtype": dname, "rows": rows, "cols": cols, "n_gpus": world}
+                    # Causal ops: prefill-shaped scores, slices of t1 = 1024 queries over `cols`
+                    # keys, the last query seeing every key (offset = cols - t1).
+                    t1 = min(1024, rows)
+                    unit = t1 if op in ("softmax_causal", "causal_mask") else 1
+                    if rows % unit:
+                        point["skipped"] = "rows must be a multiple of the 1024-query slice"
+                        out.append(point)
+                        continue
+                    _, cnt = xn.shard_rows(rows // unit, world, rank)
+                    lrows = cnt * unit  # this rank's rows
+                    need = n_tensors * lrows * cols * s + (32768 * cols * s if op == "embedding_gather" else 0) + \
+                        (RVQ_BOOKS * (RVQ_BINS * cols * s + lrows * 8) if op == "rvq_decode" else 0)
                     if need > mem_cap_gb * 1e9:
                         point["skipped"] = f"needs {need / 1e9:.1f} GB > cap {mem_cap_gb} GB"
                         out.append(point)
                         continue
+                    if op == "rope" and cols % 128:
+                        point["skipped"] = "rope needs width = heads x 128"
+                        out.append(point)
+                        continue
                     g = torch.Generator(device=device)
-                    g.manual_seed(rows + cols)
+                    g.manual_seed(rows + cols + rank)
 
                     def rnd(*shape):
                         t = torch.empty(shape, dtype=torch.float32, device=device)
@@ -518,53 +768,43 @@ def sweep(torch, xn, device, widths, rows_list, dtypes, reps: int, mem_cap_gb: f
                         return t.to(dt)
 
                     w = rnd(cols) * 0.02 + 1
+                    extra = {}
                     if op == "rms_norm_residual":
-                        x, br, y, h = rnd(rows, cols), rnd(rows, cols), torch.empty(rows, cols, dtype=dt, device=device), \
-                            torch.empty(rows, cols, dtype=dt, device=device)
+                        x, br, y, h = rnd(lrows, cols), rnd(lrows, cols), torch.empty(lrows, cols, dtype=dt, device=device), \
+                            torch.empty(lrows, cols, dtype=dt, device=device)
                         fn = lambda: xn.rms_norm_(y, x, w, 1e-5, branch=br, residual_out=h)  # noqa: E731
                         nbytes = 4 * rows * cols * s + cols * s
                     elif op == "layer_norm":
-                        x, y, b = rnd(rows, cols), torch.empty(rows, cols, dtype=dt, device=device), rnd(cols)
+                        x, y, b = rnd(lrows, cols), torch.empty(lrows, cols, dtype=dt, device=device), rnd(cols)
                         fn = lambda: xn.layer_norm_(y, x, w, b, 1e-5)  # noqa: E731
                         nbytes = 2 * rows * cols * s + 2 * cols * s
                     elif op == "rope":
-                        if cols % 128:
-                            point["skipped"] = "rope needs width = heads x 128"
-                            out.append(point)
-                            continue
                         heads, d = cols // 128, 128
-                        x, y = rnd(1, rows, heads, d), torch.empty(1, rows, heads, d, dtype=dt, device=device)
-                        cos, sin = rnd(rows, d // 2), rnd(rows, d // 2)
+                        x, y = rnd(1, lrows, heads, d), torch.empty(1, lrows, heads, d, dtype=dt, device=device)
+                        cos, sin = rnd(lrows, d // 2), rnd(lrows, d // 2)
                         fn = lambda: xn.rope_(y, x, cos, sin, 0, layout="bthd")  # noqa: E731
                         nbytes = 2 * rows * cols * s + 2 * rows * (d // 2) * s
                     elif op == "swiglu":
-                        a, b2, y = rnd(rows, cols), rnd(rows, cols), torch.empty(rows, cols, dtype=dt, device=device)
+                        a, b2, y = rnd(lrows, cols), rnd(lrows, cols), torch.empty(lrows, cols, dtype=dt, device=device)
                         fn = lambda: xn.swiglu_(y, a, b2)  # noqa: E731
                         nbytes = 3 * rows * cols * s
                     elif op == "softmax":
-                        x, y = rnd(rows, cols), torch.empty(rows, cols, dtype=dt, device=device)
+                        x, y = rnd(lrows, cols), torch.empty(lrows, cols, dtype=dt, device=device)
                         fn = lambda: xn.softmax_(y, x)  # noqa: E731
                         nbytes = 2 * rows * cols * s
                     elif op in ("silu", "gelu_erf"):
-                        x, y = rnd(rows, cols), torch.empty(rows, cols, dtype=dt, device=device)
+                        x, y = rnd(lrows, cols), torch.empty(lrows, cols, dtype=dt, device=device)
                         fn = lambda: xn.unary_(y, x, op)  # noqa: E731
                         nbytes = 2 * rows * cols * s
                     elif op == "residual_add":
-                        x, br, y = rnd(rows, cols), rnd(rows, cols), torch.empty(rows, cols, dtype=dt, device=device)
+                        x, br, y = rnd(lrows, cols), rnd(lrows, cols), torch.empty(lrows, cols, dtype=dt, device=device)
                         ls = (rnd(cols).abs() * 0.05).to(dt)
                         fn = lambda: xn.residual_add_(y, x, br, ls)  # noqa: E731
                         nbytes = 3 * rows * cols * s + cols * s
                     elif op in ("softmax_causal", "causal_mask"):
-                        # Prefill-shaped attention scores: slices of t1 = 1024 queries over
-                        # `cols` keys, the last query seeing every key (offset = cols - t1).
-                        t1 = min(1024, rows)
-                        if rows % t1:
-                            point["skipped"] = "rows must be a multiple of the 1024-query slice"
-                            out.append(point)
-                            continue
                         offset = max(cols - t1, 0)
                         live = sum(min(offset + i + 1, cols) for i in range(t1)) * (rows // t1)
-                        x = rnd(rows // t1, t1, cols)
+                        x = rnd(lrows // t1, t1, cols)
                         if op == "softmax_causal":
                             y = torch.empty_like(x)
                             fn = lambda: xn.softmax_causal_(y, x, offset)  # noqa: E731
@@ -574,23 +814,27 @@ def sweep(torch, xn, device, widths, rows_list, dtypes, reps: int, mem_cap_gb: f
                             nbytes = (rows * cols - live) * s  # the masked elements, written
                     elif op == "rvq_decode":
                         books = [rnd(RVQ_BINS, cols) for _ in range(RVQ_BOOKS)]
-                        codes = torch.randint(0, RVQ_BINS, (1, RVQ_BOOKS, rows), dtype=torch.int64, device=device,
+                        codes = torch.randint(0, RVQ_BINS, (1, RVQ_BOOKS, lrows), dtype=torch.int64, device=device,
                                               generator=g)
-                        y = torch.empty(1, rows, cols, dtype=dt, device=device)
+                        y = torch.empty(1, lrows, cols, dtype=dt, device=device)
                         fn = lambda: xn.rvq_decode_sum(books, codes, out_layout="btd", out=y)  # noqa: E731
-                        # per frame: Q codes, Q codebook rows (from L2 while the books fit), one output row
-                        nbytes = rows * (RVQ_BOOKS * 8 + RVQ_BOOKS * cols * s + cols * s)
+                        # Compulsory bytes: the codes, each codebook once (per GPU) and the output.
+                        # The rows gathered (8 per frame) mostly come from L2 while the codebooks fit
+                        # there; their count is reported beside it.
+                        nbytes = rows * (RVQ_BOOKS * 8 + cols * s) + world * RVQ_BOOKS * RVQ_BINS * cols * s
+                        extra["gathered_bytes"] = rows * (RVQ_BOOKS * 8 + RVQ_BOOKS * cols * s + cols * s)
                     else:
                         table = rnd(32768, cols)
-                        ids = torch.randint(0, 32768, (rows,), dtype=torch.int32, device=device, generator=g)
-                        y = torch.empty(rows, cols, dtype=dt, device=device)
+                        ids = torch.randint(0, 32768, (lrows,), dtype=torch.int32, device=device, generator=g)
+                        y = torch.empty(lrows, cols, dtype=dt, device=device)
                         fn = lambda: xn.index_select(table, ids, 0, out=y)  # noqa: E731
                         nbytes = rows * 4 + 2 * rows * cols * s
                     fn()
                     times = []
                     for _ in range(reps):
-                        flush.zero_()
-                        flush_clean.sum()
+                        flush()
+                        if world > 1:
+                            dist.barrier()
                         # Keep the GPU busy (a fixed ~0.5 ms spin) while the host enqueues the
                         # start event, the op and the stop event, so host launch latency never
                         # shows up between the two events of a short launch.
@@ -601,8 +845,14 @@ def sweep(torch, xn, device, widths, rows_list, dtypes, reps: int, mem_cap_gb: f
                         e1.record()
                         torch.cuda.synchronize()
                         times.append(e0.elapsed_time(e1))
+                    if world > 1:
+                        tt = torch.tensor(times, dtype=torch.float64, device=device)
+                        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+                        times = tt.tolist()
                     ms = statistics.median(times)
                     point.update(ms=round(ms, 5), gbs=round(nbytes / (ms * 1e-3) / 1e9, 1))
+                    for k, v in extra.items():
+                        point[k.replace("_bytes", "_gbs")] = round(v / (ms * 1e-3) / 1e9, 1)
                     out.append(point)
                     del fn
                     torch.cuda.empty_cache()
@@ -774,6 +1024,10 @@ def main() -> int:
                     help="token rows per GPU (a multiple of 4096; smaller values for profiling captures)")
     ap.add_argument("--ops", default=",".join(OPS), help="comma-separated subset of " + ",".join(OPS))
     ap.add_argument("--mimi-steps", type=int, default=20, help="Mimi decode replays to time (0 skips it)")
+    ap.add_argument("--mimi-stream-steps", type=int, default=300,
+                    help="frames of the Mimi streaming decode to time (0 skips it)")
+    ap.add_argument("--config1-reps", type=int, default=20,
+                    help="flushed launches per op of the config-1 f32 micro-pipeline (0 skips it)")
     ap.add_argument("--sweep", action="store_true", help="run the per-op bandwidth sweep instead (JSON per point)")
     ap.add_argument("--sweep-widths", default="256,1024,4096,16384")
     ap.add_argument("--sweep-rows", default="1024,16384,262144,1048576")
@@ -803,14 +1057,23 @@ def main() -> int:
         if unknown:
             ap.error(f"--sweep-ops: unknown op(s) {unknown}")
         xn.lib()
+        if world > 1:
+            from datetime import timedelta
+
+            dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
         peak, _ = measured_peak()
         pts = sweep(torch, xn, dev, [int(v) for v in args.sweep_widths.split(",")],
                     [int(v) for v in args.sweep_rows.split(",")], args.sweep_dtypes.split(","), max(3, args.steps),
-                    args.sweep_mem_gb, sweep_ops)
+                    args.sweep_mem_gb, sweep_ops, world=world, rank=rank)
         for pt in pts:
             if "gbs" in pt:
-                pt["frac"] = round(pt["gbs"] / peak, 3)
-            print(json.dumps(pt), flush=True)
+                pt["frac"] = round(pt["gbs"] / peak, 3)  # of one GPU's peak
+                pt["frac_per_gpu"] = round(pt["gbs"] / world / peak, 3)
+            if rank == 0:
+                print(json.dumps(pt), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
         return 0
     if args.gather_context:
         xn.lib()
@@ -916,22 +1179,64 @@ def main() -> int:
         torch.cuda.synchronize()
         gather_ms = g0.elapsed_time(g1) / 5
 
+    # The same NCCL all-gather on preallocated buffers with nothing else
+    # running: the library's own bound for the optional gather.
+    raw_gather_ms = float("nan")
+    if distributed and hasattr(wl, "y2"):
+        src = wl.y2.contiguous()
+        full = torch.empty((src.shape[0] * world, *src.shape[1:]), dtype=src.dtype, device=dev)
+        for _ in range(3):
+            dist.all_gather_into_tensor(full, src)
+        torch.cuda.synchronize()
+        dist.barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for _ in range(5):
+            dist.all_gather_into_tensor(full, src)
+        g1.record(stream)
+        torch.cuda.synchronize()
+        raw_gather_ms = g0.elapsed_time(g1) / 5
+        del full
+
     mimi = None
     if args.mimi_steps > 0:
         mimi = mimi_rate(torch, dev, args.mimi_steps)
+    mimi_stream = None
+    if args.mimi_stream_steps > 0:
+        mimi_stream = mimi_stream_rate(torch, dev, args.mimi_stream_steps)
     decode = None
     if args.decode_steps > 0:
         decode = {act: decode_rate(torch, dev, args.decode_steps, act) for act in ("silu", "gelu_erf")}
+    config1 = None
+    if args.config1_reps > 0:
+        config1 = config1_rate(torch, xn, dev, args.config1_reps)
 
     if distributed:
         vals = [elapsed_ms, e2e_ms, mimi["ms_per_decode"] if mimi else 0.0, gather_ms if gather_ms == gather_ms else 0.0,
+                raw_gather_ms if raw_gather_ms == raw_gather_ms else 0.0,
+                mimi_stream["us_per_step"] if mimi_stream else 0.0, mimi_stream["e2e_us_per_step"] if mimi_stream else 0.0,
+                config1["pipeline_us"] if config1 else 0.0,
                 mimi["e2e_frames_per_s"] if mimi else 0.0]
         t = torch.tensor(vals, dtype=torch.float64, device=dev)
-        dist.all_reduce(t[:4], op=dist.ReduceOp.MAX)
-        dist.all_reduce(t[4:], op=dist.ReduceOp.MIN)
+        dist.all_reduce(t[:8], op=dist.ReduceOp.MAX)
+        dist.all_reduce(t[8:], op=dist.ReduceOp.MIN)
         elapsed_ms, e2e_ms = float(t[0]), float(t[1])
         if gather_ms == gather_ms:
             gather_ms = float(t[3])
+        if raw_gather_ms == raw_gather_ms:
+            raw_gather_ms = float(t[4])
+        if mimi_stream:
+            # Whole job: every rank streams its own batch; the slowest rank sets the step time.
+            b = mimi_stream["batch"]
+            mimi_stream["us_per_step"], mimi_stream["e2e_us_per_step"] = round(float(t[5]), 2), round(float(t[6]), 2)
+            mimi_stream["frames_per_s"] = round(world * b / (float(t[5]) * 1e-6), 1)
+            mimi_stream["e2e_frames_per_s"] = round(world * b / (float(t[6]) * 1e-6), 1)
+            mimi_stream["ranks"] = world
+        if config1:
+            config1["pipeline_us"] = round(float(t[7]), 2)
+            config1["pipeline_gbs"] = round(world * config1["pipeline_bytes"] / (float(t[7]) * 1e-6) / 1e9, 1)
+            config1["ranks"] = world
+            config1["per_op_note"] = "per_op: rank 0's launches; pipeline: max over ranks, bytes of all ranks"
         if mimi:
             # Whole-job rate: every rank decodes its own batch; the slowest rank sets the time.
             n = mimi["batch"] * mimi["frames"]
@@ -946,7 +1251,8 @@ def main() -> int:
         peak, peak_src = measured_peak()
         dom = max(per_op_ms, key=per_op_ms.get)
         achieved = wl.bytes[dom] / (per_op_ms[dom] * 1e-3) / 1e9
-        traffic = load_traffic().get(dom)
+        traffic_all = load_traffic()
+        traffic = traffic_all.get(dom)
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
@@ -957,10 +1263,18 @@ def main() -> int:
             "roofline": {"bound": "hbm", "kernel": dom, "kernel_fn": KERNELS[dom], "achieved": round(achieved, 1),
                          "peak": peak,
                          "peak_source": peak_src, "unit": "GB/s", "frac": round(achieved / peak, 3),
-                         "traffic": traffic, "algorithmic_bytes": wl.bytes[dom]},
+                         "traffic": traffic, "algorithmic_bytes": wl.bytes[dom],
+                         "dram_gbs": None if traffic is None else round(traffic / (per_op_ms[dom] * 1e-3) / 1e9, 1),
+                         "dram_frac": None if traffic is None else round(traffic / (per_op_ms[dom] * 1e-3) / 1e9 / peak, 3)},
             "per_op": {n: {"ms": round(per_op_ms[n], 4), "bytes": wl.bytes[n],
                            "gbs": round(wl.bytes[n] / (per_op_ms[n] * 1e-3) / 1e9, 1),
-                           "frac": round(wl.bytes[n] / (per_op_ms[n] * 1e-3) / 1e9 / peak, 3)} for n in ops},
+                           "frac": round(wl.bytes[n] / (per_op_ms[n] * 1e-3) / 1e9 / peak, 3),
+                           # DRAM bytes actually moved (ncu, profiles/traffic.json), per launch
+                           "dram_bytes": traffic_all.get(n),
+                           "dram_frac": None if traffic_all.get(n) is None else
+                           round(traffic_all[n] / (per_op_ms[n] * 1e-3) / 1e9 / peak, 3)} for n in ops},
+            "step_dram_frac": None if not all(n in traffic_all for n in ops) else
+            round(sum(traffic_all[n] for n in ops) / (ms_per_step * 1e-3) / 1e9 / peak, 3),
             "e2e": None if args.e2e_steps <= 0 else {
                 "value": round(world * step_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": UNIT,
                 "h2d_bytes_per_step": wl.h2d_bytes, "d2h_bytes_per_step": wl.d2h_bytes,
@@ -976,9 +1290,14 @@ def main() -> int:
                         "NVLink; not on the data path",
                 "bytes_out": wl.rows * world * cfg["hidden"] * 2, "ms": round(gather_ms, 4),
                 "algbw_gbs": round(wl.rows * world * cfg["hidden"] * 2 / (gather_ms * 1e-3) / 1e9, 1),
-                "busbw_gbs": round(wl.rows * (world - 1) * cfg["hidden"] * 2 / (gather_ms * 1e-3) / 1e9, 1)},
+                "busbw_gbs": round(wl.rows * (world - 1) * cfg["hidden"] * 2 / (gather_ms * 1e-3) / 1e9, 1),
+                "raw_nccl_ms": None if raw_gather_ms != raw_gather_ms else round(raw_gather_ms, 4),
+                "raw_nccl_busbw_gbs": None if raw_gather_ms != raw_gather_ms else
+                round(wl.rows * (world - 1) * cfg["hidden"] * 2 / (raw_gather_ms * 1e-3) / 1e9, 1)},
             "mimi_decode": mimi,
+            "mimi_stream_decode": mimi_stream,
             "streaming_decode": decode,
+            "config1": config1,
             "clocks": clocks,
         }
         if not args.no_cpu_baseline and world == 1:
@@ -988,6 +1307,10 @@ def main() -> int:
                 line["cpu_baseline"]["mimi_decode"] = cpu_mimi_rate()
             if decode is not None:
                 line["cpu_baseline"]["streaming_decode"] = {act: cpu_decode_rate(act) for act in decode}
+            if mimi_stream is not None:
+                line["cpu_baseline"]["mimi_stream_decode"] = cpu_mimi_stream_rate()
+            if config1 is not None:
+                line["cpu_baseline"]["config1"] = cpu_config1_rate()
         print(json.dumps(line), flush=True)
     if distributed:
         dist.barrier()

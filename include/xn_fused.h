@@ -60,6 +60,12 @@ enum {
   XN_E_CUDA = 4       /* the CUDA runtime reported an error while launching */
 };
 
+/* Bits a kernel sets in a caller's device error word (err_flag). */
+enum {
+  XN_DEVERR_RANGE = 1,  /* an id, code or device position outside its table: that part was skipped */
+  XN_DEVERR_WAIT = 2    /* a bounded wait gave up (the rows that block had not finished are NaN) */
+};
+
 /* Unary ops handled by xn_unary; names follow `enum UnaryOp`
  * (mimi-rs/src/inplace_ops.rs:5-38). */
 enum {
@@ -217,6 +223,21 @@ XN_API int xn_softmax(void *dst, const void *src, int64_t rows, int64_t cols,
  */
 XN_API int xn_softmax_scaled(void *dst, const void *src, int64_t rows, int64_t cols, float scale,
                              int causal, int64_t t1, int64_t offset, int dtype, void *stream);
+
+/*
+ * xn_softmax (scaled == 0) or xn_softmax_scaled (scaled != 0) with a device
+ * status word: err_flag (a device int, may be NULL) gets XN_DEVERR_WAIT when a
+ * shared-memory stage of the wide-row kernel did not arrive within its bounded
+ * wait; that kernel then waits (bounded) for its copies in flight, writes NaN
+ * to the rows it had not finished and returns, so a lost copy shows as a
+ * status instead of a hang. It cannot happen with valid arguments. The
+ * environment variable XN_STAGE_WAIT_POLLS (read once per process) lowers the
+ * number of polls before the wait gives up, for testing that path. No
+ * reference counterpart: the reference's softmax has no waits
+ * (mimi-rs/cuda-kernels/reduce.cu:178-220).
+ */
+XN_API int xn_softmax_status(void *dst, const void *src, int64_t rows, int64_t cols, int scaled, float scale,
+                             int causal, int64_t t1, int64_t offset, int *err_flag, int dtype, void *stream);
 
 /*
  * In-place causal mask on [bh, t1, t2]: x[b, i, j] = -inf where j > offset + i.

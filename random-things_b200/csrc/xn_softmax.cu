@@ -16,6 +16,7 @@
 // Rows wider than that, or wider than 16384 elements in the scalar path, use
 // a three-pass kernel.
 #include <math.h>
+#include <cstdlib>
 
 #include <cooperative_groups.h>
 
@@ -39,6 +40,8 @@ struct SoftmaxParams {
   int nvec;
   int scaled;      // apply x = T(x * scale) first (the attention score scale)
   float scale;
+  int *err_flag;        // optional device word: XN_DEVERR_WAIT when a bounded wait gave up
+  uint32_t wait_polls;  // polls before a stage wait gives up (softmax_staged_kernel)
 };
 
 __device__ __forceinline__ int64_t row_limit(const SoftmaxParams &p, int64_t row) {
@@ -482,11 +485,13 @@ __global__ void __launch_bounds__(512, NV * sizeof(U) >= 80 ? 1 : 2) softmax_pip
 // first `lim` columns (rounded up to the 16-byte vector). Arithmetic as
 // softmax_pipe_kernel; the block reductions go through shared memory.
 //
-// A bulk copy that does not complete within kStageWaitLimit polls (it cannot
+// A bulk copy that does not complete within p.wait_polls polls (it cannot
 // happen with valid arguments; the limit guards against a hang) makes the
-// whole block stop: it waits, again bounded, for its copies still in flight
-// and writes NaN to every row it has not finished, so the failure shows in
-// the output instead of as a hang.
+// whole block stop: it waits, bounded by kStageWaitLimit, for its copies still
+// in flight (so none lands in shared memory after the block exits), writes NaN
+// to every row it has not finished and sets XN_DEVERR_WAIT in the caller's
+// error word, so the failure shows in the output and the status instead of as
+// a hang.
 constexpr int kMaxStages = 4;
 constexpr uint32_t kStageWaitLimit = 1u << 22;
 
@@ -548,7 +553,7 @@ __global__ void __launch_bounds__(NV >= 8 ? 512 : 1024) softmax_staged_kernel(co
   uint32_t parity = 0;
   for (int64_t row = blockIdx.x; row < p.rows; row += step) {
     const int lim = lim_of(q);
-    const bool arrived = mbar_wait(&full[s], parity, kStageWaitLimit);
+    const bool arrived = mbar_wait(&full[s], parity, p.wait_polls);
     const uint4 *buf = reinterpret_cast<const uint4 *>(stage_buf + static_cast<size_t>(s) * stage_bytes);
     uint4 cur[NV];
 #pragma unroll
@@ -581,6 +586,7 @@ __global__ void __launch_bounds__(NV >= 8 ? 512 : 1024) softmax_staged_kernel(co
                                                                                             0x7fc07fc0u, 0x7fc07fc0u));
       for (int64_t r = row; r < p.rows; r += step)
         for (int vi = tid; vi < p.nvec; vi += tpr) st_vec(dst + r * p.cols + vi * N, nan4);
+      if (tid == 0 && p.err_flag != nullptr) atomicOr(p.err_flag, XN_DEVERR_WAIT);
       return;
     }
     // Every thread has read buffer s: refill it with the row `stages` ahead.
@@ -984,8 +990,21 @@ __global__ void __launch_bounds__(256) causal_mask_kernel(void *dst, int64_t bh,
 
 namespace xn {
 namespace {
+// Polls of a stage wait before it gives up: kStageWaitLimit, or the value of
+// the environment variable XN_STAGE_WAIT_POLLS (read once per process), a
+// diagnostic that lets a test make the wait give up on valid inputs.
+uint32_t stage_wait_polls() {
+  static const uint32_t polls = [] {
+    const char *v = std::getenv("XN_STAGE_WAIT_POLLS");
+    if (v == nullptr || *v == '\0') return kStageWaitLimit;
+    const unsigned long n = std::strtoul(v, nullptr, 10);
+    return n < kStageWaitLimit ? static_cast<uint32_t>(n) : kStageWaitLimit;
+  }();
+  return polls;
+}
+
 int softmax_entry(void *dst, const void *src, int64_t rows, int64_t cols, int scaled, float scale, int causal,
-                  int64_t t1, int64_t offset, int dtype, void *stream) {
+                  int64_t t1, int64_t offset, int dtype, void *stream, int *err_flag = nullptr) {
   if (!is_float_dtype(dtype)) return fail(XN_E_DTYPE, "xn_softmax: unsupported dtype %d", dtype);
   if (rows < 0 || cols < 0) return fail(XN_E_INVALID, "xn_softmax: negative size");
   if (causal && (t1 <= 0 || offset < 0 || rows % t1 != 0))
@@ -995,7 +1014,8 @@ int softmax_entry(void *dst, const void *src, int64_t rows, int64_t cols, int sc
     return fail(XN_E_INVALID, "xn_softmax: t1 = %lld query rows per slice exceeds 2^30", (long long)t1);
   if (rows == 0 || cols == 0) return ok();
   if (dst == nullptr || src == nullptr) return fail(XN_E_INVALID, "xn_softmax: null dst or src");
-  SoftmaxParams p{dst, src, rows, cols, causal ? t1 : 1, causal ? offset : 0, causal ? 1 : 0, 0, 0, scaled, scale};
+  SoftmaxParams p{dst,   src,   rows,   cols, causal ? t1 : 1, causal ? offset : 0, causal ? 1 : 0, 0, 0,
+                  scaled, scale, err_flag, stage_wait_polls()};
   XN_DISPATCH_FLOAT(dtype, return launch_softmax<T>(p, as_stream(stream)));
   return fail(XN_E_DTYPE, "xn_softmax: unsupported dtype %d", dtype);
 }
@@ -1013,6 +1033,11 @@ int xn_softmax(void *dst, const void *src, int64_t rows, int64_t cols, int causa
 int xn_softmax_scaled(void *dst, const void *src, int64_t rows, int64_t cols, float scale, int causal, int64_t t1,
                       int64_t offset, int dtype, void *stream) {
   return xn::softmax_entry(dst, src, rows, cols, 1, scale, causal, t1, offset, dtype, stream);
+}
+
+int xn_softmax_status(void *dst, const void *src, int64_t rows, int64_t cols, int scaled, float scale, int causal,
+                      int64_t t1, int64_t offset, int *err_flag, int dtype, void *stream) {
+  return xn::softmax_entry(dst, src, rows, cols, scaled ? 1 : 0, scale, causal, t1, offset, dtype, stream, err_flag);
 }
 
 int xn_causality_mask(void *dst, int64_t bh, int64_t t1, int64_t t2, int64_t offset, int dtype,

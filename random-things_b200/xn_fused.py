@@ -27,6 +27,7 @@ XN_UNARY_SILU, XN_UNARY_GELU_ERF = 0, 1
 XN_LAYOUT_BHTD, XN_LAYOUT_BTHD = 0, 1
 XN_RVQ_MAX_CODEBOOKS = 32
 XN_MASK_RELATIVE, XN_MASK_ABSOLUTE, XN_MASK_CACHE_LEN = 0, 1, 2
+XN_DEVERR_RANGE, XN_DEVERR_WAIT = 1, 2
 MASK_MODES = {"relative": XN_MASK_RELATIVE, "absolute": XN_MASK_ABSOLUTE, "cache_len": XN_MASK_CACHE_LEN}
 
 # Same codes as `enum DType` (mimi-rs/src/dtype.rs:4-10).
@@ -67,6 +68,7 @@ SIGNATURES = {
     "xn_softmax_scaled": [_vp, _vp, _i64, _i64, _f32, _int, _i64, _i64, _int, _vp],
     "xn_swiglu": [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp],
     "xn_softmax": [_vp, _vp, _i64, _i64, _int, _i64, _i64, _int, _vp],
+    "xn_softmax_status": [_vp, _vp, _i64, _i64, _int, _f32, _int, _i64, _i64, _vp, _int, _vp],
     "xn_causality_mask": [_vp, _i64, _i64, _i64, _i64, _int, _vp],
     "xn_index_select": [_vp, _vp, _vp, _int, _i64, _i64, _i64, _i64, _int, _vp, _vp],
     "xn_rvq_decode_sum": [_vp, ctypes.POINTER(_vp), _i64, _vp, _i64, _i64, _i64, _i64, _int, _int, _vp,
@@ -497,6 +499,27 @@ def attn_softmax(scores: torch.Tensor, scale: float, offset: int | None = None) 
     out = torch.empty_like(scores)
     attn_softmax_(out, scores, scale, offset)
     return out
+
+
+def softmax_status_(dst: torch.Tensor, src: torch.Tensor, err_flag: torch.Tensor, *, scale: float | None = None,
+                    offset: int | None = None) -> None:
+    """softmax_ / attn_softmax_ (scale and causal offset optional) that also
+    reports, in the int32 device word err_flag, XN_DEVERR_WAIT when a bounded
+    wait of the wide-row kernel gave up (its unfinished rows are then NaN)."""
+    _check_same_shape(dst.shape, src.shape, "softmax_status_")
+    _dev(dst, src, err_flag)
+    _same_dtype(dst, src)
+    if err_flag.dtype != torch.int32:
+        raise XnError("softmax_status_: err_flag must be an int32 CUDA tensor")
+    if offset is None:
+        rows, cols = _rows_cols(dst)
+        causal, t1, off = 0, 1, 0
+    else:
+        bh, t1, cols = _mask_dims(src, "softmax_status_")
+        rows, causal, off = bh * t1, 1, int(offset)
+    _call("xn_softmax_status", _p(dst), _p(src), rows, cols, 0 if scale is None else 1,
+          1.0 if scale is None else float(scale), causal, max(t1, 1), off, _p(err_flag), _dtype_code(dst),
+          _stream(dst))
 
 
 def apply_causality_mask_(x: torch.Tensor, offset: int) -> None:
