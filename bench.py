@@ -1242,7 +1242,7 @@ def main() -> int:
             n = mimi["batch"] * mimi["frames"]
             mimi["ms_per_decode"] = round(float(t[2]), 4)
             mimi["frames_per_s"] = round(world * n / (float(t[2]) * 1e-3), 1)
-            mimi["e2e_frames_per_s"] = round(world * float(t[4]), 1)
+            mimi["e2e_frames_per_s"] = round(world * float(t[8]), 1)
 
     if rank == 0:
         step_bytes = sum(wl.bytes.values())
