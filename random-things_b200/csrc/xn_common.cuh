@@ -92,6 +92,49 @@ __device__ __forceinline__ uint4 ld_plain(const void *p) {
 
 __device__ __forceinline__ void st_vec(void *p, uint4 v) { *reinterpret_cast<uint4 *>(p) = v; }
 
+// Row accesses of AW 32-bit words (AW = 4: 16 bytes, 2: 8 bytes, 1: 4 bytes)
+// held in the low words of a uint4; the other words are 0. Rows whose byte
+// width is a multiple of 8 or 4 but not of 16 (16-bit rows of even width,
+// f32 rows of even width) keep one access per 8 / 4 bytes instead of falling
+// back to element accesses.
+template <int AW>
+__device__ __forceinline__ uint4 ld_stream_w(const void *p) {
+  if constexpr (AW == 4) {
+    return ld_stream(p);
+  } else if constexpr (AW == 2) {
+    uint4 r = make_uint4(0u, 0u, 0u, 0u);
+    asm volatile("ld.global.L1::no_allocate.v2.u32 {%0, %1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+    return r;
+  } else {
+    uint4 r = make_uint4(0u, 0u, 0u, 0u);
+    asm volatile("ld.global.L1::no_allocate.u32 %0, [%1];" : "=r"(r.x) : "l"(p));
+    return r;
+  }
+}
+
+template <int AW>
+__device__ __forceinline__ uint4 ld_cached_w(const void *p) {
+  if constexpr (AW == 4) {
+    return __ldg(reinterpret_cast<const uint4 *>(p));
+  } else if constexpr (AW == 2) {
+    const uint2 v = __ldg(reinterpret_cast<const uint2 *>(p));
+    return make_uint4(v.x, v.y, 0u, 0u);
+  } else {
+    return make_uint4(__ldg(reinterpret_cast<const unsigned int *>(p)), 0u, 0u, 0u);
+  }
+}
+
+template <int AW>
+__device__ __forceinline__ void st_w(void *p, uint4 v) {
+  if constexpr (AW == 4) {
+    *reinterpret_cast<uint4 *>(p) = v;
+  } else if constexpr (AW == 2) {
+    *reinterpret_cast<uint2 *>(p) = make_uint2(v.x, v.y);
+  } else {
+    *reinterpret_cast<unsigned int *>(p) = v.x;
+  }
+}
+
 // Returns v unchanged through moves the compiler cannot see through. Used to
 // make a second pass over packed register data unpack it again instead of
 // keeping the first pass's unpacked f32 copies live (which doubles register
@@ -267,27 +310,39 @@ __device__ __forceinline__ uint32_t t2_mul<__half>(uint32_t a, uint32_t b) {
   return *reinterpret_cast<uint32_t *>(&r);
 }
 
-template <typename T>
+// AW: the access width in 32-bit words (see ld_stream_w); only those words
+// are computed.
+template <typename T, int AW = 4>
 __device__ __forceinline__ uint4 residual_vec(uint4 x, uint4 b, const void *s) {
   if constexpr (std::is_same<T, float>::value) {
+    static_assert(AW >= 2, "f32 accesses hold whole element pairs");
+    constexpr int KP = AW / 2;
     float2 bp[2], xp[2];
     Pairs<float>::unpack(b, bp);
     Pairs<float>::unpack(x, xp);
     if (s != nullptr) {
       float2 sp[2];
-      Pairs<float>::unpack(ld_cached(s), sp);
-      bp[0] = __fmul2_rn(bp[0], sp[0]);
-      bp[1] = __fmul2_rn(bp[1], sp[1]);
+      Pairs<float>::unpack(ld_cached_w<AW>(s), sp);
+#pragma unroll
+      for (int j = 0; j < KP; ++j) bp[j] = __fmul2_rn(bp[j], sp[j]);
     }
-    xp[0] = __fadd2_rn(xp[0], bp[0]);
-    xp[1] = __fadd2_rn(xp[1], bp[1]);
+#pragma unroll
+    for (int j = 0; j < KP; ++j) xp[j] = __fadd2_rn(xp[j], bp[j]);
+    if constexpr (KP == 1) xp[1] = make_float2(0.f, 0.f);
     return Pairs<float>::pack(xp);
   } else {
+    uint32_t xw[4] = {x.x, x.y, x.z, x.w}, bw[4] = {b.x, b.y, b.z, b.w};
     if (s != nullptr) {
-      const uint4 sv = ld_cached(s);
-      b = make_uint4(t2_mul<T>(b.x, sv.x), t2_mul<T>(b.y, sv.y), t2_mul<T>(b.z, sv.z), t2_mul<T>(b.w, sv.w));
+      const uint4 sv = ld_cached_w<AW>(s);
+      const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+      for (int j = 0; j < AW; ++j) bw[j] = t2_mul<T>(bw[j], sw[j]);
     }
-    return make_uint4(t2_add<T>(x.x, b.x), t2_add<T>(x.y, b.y), t2_add<T>(x.z, b.z), t2_add<T>(x.w, b.w));
+#pragma unroll
+    for (int j = 0; j < AW; ++j) xw[j] = t2_add<T>(xw[j], bw[j]);
+#pragma unroll
+    for (int j = AW; j < 4; ++j) xw[j] = 0u;
+    return make_uint4(xw[0], xw[1], xw[2], xw[3]);
   }
 }
 

@@ -145,14 +145,15 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : 1) norm_rows
 // with 4-thread groups (rows of 32 vectors) the shorter instruction stream
 // reaches the per-vector weight loads sooner and waits on them, which measured
 // slower.
-template <typename T, int NV, bool kLN, int kMaxBlock, bool kBranch, bool kMix = false>
+template <typename T, int NV, bool kLN, int kMaxBlock, bool kBranch, bool kMix = false, int AW = 4>
 __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : (kMaxBlock == 512 ? 2 : 1))
     norm_vec_kernel(const NormParams p) {
   griddep_wait();
   griddep_release();
   using P = Pairs<T>;
-  constexpr int KP = P::kP;
-  constexpr int N = Elem<T>::kVec;
+  constexpr int KPF = P::kP;                                // element pairs in a 16-byte vector
+  constexpr int KP = std::is_same_v<T, float> ? AW / 2 : AW;  // ... in one access of AW words
+  constexpr int N = Elem<T>::kVec * AW / 4;                 // elements per access
   // One scratch array per reduction (see group_sum's kReuse); one row per group.
   __shared__ float red_a[32], red_b[32];
   const int tpr = p.tpr;
@@ -162,7 +163,7 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : (kMaxBlock =
   const int64_t row = static_cast<int64_t>(blockIdx.x) * rpb + g;
   const bool active = row < p.rows;
   const int64_t base = row * p.cols;
-  const uint4 *src = reinterpret_cast<const uint4 *>(static_cast<const T *>(p.src) + base);
+  const T *src = static_cast<const T *>(p.src) + base;
 
   // 1) h = src (+ T(branch * ls)), packed; invalid slots hold +0.
   uint4 h[NV];
@@ -170,7 +171,7 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : (kMaxBlock =
   for (int k = 0; k < NV; ++k) {
     const int vi = lr + k * tpr;
     h[k] = make_uint4(0u, 0u, 0u, 0u);
-    if (active && vi < p.nvec) h[k] = ld_stream(src + vi);
+    if (active && vi < p.nvec) h[k] = ld_stream_w<AW>(src + vi * N);
   }
   // Short rows per thread (NV <= 2, the shapes chosen for few or narrow rows):
   // fetch the weight / bias vectors together with the row, so their latency
@@ -184,38 +185,38 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : (kMaxBlock =
     for (int k = 0; k < NV; ++k) {
       const int vi = lr + k * tpr;
       if (active && vi < p.nvec) {
-        if (wp != nullptr) wpre[k] = ld_cached(wp + vi * N);
-        if (kLN && bp != nullptr) bpre[k] = ld_cached(bp + vi * N);
+        if (wp != nullptr) wpre[k] = ld_cached_w<AW>(wp + vi * N);
+        if (kLN && bp != nullptr) bpre[k] = ld_cached_w<AW>(bp + vi * N);
       }
     }
   }
   if constexpr (kBranch) {
-    const uint4 *br = reinterpret_cast<const uint4 *>(static_cast<const T *>(p.branch) + base);
+    const T *br = static_cast<const T *>(p.branch) + base;
     uint4 b[NV];
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
       const int vi = lr + k * tpr;
-      if (active && vi < p.nvec) b[k] = ld_stream(br + vi);
+      if (active && vi < p.nvec) b[k] = ld_stream_w<AW>(br + vi * N);
     }
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
       const int vi = lr + k * tpr;
       if (active && vi < p.nvec)
-        h[k] = residual_vec<T>(h[k], b[k], p.ls != nullptr ? static_cast<const T *>(p.ls) + vi * N : nullptr);
+        h[k] = residual_vec<T, AW>(h[k], b[k], p.ls != nullptr ? static_cast<const T *>(p.ls) + vi * N : nullptr);
     }
     if (p.res_out != nullptr) {
-      uint4 *ro = reinterpret_cast<uint4 *>(static_cast<T *>(p.res_out) + base);
+      T *ro = static_cast<T *>(p.res_out) + base;
 #pragma unroll
       for (int k = 0; k < NV; ++k) {
         const int vi = lr + k * tpr;
-        if (active && vi < p.nvec) st_vec(ro + vi, h[k]);
+        if (active && vi < p.nvec) st_w<AW>(ro + vi * N, h[k]);
       }
     }
   }
 
   // 2) Row statistics in f32, then 3) the epilogue dst = T(norm(h) * w (+ b)).
   const float cols_f = __ll2float_rn(p.cols);
-  uint4 *dst = reinterpret_cast<uint4 *>(static_cast<T *>(p.dst) + base);
+  T *dst = static_cast<T *>(p.dst) + base;
   if constexpr (kLN && kMix && !std::is_same_v<T, float>) {
     // kMix: every f32 sum with a row element takes the element as it is
     // stored (sm_100's mixed-precision add, add2_widen), the same values as
@@ -248,9 +249,9 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : (kMaxBlock =
       const int vi = lr + k * tpr;
       if (active && vi < p.nvec) {
         const uint4 hk = opaque(h[k]);
-        float2 x[KP], w[KP];
+        float2 x[KPF] = {}, w[KPF];
         if (wp != nullptr) {
-          P::unpack(kPre ? wpre[k] : ld_cached(wp + vi * N), w);
+          P::unpack(kPre ? wpre[k] : ld_cached_w<AW>(wp + vi * N), w);
         } else {
 #pragma unroll
           for (int j = 0; j < KP; ++j) w[j] = splat2(1.f);
@@ -258,21 +259,21 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : (kMaxBlock =
 #pragma unroll
         for (int j = 0; j < KP; ++j) x[j] = __fmul2_rn(__fmul2_rn(add2_widen<T>(u4_word(hk, j), nshift), inv), w[j]);
         if (bp != nullptr) {
-          const uint4 bv = kPre ? bpre[k] : ld_cached(bp + vi * N);
+          const uint4 bv = kPre ? bpre[k] : ld_cached_w<AW>(bp + vi * N);
 #pragma unroll
           for (int j = 0; j < KP; ++j) x[j] = add2_widen<T>(u4_word(bv, j), x[j]);
         } else {
 #pragma unroll
           for (int j = 0; j < KP; ++j) x[j] = __fadd2_rn(x[j], splat2(0.f));
         }
-        st_vec(dst + vi, P::pack(x));
+        st_w<AW>(dst + vi * N, P::pack(x));
       }
     }
   } else if constexpr (kLN) {
     float2 s2 = make_float2(0.f, 0.f);
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
-      float2 x[KP];
+      float2 x[KPF];
       P::unpack(h[k], x);
 #pragma unroll
       for (int j = 0; j < KP; ++j) s2 = __fadd2_rn(s2, x[j]);
@@ -283,7 +284,7 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : (kMaxBlock =
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
       if (lr + k * tpr < p.nvec) {
-        float2 x[KP];
+        float2 x[KPF];
         P::unpack(opaque(h[k]), x);
 #pragma unroll
         for (int j = 0; j < KP; ++j) {
@@ -301,16 +302,16 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : (kMaxBlock =
     for (int k = 0; k < NV; ++k) {
       const int vi = lr + k * tpr;
       if (active && vi < p.nvec) {
-        float2 x[KP], w[KP], b[KP];
+        float2 x[KPF] = {}, w[KPF], b[KPF];
         P::unpack(opaque(h[k]), x);
         if (wp != nullptr) {
-          P::unpack(kPre ? wpre[k] : ld_cached(wp + vi * N), w);
+          P::unpack(kPre ? wpre[k] : ld_cached_w<AW>(wp + vi * N), w);
         } else {
 #pragma unroll
           for (int j = 0; j < KP; ++j) w[j] = splat2(1.f);
         }
         if (bp != nullptr) {
-          P::unpack(kPre ? bpre[k] : ld_cached(bp + vi * N), b);
+          P::unpack(kPre ? bpre[k] : ld_cached_w<AW>(bp + vi * N), b);
         } else {
 #pragma unroll
           for (int j = 0; j < KP; ++j) b[j] = splat2(0.f);
@@ -318,7 +319,7 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : (kMaxBlock =
 #pragma unroll
         for (int j = 0; j < KP; ++j)
           x[j] = __fadd2_rn(__fmul2_rn(__fmul2_rn(__fadd2_rn(x[j], nshift), inv), w[j]), b[j]);
-        st_vec(dst + vi, P::pack(x));
+        st_w<AW>(dst + vi * N, P::pack(x));
       }
     }
   } else if constexpr (kMix && !std::is_same_v<T, float>) {
@@ -342,10 +343,10 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : (kMaxBlock =
     for (int k = 0; k < NV; ++k) {
       const int vi = lr + k * tpr;
       if (active && vi < p.nvec) {
-        float2 x[KP], w[KP];
+        float2 x[KPF] = {}, w[KPF];
         P::unpack(opaque(h[k]), x);
         if (wp != nullptr) {
-          P::unpack(kPre ? wpre[k] : ld_cached(wp + vi * N), w);
+          P::unpack(kPre ? wpre[k] : ld_cached_w<AW>(wp + vi * N), w);
         } else {
 #pragma unroll
           for (int j = 0; j < KP; ++j) w[j] = splat2(1.f);
@@ -357,14 +358,14 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : (kMaxBlock =
           const float2 q = __ffma2_rn(make_float2(-nrem.x, -nrem.y), r2, q0);
           x[j] = __fmul2_rn(q, w[j]);
         }
-        st_vec(dst + vi, P::pack(x));
+        st_w<AW>(dst + vi * N, P::pack(x));
       }
     }
   } else {
     float2 s2 = make_float2(0.f, 0.f);
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
-      float2 x[KP];
+      float2 x[KPF];
       P::unpack(h[k], x);
 #pragma unroll
       for (int j = 0; j < KP; ++j) s2 = __ffma2_rn(x[j], x[j], s2);
@@ -377,10 +378,10 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : (kMaxBlock =
     for (int k = 0; k < NV; ++k) {
       const int vi = lr + k * tpr;
       if (active && vi < p.nvec) {
-        float2 x[KP], w[KP];
+        float2 x[KPF] = {}, w[KPF];
         P::unpack(opaque(h[k]), x);
         if (wp != nullptr) {
-          P::unpack(kPre ? wpre[k] : ld_cached(wp + vi * N), w);
+          P::unpack(kPre ? wpre[k] : ld_cached_w<AW>(wp + vi * N), w);
         } else {
 #pragma unroll
           for (int j = 0; j < KP; ++j) w[j] = splat2(1.f);
@@ -395,7 +396,7 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : (kMaxBlock =
           q.y = copysignf(q.y, q0.y);
           x[j] = __fmul2_rn(q, w[j]);
         }
-        st_vec(dst + vi, P::pack(x));
+        st_w<AW>(dst + vi * N, P::pack(x));
       }
     }
   }
@@ -463,56 +464,56 @@ constexpr int kMaxNv = (kBranch || kMaxBlock > 512) ? 4 : 8;
 
 // One launch of the row-group kernel with NV accesses per thread: the paired
 // f32 kernel for 16-byte vectors, the scalar one otherwise.
-template <typename T, bool kVector, int NV, bool kLN, int kMaxBlock, bool kBranch>
+template <typename T, bool kVector, int NV, bool kLN, int kMaxBlock, bool kBranch, int AW = 4>
 void launch_nv(const NormParams &p, int block, int64_t grid, cudaStream_t st) {
   if constexpr (kVector) {
     if constexpr ((!kLN || !kBranch) && !std::is_same_v<T, float>) {
       if (p.tpr >= 8) {
-        launch_k(norm_vec_kernel<T, NV, kLN, kMaxBlock, kBranch, true>, dim3(grid), dim3(block), 0, st, p);
+        launch_k(norm_vec_kernel<T, NV, kLN, kMaxBlock, kBranch, true, AW>, dim3(grid), dim3(block), 0, st, p);
         return;
       }
     }
-    launch_k(norm_vec_kernel<T, NV, kLN, kMaxBlock, kBranch>, dim3(grid), dim3(block), 0, st, p);
+    launch_k(norm_vec_kernel<T, NV, kLN, kMaxBlock, kBranch, false, AW>, dim3(grid), dim3(block), 0, st, p);
   } else {
     launch_k(norm_rows_kernel<T, NV, kLN, kMaxBlock, kBranch>, dim3(grid), dim3(block), 0, st, p);
   }
 }
 
 // Returns false when no instantiated kernel has this shape (a dispatcher bug).
-template <typename T, bool kVector, bool kLN, int kMaxBlock, bool kBranch>
+template <typename T, bool kVector, bool kLN, int kMaxBlock, bool kBranch, int AW = 4>
 bool launch_regs_b(NormParams p, int nv, int block, int64_t grid, cudaStream_t st) {
   constexpr int cap = kMaxNv<kBranch, kMaxBlock>;
   switch (nv) {
     case 1:
-      launch_nv<T, kVector, 1, kLN, kMaxBlock, kBranch>(p, block, grid, st);
+      launch_nv<T, kVector, 1, kLN, kMaxBlock, kBranch, AW>(p, block, grid, st);
       return true;
     case 2:
       if constexpr (cap >= 2) {
-        launch_nv<T, kVector, 2, kLN, kMaxBlock, kBranch>(p, block, grid, st);
+        launch_nv<T, kVector, 2, kLN, kMaxBlock, kBranch, AW>(p, block, grid, st);
         return true;
       }
       return false;
     case 3:
       if constexpr (cap >= 4 && kVector) {
-        launch_nv<T, kVector, 3, kLN, kMaxBlock, kBranch>(p, block, grid, st);
+        launch_nv<T, kVector, 3, kLN, kMaxBlock, kBranch, AW>(p, block, grid, st);
         return true;
       }
       return false;
     case 4:
       if constexpr (cap >= 4) {
-        launch_nv<T, kVector, 4, kLN, kMaxBlock, kBranch>(p, block, grid, st);
+        launch_nv<T, kVector, 4, kLN, kMaxBlock, kBranch, AW>(p, block, grid, st);
         return true;
       }
       return false;
     case 6:
       if constexpr (cap >= 8 && kVector) {
-        launch_nv<T, kVector, 6, kLN, kMaxBlock, kBranch>(p, block, grid, st);
+        launch_nv<T, kVector, 6, kLN, kMaxBlock, kBranch, AW>(p, block, grid, st);
         return true;
       }
       return false;
     case 8:
       if constexpr (cap >= 8) {
-        launch_nv<T, kVector, 8, kLN, kMaxBlock, kBranch>(p, block, grid, st);
+        launch_nv<T, kVector, 8, kLN, kMaxBlock, kBranch, AW>(p, block, grid, st);
         return true;
       }
       return false;
@@ -524,13 +525,14 @@ bool launch_regs_b(NormParams p, int nv, int block, int64_t grid, cudaStream_t s
 // Register budgets per block size: 256-thread blocks run four per SM, the
 // 512-thread vector shape two (so one row's loads overlap another's
 // reductions), the 1024-thread shape one.
-template <typename T, bool kVector, bool kLN>
+template <typename T, bool kVector, bool kLN, int AW = 4>
 bool launch_regs(NormParams p, int nv, int block, int64_t grid, cudaStream_t st) {
   const bool branch = p.branch != nullptr;
   if (block <= 256) {
-    return branch ? launch_regs_b<T, kVector, kLN, 256, true>(p, nv, block, grid, st)
-                  : launch_regs_b<T, kVector, kLN, 256, false>(p, nv, block, grid, st);
+    return branch ? launch_regs_b<T, kVector, kLN, 256, true, AW>(p, nv, block, grid, st)
+                  : launch_regs_b<T, kVector, kLN, 256, false, AW>(p, nv, block, grid, st);
   }
+  if constexpr (AW != 4) return false;  // narrow accesses: 256-thread shapes only
   if constexpr (kVector) {
     if (block == 512 && nv > 4)
       return branch ? false : launch_regs_b<T, kVector, kLN, 512, false>(p, nv, block, grid, st);
@@ -544,10 +546,26 @@ bool launch_regs(NormParams p, int nv, int block, int64_t grid, cudaStream_t st)
 template <typename T, bool kLN>
 int launch_norm(NormParams p, cudaStream_t st, const char *op) {
   constexpr int V = Elem<T>::kVec;
-  const bool vec = (p.cols % V == 0) && is_aligned16(p.dst) && is_aligned16(p.src) &&
-                   is_aligned16(p.w) && is_aligned16(p.b) && is_aligned16(p.branch) &&
-                   is_aligned16(p.ls) && is_aligned16(p.res_out);
-  const int n = vec ? V : 1;
+  const uintptr_t addr_bits = reinterpret_cast<uintptr_t>(p.dst) | reinterpret_cast<uintptr_t>(p.src) |
+                              reinterpret_cast<uintptr_t>(p.w) | reinterpret_cast<uintptr_t>(p.b) |
+                              reinterpret_cast<uintptr_t>(p.branch) | reinterpret_cast<uintptr_t>(p.ls) |
+                              reinterpret_cast<uintptr_t>(p.res_out);
+  const int64_t row_bytes = p.cols * static_cast<int64_t>(sizeof(T));
+  // Access width in 32-bit words: 16-byte vectors when rows and pointers allow;
+  // otherwise 8-byte (f32 or 16-bit rows whose bytes are a multiple of 8) or
+  // 4-byte (16-bit rows of even width) accesses, which keep the vector
+  // kernel's paired arithmetic for ragged widths (such as 250 columns) in
+  // place of element accesses; those take the 256-thread shapes only.
+  int aw = 0;
+  if (row_bytes % 16 == 0 && (addr_bits & 15u) == 0)
+    aw = 4;
+  else if (row_bytes % 8 == 0 && (addr_bits & 7u) == 0)
+    aw = 2;
+  else if (sizeof(T) == 2 && row_bytes % 4 == 0 && (addr_bits & 3u) == 0)
+    aw = 1;
+  if (aw != 0 && aw != 4 && p.cols / (V * aw / 4) > 256LL * (p.branch != nullptr ? 4 : 8)) aw = 0;
+  const bool vec = aw != 0;
+  const int n = vec ? V * aw / 4 : 1;
   const int64_t nvec = p.cols / n;
   // Up to 32 row values per thread (16 with a branch, which doubles the
   // loads held in registers): rows of up to 32768 (16384) elements.
@@ -585,8 +603,16 @@ int launch_norm(NormParams p, cudaStream_t st, const char *op) {
     if (grid > 0x7fffffffLL) return fail(XN_E_INVALID, "%s: too many rows (%lld)", op, (long long)p.rows);
     p.tpr = static_cast<int>(tpr);
     p.nvec = static_cast<int>(nvec);
-    const bool launched =
-        vec ? launch_regs<T, true, kLN>(p, nv, block, grid, st) : launch_regs<T, false, kLN>(p, nv, block, grid, st);
+    bool launched = false;
+    if (aw == 4) {
+      launched = launch_regs<T, true, kLN, 4>(p, nv, block, grid, st);
+    } else if (aw == 2) {
+      launched = launch_regs<T, true, kLN, 2>(p, nv, block, grid, st);
+    } else if (aw == 1) {
+      if constexpr (sizeof(T) == 2) launched = launch_regs<T, true, kLN, 1>(p, nv, block, grid, st);
+    } else {
+      launched = launch_regs<T, false, kLN>(p, nv, block, grid, st);
+    }
     if (!launched) return fail(XN_E_INVALID, "%s: internal error, no kernel for %d accesses per thread", op, nv);
   } else {
     if (p.rows > 0x7fffffffLL) return fail(XN_E_INVALID, "%s: too many rows (%lld)", op, (long long)p.rows);

@@ -496,7 +496,7 @@ constexpr int kMaxStages = 4;
 constexpr uint32_t kStageWaitLimit = 1u << 22;
 
 template <typename T, int NV, bool kCausal, bool kSkip>
-__global__ void __launch_bounds__(NV >= 8 ? 512 : 1024) softmax_staged_kernel(const SoftmaxParams p, int stages,
+__global__ void __launch_bounds__(512) softmax_staged_kernel(const SoftmaxParams p, int stages,
                                                                               int stage_bytes) {
   griddep_wait();
   griddep_release();
@@ -794,8 +794,10 @@ bool launch_softmax_regs(const SoftmaxParams &p, int nv, int block, int64_t grid
                   : launch_softmax_regs_c<T, kAccess, false>(p, nv, block, grid, st);
 }
 
-// Shared-memory-staged rows: 8 vectors per thread (blocks of up to 512
-// threads), two stage buffers. Used, as measured on B200, for 16-bit rows of
+// Shared-memory-staged rows: blocks of up to 512 threads (launch_softmax_staged
+// never launches more, for any NV), two stage buffers, 8 vectors per thread by
+// default (kStagedNv); launch_softmax_staged takes 5 or 6 instead when they
+// leave fewer empty access slots. Used, as measured on B200, for 16-bit rows of
 // 256 to 4096 vectors (2048 to 32768 elements) and f32 rows of 2049 to 4096
 // vectors (8196 to 16384 elements); narrower rows run as fast or faster in the
 // register-prefetching kernel, and 4096 vectors (64 KB) is the widest row the

@@ -140,3 +140,60 @@ def test_residual_add(oracle, xn, cuda, dtype, rows, cols, with_ls):
     Y = xn.residual_add(to_device(x, dtype, cuda), to_device(br, dtype, cuda),
                         to_device(ls, dtype, cuda) if with_ls else None)
     assert np.array_equal(from_device(Y, dtype), ref)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("rows,cols", [(1000, 250), (64, 1002), (6, 2046), (33, 10), (257, 36), (4, 4094)])
+@pytest.mark.parametrize("variant", ["rms", "rms_residual_ls", "ln", "ln_residual_ls", "ln_no_mean"])
+def test_norm_narrow_accesses(oracle, xn, cuda, dtype, rows, cols, variant):
+    """Rows whose byte width is a multiple of 8 or 4 but not 16 (16-bit rows of
+    even width such as Mimi's 250 scores, f32 rows of even width): 8- and
+    4-byte accesses with the vector kernel's arithmetic. Also a view whose
+    start is 4 bytes past a 16-byte boundary."""
+    x, br, w, b, ls = _inputs(rows * 5 + cols, rows, cols, dtype, ln=variant.startswith("ln"))
+    eps = 1e-5
+    branch = br if "residual" in variant else None
+    lsc = ls if "residual_ls" in variant else None
+    X, W, B = (to_device(a, dtype, cuda) for a in (x, w, b))
+    BR = None if branch is None else to_device(br, dtype, cuda)
+    LS = None if lsc is None else to_device(lsc, dtype, cuda)
+    if variant.startswith("rms"):
+        ref_y, ref_h = oracle.rms_norm_residual(x, branch, w, eps, dtype, layer_scale=lsc)
+        Y = torch.empty_like(X)
+        H = torch.empty_like(X) if branch is not None else None
+        xn.rms_norm_(Y, X, W, eps, branch=BR, layer_scale=LS, residual_out=H)
+        allow = None
+    else:
+        rm = variant != "ln_no_mean"
+        ref_y, ref_h = oracle.layer_norm_residual(x, branch, w, b, eps, dtype, layer_scale=lsc, remove_mean=rm)
+        if branch is None:
+            Y = xn.layer_norm_rm(X, W, B, eps, rm)
+            H = None
+        else:
+            Y, H = xn.layer_norm_residual(X, BR, W, B, eps, layer_scale=LS, remove_mean=rm)
+        allow = ln_allowance(ref_h if branch is not None else x, w, dtype, rm)
+    if H is not None:
+        assert np.array_equal(from_device(H, dtype), ref_h), "residual output must be bit-exact"
+    assert_close(from_device(Y, dtype), ref_y, dtype, f"{variant} {dtype} {rows}x{cols} narrow", extra_abs=allow)
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16", "f32"])
+def test_norm_view_4_byte_aligned(oracle, xn, cuda, dtype):
+    """A [rows, 4096] view starting 4 bytes past a 16-byte boundary: 4-byte
+    (16-bit) / scalar (f32) accesses; results as the aligned tensor's."""
+    rows, cols = 37, 4096
+    x, br, w, b, ls = _inputs(9, rows, cols, dtype)
+    ref_y = oracle.rms_norm(x, w, 1e-5, dtype)
+    t = to_device(x, dtype, cuda)
+    step = 4 // t.element_size()
+    big = torch.empty(rows * cols + step, dtype=t.dtype, device=cuda)
+    X = big[step:].view(rows, cols)
+    X.copy_(t)
+    Y = torch.empty_like(X)
+    xn.rms_norm_(Y, X, to_device(w, dtype, cuda), 1e-5)
+    assert_close(from_device(Y, dtype), ref_y, dtype, f"rms_norm {dtype} 4-byte-aligned view")
+    ref_ln = oracle.layer_norm(x, w, b, 1e-5, dtype)
+    Z = torch.empty_like(X)
+    xn.layer_norm_(Z, X, to_device(w, dtype, cuda), to_device(b, dtype, cuda), 1e-5)
+    assert_close(from_device(Z, dtype), ref_ln, dtype, f"layer_norm {dtype} 4-byte-aligned view",
+                 extra_abs=ln_allowance(x, w, dtype))
