@@ -714,7 +714,7 @@ def cpu_decode_rate(act: str, steps: int = 3, batch: int = 16) -> dict:
 # ---------------------------------------------------------------------------
 SWEEP_OPS = ["rms_norm_residual", "layer_norm", "rope", "swiglu", "softmax", "embedding_gather"]
 # Further ops the sweep can run (--sweep-ops), outside benchmark config 5's list.
-SWEEP_EXTRA_OPS = ["silu", "gelu_erf", "residual_add", "softmax_causal", "causal_mask", "rvq_decode"]
+SWEEP_EXTRA_OPS = ["silu", "gelu_erf", "residual_add", "softmax_causal", "causal_mask", "rvq_decode", "copy"]
 RVQ_BINS, RVQ_BOOKS = 2048, 8
 
 
@@ -737,7 +737,7 @@ def sweep(torch, xn, device, widths, rows_list, dtypes, reps: int, mem_cap_gb: f
                 for rows in rows_list:
                     n_tensors = {"rms_norm_residual": 4, "layer_norm": 2, "rope": 2, "swiglu": 3, "softmax": 2,
                                  "embedding_gather": 1, "silu": 2, "gelu_erf": 2, "residual_add": 3,
-                                 "softmax_causal": 2, "causal_mask": 1, "rvq_decode": 1}[op]
+                                 "softmax_causal": 2, "causal_mask": 1, "rvq_decode": 1, "copy": 2}[op]
                     point = {"op": op, "dtype": dname, "rows": rows, "cols": cols, "n_gpus": world}
                     # Causal ops: prefill-shaped scores, slices of t1 = 1024 queries over `cols`
                     # keys, the last query seeing every key (offset = cols - t1).
@@ -791,6 +791,12 @@ def sweep(torch, xn, device, widths, rows_list, dtypes, reps: int, mem_cap_gb: f
                     elif op == "softmax":
                         x, y = rnd(lrows, cols), torch.empty(lrows, cols, dtype=dt, device=device)
                         fn = lambda: xn.softmax_(y, x)  # noqa: E731
+                        nbytes = 2 * rows * cols * s
+                    elif op == "copy":
+                        # Not a library op: torch's device copy of the same bytes, the
+                        # reference for what a launch of this size reaches at all.
+                        x, y = rnd(lrows, cols), torch.empty(lrows, cols, dtype=dt, device=device)
+                        fn = lambda: y.copy_(x)  # noqa: E731
                         nbytes = 2 * rows * cols * s
                     elif op in ("silu", "gelu_erf"):
                         x, y = rnd(lrows, cols), torch.empty(lrows, cols, dtype=dt, device=device)

@@ -216,8 +216,13 @@ __device__ __forceinline__ float unary_op(float x) {
 
 constexpr int kBlock = 256;
 constexpr int kUnroll = 4;
+// Accesses per thread of the unary kernel on large tensors: 8 (128 bytes in
+// flight, one input) measured 2-4 points of the copy peak above 4 for bf16 /
+// f16 SiLU and GELU at 67 M - 1 G elements, and 2 lost 3-10; SwiGLU, with two
+// inputs, keeps kUnroll (8 accesses of each lost 3-10 points there).
+constexpr int kUnaryUnroll = 8;
 
-// kU accesses per thread: kUnroll for large tensors; 1 for tensors whose
+// kU accesses per thread: kUnaryUnroll for large tensors; 1 for tensors whose
 // one-access grid fits in one wave (8 blocks per SM), where the per-thread
 // chain of work, not bandwidth, sets the time.
 template <typename T, int OP, bool kVector, int kU>
@@ -462,13 +467,13 @@ int launch_unary(void *dst, const void *src, int64_t n, int op, cudaStream_t st)
   constexpr int V = Elem<T>::kVec;
   const bool vec = is_aligned16(dst) && is_aligned16(src);
   const int64_t nacc = vec ? n / V : n;
-  const int64_t per_block = static_cast<int64_t>(kBlock) * kUnroll;
+  const int64_t per_block = static_cast<int64_t>(kBlock) * kUnaryUnroll;
   if (ceil_div(nacc > 0 ? nacc : 1, static_cast<int64_t>(kBlock)) <= static_cast<int64_t>(sm_count()) * 8) {
     launch_unary_u<T, 1>(dst, src, n, op, vec, ceil_div(nacc > 0 ? nacc : 1, kBlock), st);
   } else {
     const int64_t grid = ceil_div(nacc, per_block);
     if (grid > 0x7fffffffLL) return fail(XN_E_INVALID, "xn_unary: too many elements");
-    launch_unary_u<T, kUnroll>(dst, src, n, op, vec, grid, st);
+    launch_unary_u<T, kUnaryUnroll>(dst, src, n, op, vec, grid, st);
   }
   return check_launch("xn_unary");
 }
