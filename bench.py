@@ -473,7 +473,12 @@ def config1_rate(torch, xn, device, reps: int = 20) -> dict:
     for name, (fn, nbytes) in ops.items():
         ms = time_flushed(torch, fn, flush, reps)
         gbs = nbytes / (ms * 1e-3) / 1e9
-        out[name] = {"us": round(ms * 1e3, 2), "bytes": nbytes, "gbs": round(gbs, 1), "frac": round(gbs / peak, 3)}
+        # The size reference: torch's device copy moving the same bytes (half read, half written).
+        a = torch.empty(nbytes // 8, dtype=torch.float32, device=device)
+        b = torch.empty_like(a)
+        copy_ms = time_flushed(torch, lambda: b.copy_(a), flush, reps)
+        out[name] = {"us": round(ms * 1e3, 2), "bytes": nbytes, "gbs": round(gbs, 1), "frac": round(gbs / peak, 3),
+                     "copy_same_bytes_us": round(copy_ms * 1e3, 2)}
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
     stream = torch.cuda.Stream(device)
@@ -495,7 +500,8 @@ def config1_rate(torch, xn, device, reps: int = 20) -> dict:
             "what": "benchmark config 1, f32: RMSNorm [512, 2048], RoPE half-split on Q/K [1, 512, 16, 128] (BTHD), "
                     "SwiGLU [512, 5632], causal softmax [1, 16, 512, 512]; each op after an L2 flush (inputs are "
                     "smaller than L2), median of launches; pipeline = the four ops as one CUDA graph after a flush; "
-                    "causal softmax bytes = unmasked reads + all writes"}
+                    "causal softmax bytes = unmasked reads + all writes; copy_same_bytes_us = torch's device copy "
+                    "of the same bytes, timed the same way (what a launch of that size takes at all)"}
 
 
 # ---------------------------------------------------------------------------
