@@ -922,6 +922,12 @@ int launch_softmax(SoftmaxParams p, cudaStream_t st) {
     // vectors sit in one warp and longer ones span half as many warps, with
     // fewer block barriers per row.
     if ((vec || win) && nvec > 128) tpr = pow2_ceil(ceil_div(nvec, 8));
+    // Window rows of 17-64 vectors (Mimi's 250 attention columns: 33 bf16 / 64
+    // f32 vectors) in groups of 8 threads with 5-8 accesses each rather than 16
+    // with 3-4: fewer shuffle steps per row (bf16 250 columns: 0.41 -> 0.46 of
+    // the copy peak, f32 0.73 -> 0.80, causal 0.39 -> 0.48 / 0.69 -> 0.76).
+    // Whole-vector rows of that size measured slower so, and keep the wider groups.
+    if (win && nvec > 16 && nvec <= 64) tpr = pow2_ceil(ceil_div(nvec, 8));
     // Pairs are 4-byte registers: 8 per thread cost little and halve the
     // reduction steps per element.
     if (pair) tpr = pow2_ceil(ceil_div(nvec, 8));
