@@ -1030,6 +1030,8 @@ def main() -> int:
     ap.add_argument("--decode-only", action="store_true",
                     help="run only the config-3 streaming-decode measurement")
     ap.add_argument("--decode-acts", default="silu,gelu_erf", help="MLP activations for --decode-only")
+    ap.add_argument("--mimi-stream-only", action="store_true",
+                    help="run only the Mimi streaming-decode measurement (--mimi-stream-steps frames)")
     ap.add_argument("--gather-context", action="store_true",
                     help="time the config-4 gather after dirty-L2 and clean-L2 predecessors")
     ap.add_argument("--rows", type=int, default=CFG["batch"] * CFG["seq"],
@@ -1091,6 +1093,10 @@ def main() -> int:
         xn.lib()
         for pt in gather_context(torch, xn, dev):
             print(json.dumps({"op": "embedding_gather", **pt}), flush=True)
+        return 0
+    if args.mimi_stream_only:
+        xn.lib()
+        print(json.dumps({"mimi_stream_decode": mimi_stream_rate(torch, dev, args.mimi_stream_steps)}), flush=True)
         return 0
     if args.decode_only:
         xn.lib()
