@@ -91,8 +91,11 @@ struct RingKvCache {
   size_t total = 0;
 };
 
-// Which causal mask the decode attention applies (xn_fused.h XN_MASK_*).
-enum class DecodeMask { Relative = XN_MASK_RELATIVE, Absolute = XN_MASK_ABSOLUTE };
+// Which causal mask / position bookkeeping the decode attention applies
+// (xn_fused.h XN_MASK_*): CacheLen is mimi-rs's StreamingTransformer (offset =
+// the cache's length before the step), Absolute Pocket's Mimi attention,
+// Relative the flow LM's additive mask.
+enum class DecodeMask { Relative = XN_MASK_RELATIVE, Absolute = XN_MASK_ABSOLUTE, CacheLen = XN_MASK_CACHE_LEN };
 
 // The CUDA device of the reference (cuda_backend.rs:34-54): one stream on
 // which every op is enqueued.

@@ -70,9 +70,25 @@ def test_argument_errors_without_gpu(xn):
     # head dim outside {32, 64, 128}; context > cap; unknown mask mode; context above the shared-memory bound
     assert _rc(xn, at, 1, 1, 1, 1, 2, 4, 1, 48, 0, None, 16, 16, 0, 0.125, 1, None) == xn.XN_E_INVALID
     assert _rc(xn, at, 1, 1, 1, 1, 2, 4, 1, 64, 0, None, 16, 17, 0, 0.125, 1, None) == xn.XN_E_INVALID
-    assert _rc(xn, at, 1, 1, 1, 1, 2, 4, 1, 64, 0, None, 16, 16, 2, 0.125, 1, None) == xn.XN_E_INVALID
+    assert _rc(xn, at, 16, 16, 16, 16, 2, 4, 1, 64, 0, None, 16, 16, 3, 0.125, 1, None) == xn.XN_E_INVALID
+    assert "unknown mask mode" in xn.last_error()
     assert _rc(xn, at, 1, 1, 1, 1, 2, 4, 1, 64, 0, None, 9000, 8193, 0, 0.125, 1, None) == xn.XN_E_INVALID
     assert _rc(xn, "xn_position_advance", None, 1, None) == xn.XN_E_INVALID
+    # The fused decode step rotates at total (XN_MASK_ABSOLUTE): position 1000 is past 300 table rows.
+    # XN_MASK_CACHE_LEN rotates at min(total, context) = 250, which is in range, so that call gets as
+    # far as the null output pointer (every call here fails a host check before any launch).
+    st = "xn_decode_attention_step"
+    assert _rc(xn, st, None, 16, 16, 16, 16, 16, 1, 2, 1, 64, 1000, None, 300, 256, 250, xn.XN_MASK_ABSOLUTE, 0.125,
+               1, 1, None, None) == xn.XN_E_RANGE
+    assert _rc(xn, st, None, 16, 16, 16, 16, 16, 1, 2, 1, 64, 1000, None, 300, 256, 250, xn.XN_MASK_CACHE_LEN,
+               0.125, 1, 1, None, None) == xn.XN_E_INVALID
+    assert "null pointer" in xn.last_error()
+    assert _rc(xn, st, None, 16, 16, 16, 16, 16, 1, 2, 1, 64, 0, None, 300, 256, 250, 3, 0.125, 1, 1, None,
+               None) == xn.XN_E_INVALID
+    # softmax with a status word: the checks of xn_softmax
+    assert _rc(xn, "xn_softmax_status", 16, 16, -1, 4, 0, 1.0, 0, 1, 0, None, 2, None) == xn.XN_E_INVALID
+    assert _rc(xn, "xn_softmax_status", 16, 16, 6, 4, 0, 1.0, 1, 4, 0, None, 2, None) == xn.XN_E_INVALID
+    assert _rc(xn, "xn_softmax_status", 16, 16, 6, 4, 0, 1.0, 0, 1, 0, None, 9, None) == xn.XN_E_DTYPE
     assert L.xn_abi_version() == 1
 
 
