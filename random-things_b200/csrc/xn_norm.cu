@@ -575,7 +575,10 @@ int launch_norm(NormParams p, cudaStream_t st, const char *op) {
   // Row-group shape: 256-thread blocks take up to 8 accesses per thread (4
   // with a branch); wider vector rows without a branch use 512-thread groups
   // with 8; the rest groups of up to 1024 threads with up to 4.
-  const int cap256 = p.branch != nullptr ? 4 : 8;
+  // LayerNorm rows of at most 32 vectors (256 bf16 columns) take 8-thread groups
+  // with 4 accesses each rather than 4 with 8 (0.77 -> 0.80 of the copy peak at
+  // 262144 x 256 bf16; rows of 64 vectors measured slower so).
+  const int cap256 = (p.branch != nullptr || (kLN && aw == 4 && p.cols / V <= 32)) ? 4 : 8;
   int64_t tpr = 0;
   if (nvec <= 256LL * cap256) {
     tpr = pow2_ceil(ceil_div(nvec, vec ? cap256 : 4));
