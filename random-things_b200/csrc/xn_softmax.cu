@@ -1006,6 +1006,43 @@ __global__ void __launch_bounds__(256) causal_mask_kernel(void *dst, int64_t bh,
   }
 }
 
+// Rows of whole 16-byte vectors (t2 a multiple of the vector, dst 16-byte
+// aligned): a warp per masked row as above, its lanes walking only the row's
+// masked vectors from the one holding the first masked column. That vector
+// keeps its live elements: lane 0 rewrites it (no other thread touches it), and
+// the vectors after it are whole -inf stores. t2 < 2^30 (checked on the host),
+// so every in-row index is an int; the row base is formed in 64 bits.
+template <typename T>
+__global__ void __launch_bounds__(256) causal_mask_vec_kernel(void *dst, int64_t bh, int64_t t1, int t2v,
+                                                              int64_t offset, int64_t mrows) {
+  griddep_wait();
+  griddep_release();
+  constexpr int N = Elem<T>::kVec;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (i >= mrows) return;
+  const int lane = threadIdx.x & 31;
+  const int first = static_cast<int>(offset + i + 1);  // first masked column, < t2
+  const int vf = first / N, rem = first - vf * N;
+  const T ninf = Elem<T>::from_f32(-INFINITY);
+  uint4 v;
+  T *vt = reinterpret_cast<T *>(&v);
+#pragma unroll
+  for (int j = 0; j < N; ++j) vt[j] = ninf;
+  const int v0 = rem != 0 ? vf + 1 : vf;  // first whole masked vector
+  for (int64_t b = blockIdx.y; b < bh; b += gridDim.y) {
+    uint4 *row = reinterpret_cast<uint4 *>(static_cast<T *>(dst) + (b * t1 + i) * static_cast<int64_t>(t2v) * N);
+    if (rem != 0 && lane == 0) {
+      uint4 w = row[vf];
+      T *wt = reinterpret_cast<T *>(&w);
+#pragma unroll
+      for (int j = 0; j < N; ++j)
+        if (j >= rem) wt[j] = ninf;
+      row[vf] = w;
+    }
+    for (int c = v0 + lane; c < t2v; c += 32) row[c] = v;
+  }
+}
+
 }  // namespace
 }  // namespace xn
 
@@ -1076,7 +1113,10 @@ int xn_causality_mask(void *dst, int64_t bh, int64_t t1, int64_t t2, int64_t off
   const int64_t gy = bh < 65535 ? bh : 65535;
   const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy));
   const bool narrow = t1 < (int64_t{1} << 30) && t2 < (int64_t{1} << 30) && offset < (int64_t{1} << 30);
-  XN_DISPATCH_FLOAT(dtype, if (narrow) launch_k(causal_mask_kernel<T, int>, grid, dim3(256), 0, as_stream(stream), dst, bh, t1, t2, offset, mrows);
+  // Whole-vector rows: t2 a multiple of the 16-byte vector and dst aligned.
+  const bool vec_rows = narrow && is_aligned16(dst) && (t2 * dtype_bytes(dtype)) % 16 == 0;
+  XN_DISPATCH_FLOAT(dtype, if (vec_rows) launch_k(causal_mask_vec_kernel<T>, grid, dim3(256), 0, as_stream(stream), dst, bh, t1, static_cast<int>(t2 / Elem<T>::kVec), offset, mrows);
+                    else if (narrow) launch_k(causal_mask_kernel<T, int>, grid, dim3(256), 0, as_stream(stream), dst, bh, t1, t2, offset, mrows);
                     else launch_k(causal_mask_kernel<T, int64_t>, grid, dim3(256), 0, as_stream(stream), dst, bh, t1, t2, offset, mrows);
                     return check_launch("xn_causality_mask"));
   return fail(XN_E_DTYPE, "xn_causality_mask: unsupported dtype %d", dtype);

@@ -87,7 +87,10 @@ def test_softmax_causal(oracle, xn, cuda, dtype, shape, offset):
 @pytest.mark.parametrize("shape,offset", [((1, 3, 4), 0), ((1, 2, 4), 2), ((2, 4, 33, 70), 5), ((6, 1, 9), 3),
                                           ((16, 16, 64, 203), 101), ((2, 3, 301, 4096), 3792),
                                           ((2, 3, 1024, 256), 0), ((2, 2, 8, 16), 15), ((1, 2, 4, 8), 100),
-                                          ((50, 60, 3, 5), 0), ((50, 60, 3, 5), 1)])
+                                          ((50, 60, 3, 5), 0), ((50, 60, 3, 5), 1),
+                                          # whole-vector rows (the lanes-over-masked-vectors kernel)
+                                          ((3, 5, 33, 64), 0), ((2, 4, 70, 72), 5), ((1, 3, 1024, 1024), 0),
+                                          ((70000, 1, 2, 64), 3)])
 def test_causality_mask(oracle, xn, cuda, dtype, shape, offset):
     r = rng(len(shape) + offset)
     x = to_storage(randn(r, shape), dtype)
