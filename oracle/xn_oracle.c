@@ -180,9 +180,12 @@ static const float kFrac1Sqrt2 = (float)0.707106781186547524400844362104849039;
     }                                                                                  \
   }                                                                                    \
                                                                                        \
-  /* cpu_backend.rs:197-204 (GeluErf) and :213-215 (Silu) */                           \
+  /* cpu_backend.rs:197-204 (GeluErf), :213-215 (Silu) and the exp of one element   \
+     of the softmax, :681 ((s - max).exp() on T: exp in f32, rounded to T) */          \
   static void unary_##SUF(ST *dst, const ST *src, int64_t len, int op) {               \
-    if (op == 0) {                                                                     \
+    if (op == 2) {                                                                     \
+      for (int64_t i = 0; i < len; i++) dst[i] = FROM(expf(TO(src[i])));               \
+    } else if (op == 0) {                                                              \
       for (int64_t i = 0; i < len; i++) {                                              \
         float s = TO(src[i]);                                                          \
         float e = tb_##SUF(expf(tb_##SUF(0.0f - s)));                                  \

@@ -60,7 +60,7 @@ void xo_rope(int dtype, void *dst, const void *src, const void *cos,
 void xo_rope_i(int dtype, void *dst, const void *src, const void *cos,
                const void *sin, int64_t b, int64_t h, int64_t t, int64_t d,
                int64_t pos);
-/* cpu_backend.rs:184-222; op 0 = Silu, 1 = GeluErf */
+/* cpu_backend.rs:184-222; op 0 = Silu, 1 = GeluErf, 2 = T(exp(x)) (the softmax step, :681) */
 void xo_unary(int dtype, void *dst, const void *src, int64_t len, int op);
 /* cpu_backend.rs:224-258; op 0 = Add, 1 = Sub, 2 = Mul, 3 = Div */
 void xo_binary(int dtype, void *dst, const void *lhs, const void *rhs,

@@ -94,7 +94,7 @@ def _chk(a: np.ndarray, dtype: str) -> np.ndarray:
 
 
 BINARY_OPS = {"add": 0, "sub": 1, "mul": 2, "div": 3}
-UNARY_OPS = {"silu": 0, "gelu_erf": 1}
+UNARY_OPS = {"silu": 0, "gelu_erf": 1, "exp": 2}  # "exp": the softmax exp step, cpu_backend.rs:681
 
 
 def rms_norm(x, alpha, eps: float, dtype: str):
@@ -149,7 +149,8 @@ def rope(x, cos, sin, pos: int, dtype: str, interleaved: bool = False):
 
 
 def unary(x, op: str, dtype: str):
-    """cpu_backend.rs:184-222 for Silu / GeluErf."""
+    """cpu_backend.rs:184-222 for Silu / GeluErf; "exp" is T(exp(x)), the
+    per-element step of the softmax (cpu_backend.rs:681)."""
     x = _chk(x, dtype)
     out = np.empty_like(x)
     lib().xo_unary(DTYPES[dtype], _ptr(out), _ptr(x), x.size, UNARY_OPS[op])
