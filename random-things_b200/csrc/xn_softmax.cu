@@ -60,6 +60,7 @@ struct Pair<__nv_bfloat16> {
   __device__ __forceinline__ static float2 to_f2(T2 v) { return bf2_to_f2(*reinterpret_cast<uint32_t *>(&v)); }
   __device__ __forceinline__ static T2 from_f2(float a, float b) { return __floats2bfloat162_rn(a, b); }
   __device__ __forceinline__ static T2 neg_inf() { return splat(-INFINITY); }
+  static constexpr uint32_t kNegInfBits = 0xff80ff80u, kPosInfBits = 0x7f807f80u, kNanBits = 0x7fc07fc0u;
   // Keeps the low element, sets the high one to -inf.
   __device__ __forceinline__ static T2 mask_high(T2 v) {
     return __halves2bfloat162(__low2bfloat16(v), __float2bfloat16(-INFINITY));
@@ -79,6 +80,7 @@ struct Pair<__half> {
   __device__ __forceinline__ static float2 to_f2(T2 v) { return __half22float2(v); }
   __device__ __forceinline__ static T2 from_f2(float a, float b) { return __floats2half2_rn(a, b); }
   __device__ __forceinline__ static T2 neg_inf() { return splat(-INFINITY); }
+  static constexpr uint32_t kNegInfBits = 0xfc00fc00u, kPosInfBits = 0x7c007c00u, kNanBits = 0x7e007e00u;
   __device__ __forceinline__ static T2 mask_high(T2 v) {
     return __halves2half2(__low2half(v), __float2half(-INFINITY));
   }
@@ -182,10 +184,24 @@ __global__ void __launch_bounds__(512) softmax_rows_kernel(const SoftmaxParams p
 // kDead: accesses wholly past `lim` (common with a causal mask or a window)
 // are set to -inf at once; otherwise the rare padding access takes the
 // per-element path, which keeps the check off the common path.
-template <typename T, int NV, typename U, bool kWin = false, bool kDead = false>
+// kDead without a window (causal rows): the tests are made per slot k, on the
+// elements [(g0 + k * tpr) * N, (g0 + k * tpr + tpr) * N) that the row group's
+// tpr threads hold in it (g0: the group's first vector), so the whole group
+// takes one branch: a dead slot, a live slot, or the one slot holding the
+// row's last live element, where each thread masks its access with bit
+// selects instead of per-element branches (kSlot: 16-bit rows, where it
+// measured faster; f32 rows measured slower with it, and the
+// shared-memory-staged kernel keeps the per-thread tests, with which ptxas
+// holds its row in registers without spilling).
+template <typename T, bool kDead, bool kWin>
+constexpr bool kSlotTests = kDead && !kWin && !std::is_same_v<T, float>;
+
+template <typename T, int NV, typename U, bool kWin = false, bool kDead = false,
+          bool kSlot = kSlotTests<T, kDead, kWin>>
 __device__ __forceinline__ float softmax_prep(U (&cur)[NV], int lr, int tpr, int lim, const SoftmaxParams &p,
-                                              float &mn, int lo = 0) {
+                                              float &mn, int lo = 0, int g0 = 0) {
   constexpr int N = static_cast<int>(sizeof(U) / sizeof(T));
+  static_assert(!kSlot || (kDead && !kWin), "slot tests are for masked rows without a window");
   const int lo_ = kWin ? lo : 0;
   if constexpr (std::is_same_v<T, float>) {
     static_assert(sizeof(U) == 16, "f32 rows use 16-byte accesses");
@@ -197,7 +213,23 @@ __device__ __forceinline__ float softmax_prep(U (&cur)[NV], int lr, int tpr, int
       const int a0 = (lr + k * tpr) * N - lo_;  // row position of the access's first element
       float2 *x2 = reinterpret_cast<float2 *>(&cur[k]);
       float *x = reinterpret_cast<float *>(&cur[k]);
-      if (kDead && a0 >= lim) {  // masked, or past the row (a window's spare accesses)
+      if constexpr (kSlot) {
+        const int s0 = (g0 + k * tpr) * N;
+        if (s0 >= lim) {
+          x2[0] = x2[1] = splat2(-INFINITY);
+        } else if (s0 + tpr * N <= lim) {
+          if (p.scaled) {
+            x2[0] = __fmul2_rn(x2[0], sc);
+            x2[1] = __fmul2_rn(x2[1], sc);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < N; ++j) {
+            const float v = p.scaled ? __fmul_rn(x[j], p.scale) : x[j];
+            x[j] = a0 + j < lim ? v : -INFINITY;
+          }
+        }
+      } else if (kDead && a0 >= lim) {  // masked, or past the row (a window's spare accesses)
         x2[0] = x2[1] = splat2(-INFINITY);
       } else if ((!kWin || a0 >= 0) && a0 + N <= lim) {
         if (p.scaled) {
@@ -227,7 +259,33 @@ __device__ __forceinline__ float softmax_prep(U (&cur)[NV], int lr, int tpr, int
     for (int k = 0; k < NV; ++k) {
       const int a0 = (lr + k * tpr) * N - lo_;
       T2 *w = reinterpret_cast<T2 *>(&cur[k]);
-      if (kDead && a0 >= lim) {  // masked, or past the row (a window's spare accesses)
+      if constexpr (kSlot) {
+        const int s0 = (g0 + k * tpr) * N;
+        if (s0 >= lim) {
+#pragma unroll
+          for (int j = 0; j < W; ++j) w[j] = P::neg_inf();
+        } else if (s0 + tpr * N <= lim) {
+#pragma unroll
+          for (int j = 0; j < W; ++j) {
+            if (p.scaled) w[j] = __hmul2(w[j], sc2);
+            mn2 = __hmin2(mn2, w[j]);
+          }
+        } else {
+          // Element 2j of the access is the low half of word j; nl of the
+          // access's elements are live (none when nl <= 0).
+          const int nl = lim - a0;
+#pragma unroll
+          for (int j = 0; j < W; ++j) {
+            if (p.scaled) w[j] = __hmul2(w[j], sc2);
+            const uint32_t m = nl > 2 * j + 1 ? 0xffffffffu : (nl > 2 * j ? 0x0000ffffu : 0u);
+            const uint32_t v = *reinterpret_cast<const uint32_t *>(&w[j]);
+            const uint32_t live = v & m;
+            const uint32_t lo_bits = live | (P::kPosInfBits & ~m);  // +inf where masked, for the minimum
+            *reinterpret_cast<uint32_t *>(&w[j]) = live | (P::kNegInfBits & ~m);
+            mn2 = __hmin2(mn2, *reinterpret_cast<const T2 *>(&lo_bits));
+          }
+        }
+      } else if (kDead && a0 >= lim) {  // masked, or past the row (a window's spare accesses)
 #pragma unroll
         for (int j = 0; j < W; ++j) w[j] = P::neg_inf();
       } else if ((!kWin || a0 >= 0) && a0 + N <= lim) {
@@ -281,9 +339,23 @@ __device__ __forceinline__ float softmax_prep(U (&cur)[NV], int lr, int tpr, int
 //
 // kSkip: vectors starting at or past `lim` hold only masked entries; they
 // become +0 without the arithmetic (the same values and sums: exp(-inf) = +0).
+// For 16-bit rows without a window the test is per slot (softmax_prep's
+// kSlot): the masked accesses of the slot holding the row's last live element
+// take the arithmetic on their -inf entries, which gives the same +0.
+template <typename T, int NV, bool kSkip, typename U, bool kWin = false>
+__device__ __forceinline__ bool access_dead(int lr, int k, int tpr, int lim, int lo, int g0) {
+  constexpr int N = static_cast<int>(sizeof(U) / sizeof(T));
+  if constexpr (!kSkip)
+    return false;
+  else if constexpr (kSlotTests<T, kSkip, kWin>)
+    return (g0 + k * tpr) * N >= lim;
+  else
+    return (lr + k * tpr) * N - lo >= lim;
+}
+
 template <typename T, int NV, bool kSkip, typename U, bool kWin = false>
 __device__ __forceinline__ float softmax_exp(U (&cur)[NV], float mx, float mn, int lr, int tpr, int lim,
-                                             int lo = 0) {
+                                             int lo = 0, int g0 = 0) {
   constexpr int N = static_cast<int>(sizeof(U) / sizeof(T));
   const int lo_ = kWin ? lo : 0;
   float2 s2 = make_float2(0.f, 0.f);
@@ -291,7 +363,7 @@ __device__ __forceinline__ float softmax_exp(U (&cur)[NV], float mx, float mn, i
     const float2 nmx = splat2(-mx);
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
-      if (kSkip && (lr + k * tpr) * N - lo_ >= lim) {
+      if (access_dead<T, NV, kSkip, U, kWin>(lr, k, tpr, lim, lo_, g0)) {
         cur[k] = U{};
         continue;
       }
@@ -322,7 +394,7 @@ __device__ __forceinline__ float softmax_exp(U (&cur)[NV], float mx, float mn, i
     auto run = [&](auto kind) {
 #pragma unroll
       for (int k = 0; k < NV; ++k) {
-        if (kSkip && (lr + k * tpr) * N - lo_ >= lim) {
+        if (access_dead<T, NV, kSkip, U, kWin>(lr, k, tpr, lim, lo_, g0)) {
           cur[k] = U{};
           continue;
         }
@@ -344,22 +416,37 @@ __device__ __forceinline__ float softmax_exp(U (&cur)[NV], float mx, float mn, i
 }
 
 // y = T(e / s) for the accesses below nvec, stored to the row at dst_row.
-// s >= 1 for a live row: its maximum contributes exp(0). kSkip: the +0
-// accesses at or past `lim` are stored as they are. kWin: dst_row points at
-// the window start; accesses that reach outside the row's `cols` elements
-// store only the row's own elements.
+// s >= 1 for a live row: its maximum contributes exp(0). kSkip: the accesses
+// that softmax_exp skipped hold only masked entries, whose quotient 0 / s is
+// +0, stored without the division; or NaN when s is NaN (a live +inf or NaN,
+// or a row whose live entries are all -inf: the reference's masked outputs
+// are NaN then too). kWin: dst_row points at the window start; accesses that
+// reach outside the row's `cols` elements store only the row's own elements.
+template <typename T, typename U>
+__device__ __forceinline__ U nan_access() {
+  uint32_t w = 0x7fc00000u;
+  if constexpr (!std::is_same_v<T, float>) w = Pair<T>::kNanBits;
+  if constexpr (sizeof(U) == 16)
+    return make_uint4(w, w, w, w);
+  else
+    return w;
+}
+
 template <typename T, int NV, bool kSkip, typename U, bool kWin = false>
 __device__ __forceinline__ void softmax_store(U (&cur)[NV], float s, T *dst_row, int lr, int tpr, int nvec,
-                                              int lim, int lo = 0, int cols = 0) {
+                                              int lim, int lo = 0, int cols = 0, int g0 = 0) {
   constexpr int N = static_cast<int>(sizeof(U) / sizeof(T));
   const int lo_ = kWin ? lo : 0;
   const float2 rs = splat2(__frcp_rn(s)), ns = splat2(-s);
+  // f32 rows divide their skipped (+0) accesses too: 0 / s gives the NaN of a
+  // NaN sum by itself, and measured faster than a separate NaN pass.
+  constexpr bool kSkipDiv = kSkip && !std::is_same_v<T, float>;
 #pragma unroll
   for (int k = 0; k < NV; ++k) {
     const int vi = lr + k * tpr;
     if (vi < nvec) {
       const int a0 = vi * N - lo_;
-      if (kSkip && a0 >= lim) {
+      if (access_dead<T, NV, kSkipDiv, U, kWin>(lr, k, tpr, lim, lo_, g0)) {
         // masked: already +0
       } else if constexpr (std::is_same_v<T, float>) {
         float2 *x2 = reinterpret_cast<float2 *>(&cur[k]);
@@ -382,6 +469,26 @@ __device__ __forceinline__ void softmax_store(U (&cur)[NV], float s, T *dst_row,
 #pragma unroll
         for (int j = 0; j < N; ++j)
           if (a0 + j >= 0 && a0 + j < cols) dst_row[vi * N + j] = el[j];
+      }
+    }
+  }
+  if (kSkipDiv && isnan(s)) {
+    // Rare, and after the loop so that it costs the loop nothing: with a NaN
+    // sum every output of the row is NaN (e / NaN), the skipped ones included.
+    const U nan = nan_access<T, U>();
+    const T *el = reinterpret_cast<const T *>(&nan);
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int vi = lr + k * tpr;
+      if (vi < nvec) {
+        const int a0 = vi * N - lo_;
+        if (!kWin || (a0 >= 0 && a0 + N <= cols)) {
+          store_access<U>(dst_row + vi * N, nan);
+        } else {
+#pragma unroll
+          for (int j = 0; j < N; ++j)
+            if (a0 + j >= 0 && a0 + j < cols) dst_row[vi * N + j] = el[j];
+        }
       }
     }
   }
@@ -575,7 +682,7 @@ __global__ void __launch_bounds__(512) softmax_staged_kernel(const SoftmaxParams
       if (vi * N < lim) cur[k] = buf[vi];
     }
     float mn;
-    float m = softmax_prep<T, NV, uint4, false, kSkip>(cur, tid, tpr, lim, p, mn);
+    float m = softmax_prep<T, NV, uint4, false, kSkip, false>(cur, tid, tpr, lim, p, mn);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     if ((tid & 31) == 0) red_max[tid >> 5] = m;
@@ -667,21 +774,24 @@ __global__ void __launch_bounds__(kClusterThreads, 2) softmax_cluster_kernel(con
   }
   float mn;
   const float m =
-      group_max<false>(softmax_prep<T, NV, uint4, false, kCausal>(cur, v0 + tid, tpr, lim, p, mn), tpr, red_max);
+      group_max<false>(softmax_prep<T, NV, uint4, false, kCausal>(cur, v0 + tid, tpr, lim, p, mn, 0, v0), tpr,
+                       red_max);
   if (tid == 0) {
     for (int r = 0; r < csize; ++r) *cluster.map_shared_rank(&cmax[rank], r) = m;
   }
   cluster.sync();
   float mx = cmax[0];
   for (int r = 1; r < csize; ++r) mx = fmaxf(mx, cmax[r]);
-  const float s = group_sum<false>(softmax_exp<T, NV, kCausal>(cur, mx, mn, v0 + tid, tpr, lim), tpr, red_sum);
+  const float s =
+      group_sum<false>(softmax_exp<T, NV, kCausal>(cur, mx, mn, v0 + tid, tpr, lim, 0, v0), tpr, red_sum);
   if (tid == 0) {
     for (int r = 0; r < csize; ++r) *cluster.map_shared_rank(&csum[rank], r) = s;
   }
   cluster.sync();
   float sum = csum[0];
   for (int r = 1; r < csize; ++r) sum = __fadd_rn(sum, csum[r]);
-  softmax_store<T, NV, kCausal>(cur, sum, static_cast<T *>(p.dst) + row * p.cols, v0 + tid, tpr, p.nvec, lim);
+  softmax_store<T, NV, kCausal>(cur, sum, static_cast<T *>(p.dst) + row * p.cols, v0 + tid, tpr, p.nvec, lim, 0, 0,
+                                v0);
 }
 
 // Rows wider than the register budget: one block per row, three passes; the

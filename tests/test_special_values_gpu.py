@@ -71,3 +71,36 @@ def test_activations_special_values(oracle, xn, cuda, dtype):
         assert np.array_equal(g, r) or dtype == "f32", f"{op}"
         if dtype == "f32":
             assert_close(g, r, dtype, op)
+
+
+# Widths that reach each softmax kernel with a causal mask: the scalar/pair
+# rows (37), the window (250), the register pipe (1024, 1536; f32 4096), the
+# shared-memory-staged rows (16-bit 4096, f32 12000), the cluster (16-bit
+# 40000, f32 20000) and the loop kernel (16-bit 140000).
+CAUSAL_WIDTHS = {"f32": [37, 250, 1024, 1536, 4096, 12000, 20000],
+                 "bf16": [37, 250, 1024, 1536, 4096, 40000, 140000],
+                 "f16": [37, 250, 1024, 4096, 40000]}
+
+
+@pytest.mark.parametrize("dtype,cols", [(d, c) for d, cs in CAUSAL_WIDTHS.items() for c in cs])
+def test_causal_softmax_special_values(oracle, xn, cuda, dtype, cols):
+    """Causal rows holding +inf, NaN or only -inf among their live columns:
+    the reference masks with -inf and then takes the softmax, so such a row's
+    sum is NaN and every output of the row is NaN, the masked columns'
+    0 / NaN included. +inf or NaN in masked columns is never read. The offset
+    leaves most of each row masked, which selects the kernels' masked-vector
+    skipping."""
+    t1, offset = 8, cols // 4
+    x = randn(rng(cols + 1), (1, t1, cols))
+    x[0, 0, 0] = np.inf  # live
+    x[0, 1, 1] = np.nan  # live
+    x[0, 2, :] = -np.inf  # every live entry -inf
+    x[0, 3, 2] = -np.inf  # one live entry -inf: an ordinary row
+    x[0, 5, offset + 6:] = np.inf  # masked columns only
+    x[0, 6, offset + 7:] = np.nan  # masked columns only
+    x = to_storage(x, dtype)
+    ref = oracle.softmax_causal(x, offset, dtype)
+    got = from_device(xn.softmax_causal(to_device(x, dtype, cuda), offset), dtype)
+    g, r = _same_nonfinite(got, ref, dtype)
+    assert np.isnan(storage_to_f32(ref, dtype)[0, :3]).all()
+    assert_close(g, r, dtype, f"softmax_causal {dtype} special values {cols}")
