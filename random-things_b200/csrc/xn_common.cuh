@@ -459,7 +459,8 @@ __device__ __forceinline__ uint4 rotate_interleaved(const uint4 &x, const uint2 
 
 // ---------------------------------------------------------------------------
 // Reductions inside a row group of `tpr` threads (power of two, 1..1024).
-// Groups smaller than a warp use xor-shuffles that stay inside the group;
+// Groups smaller than a warp use xor-shuffles that stay inside the group (the
+// offsets below tpr, largest first, unrolled: no loop counter per step);
 // larger groups combine per-warp partials through shared memory `red`, which
 // must hold one float per warp of the block. The combination order is fixed,
 // so results are deterministic run to run.
@@ -472,8 +473,9 @@ __device__ __forceinline__ uint4 rotate_interleaved(const uint4 &x, const uint2 
 // ---------------------------------------------------------------------------
 template <bool kReuse = true>
 __device__ __forceinline__ float group_sum(float v, int tpr, float *red) {
-  const int width = tpr < 32 ? tpr : 32;
-  for (int o = width >> 1; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+    if (o < tpr) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
   if (tpr <= 32) return v;
   const int warp = threadIdx.x >> 5;
   const int wpr = tpr >> 5;
@@ -488,8 +490,9 @@ __device__ __forceinline__ float group_sum(float v, int tpr, float *red) {
 
 template <bool kReuse = true>
 __device__ __forceinline__ float group_max(float v, int tpr, float *red) {
-  const int width = tpr < 32 ? tpr : 32;
-  for (int o = width >> 1; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+    if (o < tpr) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   if (tpr <= 32) return v;
   const int warp = threadIdx.x >> 5;
   const int wpr = tpr >> 5;
