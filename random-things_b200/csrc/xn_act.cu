@@ -222,6 +222,29 @@ constexpr int kUnroll = 4;
 // inputs, keeps kUnroll (8 accesses of each lost 3-10 points there).
 constexpr int kUnaryUnroll = 8;
 
+// The op on one 16-byte vector of T.
+template <typename T, int OP>
+__device__ __forceinline__ uint4 unary_vec(uint4 raw) {
+  constexpr int N = Elem<T>::kVec;
+  if constexpr (std::is_same_v<T, __nv_bfloat16> && OP == XN_UNARY_SILU) {
+    return silu_bf16x8(raw);
+  } else if constexpr (std::is_same_v<T, __half> && OP == XN_UNARY_SILU) {
+    return silu_f16x8(raw);
+  } else if constexpr (!std::is_same_v<T, float> && OP == XN_UNARY_GELU_ERF) {
+    float2 v2[N / 2];
+    Pairs<T>::unpack(raw, v2);
+#pragma unroll
+    for (int j = 0; j < N / 2; ++j) v2[j] = gelu_erf2(v2[j]);
+    return Pairs<T>::pack(v2);
+  } else {
+    float v[N];
+    unpack<T>(raw, v);
+#pragma unroll
+    for (int j = 0; j < N; ++j) v[j] = unary_op<T, OP>(v[j]);
+    return pack<T>(v);
+  }
+}
+
 // kU accesses per thread: kUnaryUnroll for large tensors; 1 for tensors whose
 // one-access grid fits in one wave (8 blocks per SM), where the per-thread
 // chain of work, not bandwidth, sets the time.
@@ -244,25 +267,7 @@ __global__ void __launch_bounds__(kBlock) unary_kernel(void *dst, const void *sr
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
       const int64_t i = base + u * kBlock;
-      if (i < nacc) {
-        if constexpr (std::is_same_v<T, __nv_bfloat16> && OP == XN_UNARY_SILU) {
-          st_vec(d + i * N, silu_bf16x8(raw[u]));
-        } else if constexpr (std::is_same_v<T, __half> && OP == XN_UNARY_SILU) {
-          st_vec(d + i * N, silu_f16x8(raw[u]));
-        } else if constexpr (!std::is_same_v<T, float> && OP == XN_UNARY_GELU_ERF) {
-          float2 v2[N / 2];
-          Pairs<T>::unpack(raw[u], v2);
-#pragma unroll
-          for (int j = 0; j < N / 2; ++j) v2[j] = gelu_erf2(v2[j]);
-          st_vec(d + i * N, Pairs<T>::pack(v2));
-        } else {
-          float v[N];
-          unpack<T>(raw[u], v);
-#pragma unroll
-          for (int j = 0; j < N; ++j) v[j] = unary_op<T, OP>(v[j]);
-          st_vec(d + i * N, pack<T>(v));
-        }
-      }
+      if (i < nacc) st_vec(d + i * N, unary_vec<T, OP>(raw[u]));
     }
     // Ragged tail (< N elements), handled by block 0.
     if (blockIdx.x == 0) {
