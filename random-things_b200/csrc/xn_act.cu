@@ -99,15 +99,29 @@ __device__ __forceinline__ float silu_t(float s) {
   }
 }
 
-// silu_t<__half> on an element pair, same results bit for bit: -s by a sign
-// flip (exp(-0) = exp(+0), so the sign of 0 - s does not matter), exp from
-// CUDA's expf, and the f16 additions as f16x2 instructions: 1 + e in f32 is
-// exact for e >= 2^-13 and below 1 + 2^-11 (which rounds to 1) otherwise, so
-// its f16 rounding is the f16x2 sum's. The division is div_f16_by_d on f32
-// pairs.
+// silu_t<__half> on an element pair. e = T(exp(-s)): as for bf16 below,
+// 2^(x log2 e) for x = -s, but with a 13-bit piece of log2 e (kL2eHi16), so
+// that x * kL2eHi16 is exact for an f16 x (11 significant bits); the low part
+// enters as the factor 1 + c to second order (|x kL2eLo16| < 2^-8.5 for
+// |x| <= 40, so the third-order term is below 2^-29 relative). x is clamped to [-40, 40] first: exp(x) rounds to f16 0 below
+// -17.4 and to inf above 11.09, so no result changes, and NaN passes through.
+// The result carries the error of the hardware ex2 only;
+// test_silu_f16_exhaustive runs every finite f16 input against glibc's expf.
+// The f16 additions are f16x2 instructions: 1 + e in f32 is exact for
+// e >= 2^-13 and below 1 + 2^-11 (which rounds to 1) otherwise, so its f16
+// rounding is the f16x2 sum's. The division is div_f16_by_d on f32 pairs.
+constexpr float kL2eHi16 = 0x1.715p+0f;
+constexpr float kL2eLo16 = 0x1.1d94aep-14f;
+
 __device__ __forceinline__ __half2 silu_f16x2(__half2 s) {
-  const float2 x = __half22float2(__hneg2(s));
-  const __half2 e = __floats2half2_rn(expf(x.x), expf(x.y));
+  const __half2 xh = __hmin2_nan(__hmax2_nan(__hneg2(s), __float2half2_rn(-40.f)), __float2half2_rn(40.f));
+  const float2 x = __half22float2(xh);
+  const float2 th = __fmul2_rn(x, splat2(kL2eHi16));
+  const float2 tl = __fmul2_rn(x, splat2(kL2eLo16));
+  const float2 eh = make_float2(ex2_approx_ftz(th.x), ex2_approx_ftz(th.y));
+  const float2 c = __fmul2_rn(tl, __ffma2_rn(tl, splat2(kLn2SqHalf), splat2(kLn2)));
+  const float2 ef = __ffma2_rn(eh, c, eh);
+  const __half2 e = __floats2half2_rn(ef.x, ef.y);
   const __half2 d = __hadd2(__float2half2_rn(1.f), e);
   const float2 sf = __half22float2(s), df = __half22float2(d);
   const float2 r = make_float2(rcp_approx(df.x), rcp_approx(df.y));
