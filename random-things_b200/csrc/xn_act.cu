@@ -51,8 +51,6 @@ __device__ __forceinline__ float gelu_erf(float x) {
 // function against the oracle's glibc expf and IEEE division.
 constexpr float kL2eHi = 0x1.7154p+0f;
 constexpr float kL2eLo = 0x1.d94aep-18f;
-constexpr float kLn2 = 0x1.62e43p-1f;
-constexpr float kLn2SqHalf = 0x1.ebfbep-3f;
 
 __device__ __forceinline__ float rcp_approx(float x) {
   float y;
@@ -110,17 +108,9 @@ __device__ __forceinline__ float silu_t(float s) {
 // The f16 additions are f16x2 instructions: 1 + e in f32 is exact for
 // e >= 2^-13 and below 1 + 2^-11 (which rounds to 1) otherwise, so its f16
 // rounding is the f16x2 sum's. The division is div_f16_by_d on f32 pairs.
-constexpr float kL2eHi16 = 0x1.715p+0f;
-constexpr float kL2eLo16 = 0x1.1d94aep-14f;
-
 __device__ __forceinline__ __half2 silu_f16x2(__half2 s) {
   const __half2 xh = __hmin2_nan(__hmax2_nan(__hneg2(s), __float2half2_rn(-40.f)), __float2half2_rn(40.f));
-  const float2 x = __half22float2(xh);
-  const float2 th = __fmul2_rn(x, splat2(kL2eHi16));
-  const float2 tl = __fmul2_rn(x, splat2(kL2eLo16));
-  const float2 eh = make_float2(ex2_approx_ftz(th.x), ex2_approx_ftz(th.y));
-  const float2 c = __fmul2_rn(tl, __ffma2_rn(tl, splat2(kLn2SqHalf), splat2(kLn2)));
-  const float2 ef = __ffma2_rn(eh, c, eh);
+  const float2 ef = exp_split_f16(__half22float2(xh));
   const __half2 e = __floats2half2_rn(ef.x, ef.y);
   const __half2 d = __hadd2(__float2half2_rn(1.f), e);
   const float2 sf = __half22float2(s), df = __half22float2(d);

@@ -538,6 +538,17 @@ __device__ __forceinline__ float div_by(float x, float d, float r) {
 // f16, whose finer output grids would expose the error, nor for positive
 // arguments (SiLU's exp(-s)), which were not proven.
 constexpr float kLog2e = 0x1.715476p+0f;
+constexpr float kLn2 = 0x1.62e43p-1f;
+constexpr float kLn2SqHalf = 0x1.ebfbep-3f;
+
+// exp(x) for f16 values x with |x| <= 40 (a pair), accurate to the hardware
+// ex2's error: 2^(x kL2eHi16) (kL2eHi16 has 13 significant bits, x 11, so the
+// product is exact in f32) times 1 + c, c = t ln2 + (t ln2)^2 / 2 for the low
+// part t = x kL2eLo16 (|t| < 2^-8.5, so the dropped third-order term is below
+// 2^-29 relative). Callers clamp to [-40, 40], where exp's f16 value is
+// already 0 or inf beyond.
+constexpr float kL2eHi16 = 0x1.715p+0f;
+constexpr float kL2eLo16 = 0x1.1d94aep-14f;
 
 // 2^t by the hardware approximation, subnormal results kept.
 __device__ __forceinline__ float ex2_approx(float t) {
@@ -557,6 +568,14 @@ __device__ __forceinline__ float ex2_approx_ftz(float t) {
 }
 
 __device__ __forceinline__ float exp_of_bf16(float x) { return ex2_approx(__fmul_rn(x, kLog2e)); }
+
+__device__ __forceinline__ float2 exp_split_f16(float2 x) {
+  const float2 th = __fmul2_rn(x, make_float2(kL2eHi16, kL2eHi16));
+  const float2 tl = __fmul2_rn(x, make_float2(kL2eLo16, kL2eLo16));
+  const float2 eh = make_float2(ex2_approx_ftz(th.x), ex2_approx_ftz(th.y));
+  const float2 c = __fmul2_rn(tl, __ffma2_rn(tl, make_float2(kLn2SqHalf, kLn2SqHalf), make_float2(kLn2, kLn2)));
+  return __ffma2_rn(eh, c, eh);
+}
 
 // exp of a non-positive argument as the T-typed reference computes it, before
 // the rounding to T.
