@@ -325,6 +325,22 @@ __device__ __forceinline__ float softmax_prep(U (&cur)[NV], int lr, int tpr, int
   }
 }
 
+// Whether access k of thread lr is skipped as wholly masked (kSkip). For
+// 16-bit rows without a window the test is per slot (softmax_prep's kSlot),
+// the same for the whole row group: the masked accesses of the slot holding
+// the row's last live element then take the arithmetic on their -inf
+// entries, which gives the same +0.
+template <typename T, int NV, bool kSkip, typename U, bool kWin = false>
+__device__ __forceinline__ bool access_dead(int lr, int k, int tpr, int lim, int lo, int g0) {
+  constexpr int N = static_cast<int>(sizeof(U) / sizeof(T));
+  if constexpr (!kSkip)
+    return false;
+  else if constexpr (kSlotTests<T, kSkip, kWin>)
+    return (g0 + k * tpr) * N >= lim;
+  else
+    return (lr + k * tpr) * N - lo >= lim;
+}
+
 // e = T(exp(T(x - mx))) in place (exp(-inf) = 0 for masked and padding
 // entries); returns the thread's f32 sum of e, kept as two interleaved partial
 // sums. mx is the row maximum, a T value; mn is softmax_prep's minimum.
@@ -339,20 +355,6 @@ __device__ __forceinline__ float softmax_prep(U (&cur)[NV], int lr, int tpr, int
 //
 // kSkip: vectors starting at or past `lim` hold only masked entries; they
 // become +0 without the arithmetic (the same values and sums: exp(-inf) = +0).
-// For 16-bit rows without a window the test is per slot (softmax_prep's
-// kSlot): the masked accesses of the slot holding the row's last live element
-// take the arithmetic on their -inf entries, which gives the same +0.
-template <typename T, int NV, bool kSkip, typename U, bool kWin = false>
-__device__ __forceinline__ bool access_dead(int lr, int k, int tpr, int lim, int lo, int g0) {
-  constexpr int N = static_cast<int>(sizeof(U) / sizeof(T));
-  if constexpr (!kSkip)
-    return false;
-  else if constexpr (kSlotTests<T, kSkip, kWin>)
-    return (g0 + k * tpr) * N >= lim;
-  else
-    return (lr + k * tpr) * N - lo >= lim;
-}
-
 template <typename T, int NV, bool kSkip, typename U, bool kWin = false>
 __device__ __forceinline__ float softmax_exp(U (&cur)[NV], float mx, float mn, int lr, int tpr, int lim,
                                              int lo = 0, int g0 = 0) {
