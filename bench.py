@@ -1043,8 +1043,9 @@ def main() -> int:
     ap.add_argument("--config1-reps", type=int, default=20,
                     help="flushed launches per op of the config-1 f32 micro-pipeline (0 skips it)")
     ap.add_argument("--sweep", action="store_true", help="run the per-op bandwidth sweep instead (JSON per point)")
-    ap.add_argument("--sweep-widths", default="256,1024,4096,16384")
-    ap.add_argument("--sweep-rows", default="1024,16384,262144,1048576")
+    # Benchmark config 5's grid: power-of-two widths 256-16384 x rows 1K-1M.
+    ap.add_argument("--sweep-widths", default="256,512,1024,2048,4096,8192,16384")
+    ap.add_argument("--sweep-rows", default="1024,4096,16384,65536,262144,1048576")
     ap.add_argument("--sweep-dtypes", default="f32,bf16", help="comma-separated subset of f32, bf16, f16")
     ap.add_argument("--sweep-mem-gb", type=float, default=48.0)
     ap.add_argument("--sweep-ops", default=",".join(SWEEP_OPS),
