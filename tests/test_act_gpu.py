@@ -123,6 +123,20 @@ def test_silu_f16_exhaustive(oracle, xn, cuda):
     assert np.all(got[neg_big] == 0x8000)
 
 
+def test_gelu_f16_exhaustive(oracle, xn, cuda):
+    """Every finite f16 input through the 16-bit GELU(erf) (element pairs, the
+    kernels' own erfc fit) against glibc's erff: within one ulp, or within the
+    cancellation allowance |x| 2^-23 where x << 0."""
+    bits = np.arange(0x10000, dtype=np.uint32).astype(np.uint16)
+    x = bits[((bits >> 10) & 0x1F) != 0x1F]
+    ref = oracle.unary(x, "gelu_erf", "f16")
+    got = from_device(xn.gelu_erf(to_device(x, "f16", cuda)), "f16")
+    allow = gelu_erf_abs_bound(storage_to_f32(x, "f16"))
+    stats = assert_close(got, ref, "f16", "gelu_erf f16 exhaustive", extra_abs=allow)
+    print(f"gelu_erf f16: {int(np.sum(got != ref))} of {x.size} inputs differ")
+    assert stats["exact_frac"] > 0.999, stats
+
+
 def test_swiglu_f16_all_gates(oracle, xn, cuda):
     """Every finite f16 gate value against random up values."""
     bits = np.arange(0x10000, dtype=np.uint32).astype(np.uint16)
