@@ -104,3 +104,29 @@ def test_causal_softmax_special_values(oracle, xn, cuda, dtype, cols):
     g, r = _same_nonfinite(got, ref, dtype)
     assert np.isnan(storage_to_f32(ref, dtype)[0, :3]).all()
     assert_close(g, r, dtype, f"softmax_causal {dtype} special values {cols}")
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16", "f16"])
+@pytest.mark.parametrize("interleaved", [False, True])
+def test_rope_special_values(oracle, xn, cuda, dtype, interleaved):
+    """RoPE on rows holding +-inf, NaN and values whose products overflow:
+    each product and sum rounds to T as the reference's T arithmetic does
+    (cpu_backend.rs:359-422), so the results match bit for bit, inf signs
+    included; NaN positions match (their payloads are not compared)."""
+    b, h, t, d, max_pos = 1, 3, 6, 16, 8
+    x = randn(rng(d + t), (b, h, t, d))
+    x[0, 0, 1, 2] = np.inf
+    x[0, 0, 2, 9] = -np.inf
+    x[0, 1, 3, 0] = np.nan
+    x[0, 1, 4, :] = 6.0e4 if dtype == "f16" else 3.0e38  # products near the top of the range
+    x[0, 2, 5, :] = -0.0
+    x = to_storage(x, dtype)
+    cos, sin = oracle.rope_tables(d, max_pos, 10000.0, dtype, "mimi")
+    ref = oracle.rope(x, cos, sin, 2, dtype, interleaved=interleaved)
+    f = xn.rope_i if interleaved else xn.rope
+    got = from_device(f(to_device(x, dtype, cuda), to_device(cos, dtype, cuda), to_device(sin, dtype, cuda), 2),
+                      dtype)
+    g, r = storage_to_f32(got, dtype), storage_to_f32(ref, dtype)
+    assert np.array_equal(np.isnan(g), np.isnan(r)), "NaN pattern differs"
+    keep = ~np.isnan(r)
+    assert np.array_equal(got[keep], ref[keep]), "non-NaN outputs differ"
