@@ -6,6 +6,7 @@ IEEE arithmetic element for element: the same non-finite pattern, and the
 same values elsewhere within the usual tolerance."""
 import numpy as np
 import pytest
+import torch
 
 from helpers import (assert_close, from_device, layer_norm_abs_bound, randn, rng, storage_to_f32, to_device,
                      to_storage)
@@ -130,3 +131,55 @@ def test_rope_special_values(oracle, xn, cuda, dtype, interleaved):
     assert np.array_equal(np.isnan(g), np.isnan(r)), "NaN pattern differs"
     keep = ~np.isnan(r)
     assert np.array_equal(got[keep], ref[keep]), "non-NaN outputs differ"
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16", "f16"])
+@pytest.mark.parametrize("cols", [64, 250, 1024])
+def test_residual_norms_special_values(oracle, xn, cuda, dtype, cols):
+    """The fused residual prologue h = T(x + T(branch * ls)) with +-inf, NaN
+    and cancelling infinities in x or the branch: h bit for bit outside NaN
+    positions (which match), then both norms of h with the same non-finite
+    pattern as the reference."""
+    r = rng(cols + 3)
+    x = randn(r, (6, cols))
+    br = randn(r, (6, cols))
+    x[0, 1], br[0, 1] = np.inf, -np.inf  # inf + (-inf) = NaN
+    x[1, 2] = np.nan
+    br[2, 3] = np.inf
+    x[3, :], br[3, :] = 1.0, -1.0  # exact cancellation: h = +0 everywhere (up to ls)
+    x, br = to_storage(x, dtype), to_storage(br, dtype)
+    ls = to_storage(r.uniform(0.5, 1.0, cols).astype(np.float32), dtype)
+    w = to_storage(randn(r, cols, 0.02, 1.0), dtype)
+    b = to_storage(randn(r, cols, 0.1), dtype)
+    X, BR, LS, W, B = (to_device(a, dtype, cuda) for a in (x, br, ls, w, b))
+    for name, (y, h), (ry, rh) in [
+        ("rms_norm_residual", xn.rms_norm_residual(X, BR, W, 1e-5, layer_scale=LS),
+         oracle.rms_norm_residual(x, br, w, 1e-5, dtype, layer_scale=ls)),
+        ("layer_norm_residual", xn.layer_norm_residual(X, BR, W, B, 1e-5, layer_scale=LS),
+         oracle.layer_norm_residual(x, br, w, b, 1e-5, dtype, layer_scale=ls)),
+    ]:
+        gh = from_device(h, dtype)
+        assert np.array_equal(np.isnan(storage_to_f32(gh, dtype)), np.isnan(storage_to_f32(rh, dtype))), name
+        keep = ~np.isnan(storage_to_f32(rh, dtype))
+        assert np.array_equal(gh[keep], rh[keep]), f"{name}: residual output differs"
+        gy = from_device(y, dtype)
+        _same_nonfinite(gy, ry, dtype)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16", "f16"])
+def test_gather_copies_every_bit_pattern(xn, cuda, dtype):
+    """The embedding gather is a byte copy: NaN payloads, infinities, signed
+    zeros and subnormals arrive unchanged."""
+    width = 64
+    if dtype == "f32":
+        pats = np.array([0x7fc00001, 0xffc00123, 0x7f800000, 0xff800000, 0x80000000, 0x00000001, 0x807fffff],
+                        dtype=np.uint32)
+    else:
+        pats = np.array([0x7e01, 0xfe77, 0x7c00, 0xfc00, 0x8000, 0x0001, 0x83ff] if dtype == "f16"
+                        else [0x7fc1, 0xffa3, 0x7f80, 0xff80, 0x8000, 0x0001, 0x807f], dtype=np.uint16)
+    table = np.resize(pats, (40, width)).astype(pats.dtype)
+    table[np.arange(40), np.arange(40) % width] = pats[0]
+    ids = np.array([39, 0, 7, 7, 21, 3], dtype=np.int64)
+    store = table.view(np.float32) if dtype == "f32" else table
+    got = from_device(xn.index_select(to_device(store, dtype, cuda), torch.from_numpy(ids).to(cuda), 0), dtype)
+    assert np.array_equal(got.view(pats.dtype), table[ids])
