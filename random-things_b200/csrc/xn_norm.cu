@@ -405,6 +405,162 @@ __global__ void __launch_bounds__(kMaxBlock, kMaxBlock == 256 ? 4 : (kMaxBlock =
   }
 }
 
+// RMSNorm rows whose byte width is not a multiple of 16 (such as 250 16-bit
+// columns), taken R at a time: R = 16 / gcd(cols * s, 16) consecutive rows are
+// a run of R * cols elements that starts and ends on a 16-byte boundary, so a
+// group of tpr threads reads and writes it with aligned 16-byte accesses, as
+// the vector kernel does a row. An access holds elements of one row, or of
+// two where a row ends inside it (R - 1 accesses of a run). The weights (and
+// the layer scale) are tiled R times in shared memory, so every access's
+// weights are one aligned 16-byte load. Each access adds its sum of squares
+// to the row (or two) it covers, and the R row sums of a run are reduced
+// across the group together. Per element, the arithmetic is the vector
+// kernel's (the same IEEE f32 operations in the same order), so the values
+// match it; only the grouping of the row sums differs. tpr <= 32 (shuffle
+// reductions only).
+template <int R>
+__device__ __forceinline__ void add_to_row(float (&acc)[R], int row, float v) {
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+    if (r == row) acc[r] = __fadd_rn(acc[r], v);
+}
+
+template <int R>
+__device__ __forceinline__ float row_value(const float (&v)[R], int row) {
+  float out = v[0];
+#pragma unroll
+  for (int r = 1; r < R; ++r)
+    if (r == row) out = v[r];
+  return out;
+}
+
+template <typename T, int NV, int R, bool kBranch>
+__global__ void __launch_bounds__(256, 4) norm_run_kernel(const NormParams p) {
+  griddep_wait();
+  griddep_release();
+  using P = Pairs<T>;
+  constexpr int N = Elem<T>::kVec;
+  constexpr int KP = P::kP;
+  extern __shared__ __align__(16) unsigned char run_smem[];
+  const int cols = static_cast<int>(p.cols);
+  const int run_len = R * cols;  // = p.nvec * N, a multiple of the vector
+  T *wt = reinterpret_cast<T *>(run_smem);
+  T *lt = wt + run_len;
+  const T *w = static_cast<const T *>(p.w);
+  const T *ls = static_cast<const T *>(p.ls);
+  for (int e = threadIdx.x; e < run_len; e += blockDim.x) {
+    const int c = e % cols;
+    wt[e] = w != nullptr ? w[c] : Elem<T>::from_f32(1.f);
+    if constexpr (kBranch) {
+      if (ls != nullptr) lt[e] = ls[c];
+    }
+  }
+  __syncthreads();
+  const int tpr = p.tpr;
+  const int g = threadIdx.x / tpr;
+  const int lr = threadIdx.x - g * tpr;
+  const int rpb = blockDim.x / tpr;
+  const int64_t run = static_cast<int64_t>(blockIdx.x) * rpb + g;
+  const bool active = run * R < p.rows;
+  const int64_t base = run * run_len;
+  // Per access: the run row of its first element and how many of its
+  // elements come before the next row (>= N: all of them).
+  int r0[NV], sp[NV];
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int e0 = (lr + k * tpr) * N;
+    r0[k] = e0 / cols;
+    sp[k] = (r0[k] + 1) * cols - e0;
+  }
+  auto live = [&](int k) { return active && lr + k * tpr < p.nvec; };
+
+  // 1) h = src (+ T(branch * ls)), packed.
+  const T *src = static_cast<const T *>(p.src) + base;
+  uint4 h[NV];
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    h[k] = make_uint4(0u, 0u, 0u, 0u);
+    if (live(k)) h[k] = ld_stream(src + (lr + k * tpr) * N);
+  }
+  if constexpr (kBranch) {
+    const T *br = static_cast<const T *>(p.branch) + base;
+    uint4 bv[NV];
+#pragma unroll
+    for (int k = 0; k < NV; ++k)
+      if (live(k)) bv[k] = ld_stream(br + (lr + k * tpr) * N);
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      if (live(k)) {
+        const int vi = lr + k * tpr;
+        if (ls != nullptr) {
+          const uint4 sv = *reinterpret_cast<const uint4 *>(lt + vi * N);
+          h[k] = residual_vec_sv<T>(h[k], bv[k], &sv);
+        } else {
+          h[k] = residual_vec_sv<T>(h[k], bv[k], nullptr);
+        }
+        if (p.res_out != nullptr) st_vec(static_cast<T *>(p.res_out) + base + vi * N, h[k]);
+      }
+    }
+  }
+
+  // 2) Each row's sum of squares: an access's goes to its row, or is split.
+  const float cols_f = __int2float_rn(cols);
+  T *dst = static_cast<T *>(p.dst) + base;
+  auto elem = [](const float2 (&x)[KP], int e) { return (e & 1) ? x[e >> 1].y : x[e >> 1].x; };
+  float acc[R] = {};
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    if (!live(k)) continue;
+    float2 x[KP];
+    P::unpack(h[k], x);
+    if (sp[k] >= N) {
+      float2 s2 = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < KP; ++j) s2 = __ffma2_rn(x[j], x[j], s2);
+      add_to_row(acc, r0[k], __fadd_rn(s2.x, s2.y));
+    } else {
+      float lo = 0.f, hi = 0.f;
+#pragma unroll
+      for (int e = 0; e < N; ++e) {
+        const float v = elem(x, e);
+        if (e < sp[k])
+          lo = __fmaf_rn(v, v, lo);
+        else
+          hi = __fmaf_rn(v, v, hi);
+      }
+      add_to_row(acc, r0[k], lo);
+      add_to_row(acc, r0[k] + 1, hi);
+    }
+  }
+  float m[R], rc[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    m[r] = __fsqrt_rn(__fadd_rn(__fdiv_rn(group_sum<false>(acc[r], tpr, nullptr), cols_f), p.eps));
+    rc[r] = __frcp_rn(m[r]);
+  }
+  // 3) dst = T(x / m * alpha), each element with its own row's m.
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    if (!live(k)) continue;
+    const int vi = lr + k * tpr;
+    float2 x[KP], wv[KP];
+    P::unpack(opaque(h[k]), x);
+    P::unpack(*reinterpret_cast<const uint4 *>(wt + vi * N), wv);
+    const float m_lo = row_value(m, r0[k]), r_lo = row_value(rc, r0[k]);
+    const float m_hi = sp[k] >= N ? m_lo : row_value(m, r0[k] + 1);
+    const float r_hi = sp[k] >= N ? r_lo : row_value(rc, r0[k] + 1);
+#pragma unroll
+    for (int j = 0; j < KP; ++j) {
+      // The quotient by div_by's steps, per element: the two elements of a
+      // pair may belong to different rows.
+      const bool fx = 2 * j < sp[k], fy = 2 * j + 1 < sp[k];
+      x[j].x = __fmul_rn(div_by(x[j].x, fx ? m_lo : m_hi, fx ? r_lo : r_hi), wv[j].x);
+      x[j].y = __fmul_rn(div_by(x[j].y, fy ? m_lo : m_hi, fy ? r_lo : r_hi), wv[j].y);
+    }
+    st_vec(dst + vi * N, P::pack(x));
+  }
+}
+
 // Rows wider than the register budget: one block per row, several passes.
 template <typename T, bool kLN>
 __global__ void __launch_bounds__(1024) norm_loop_kernel(const NormParams p) {
@@ -546,9 +702,62 @@ bool launch_regs(NormParams p, int nv, int block, int64_t grid, cudaStream_t st)
 
 // Chooses the row-group shape and launches. Register budget: <= 32 f32 values
 // of the row per thread, so rows of up to 32768 elements stay in registers.
+// norm_run_kernel for RMSNorm rows whose byte width is not a multiple of 16,
+// when runs are of 4 rows (2 or 4 for f32; odd 16-bit widths would need 8,
+// whose row sums spill), the row count
+// divides into runs, a run fits 32 threads of 4 accesses and its tiled
+// weights fit 48 KB of shared memory; false leaves the rows to the other
+// kernels. LayerNorm measured slower in this form (bf16 262144 x 250: 0.42
+// with 4-byte accesses, 0.29 here: its two reductions of R row values and the
+// per-access row selection cost more than the wider accesses save).
+template <typename T, bool kBranch>
+bool launch_norm_run_r(const NormParams &p, int r, int64_t grid, size_t smem, cudaStream_t st) {
+  switch (r) {
+    case 2:
+      launch_k(norm_run_kernel<T, 4, 2, kBranch>, dim3(grid), dim3(256), smem, st, p);
+      return true;
+    case 4:
+      launch_k(norm_run_kernel<T, 4, 4, kBranch>, dim3(grid), dim3(256), smem, st, p);
+      return true;
+    default:
+      return false;
+  }
+}
+
+template <typename T>
+bool try_launch_norm_run(NormParams p, cudaStream_t st) {
+  constexpr int V = Elem<T>::kVec;
+  const int64_t row_bytes = p.cols * static_cast<int64_t>(sizeof(T));
+  if (row_bytes % 16 == 0 || p.cols <= 0) return false;
+  const uintptr_t big = reinterpret_cast<uintptr_t>(p.dst) | reinterpret_cast<uintptr_t>(p.src) |
+                        reinterpret_cast<uintptr_t>(p.branch) | reinterpret_cast<uintptr_t>(p.res_out);
+  if ((big & 15u) != 0) return false;
+  int64_t gcd = 16;
+  while (row_bytes % gcd != 0) gcd /= 2;
+  const int r = static_cast<int>(16 / gcd);
+  // 16-bit rows of a multiple of 8 bytes (R = 2) keep the 8-byte accesses,
+  // which measured a little faster (bf16 262144 x 100: 0.71 against 0.68).
+  if (r > 4 || (sizeof(T) == 2 && r == 2) || p.rows % r != 0) return false;
+  const bool branch = p.branch != nullptr;
+  const int64_t nvec = r * p.cols / V;
+  const int64_t tpr = pow2_ceil(ceil_div(nvec, static_cast<int64_t>(4)));
+  if (tpr > 32) return false;
+  const size_t smem = static_cast<size_t>(r * p.cols) * sizeof(T) * (branch ? 2 : 1);
+  if (smem > 48 * 1024) return false;
+  p.tpr = static_cast<int>(tpr);
+  p.nvec = static_cast<int>(nvec);
+  const int64_t grid = ceil_div(p.rows / r, 256 / tpr);
+  if (grid > 0x7fffffffLL) return false;
+  return branch ? launch_norm_run_r<T, true>(p, r, grid, smem, st)
+                : launch_norm_run_r<T, false>(p, r, grid, smem, st);
+}
+
 template <typename T, bool kLN>
 int launch_norm(NormParams p, cudaStream_t st, const char *op) {
   constexpr int V = Elem<T>::kVec;
+  if constexpr (!kLN) {
+    if (try_launch_norm_run<T>(p, st)) return check_launch(op);
+  }
   const uintptr_t addr_bits = reinterpret_cast<uintptr_t>(p.dst) | reinterpret_cast<uintptr_t>(p.src) |
                               reinterpret_cast<uintptr_t>(p.w) | reinterpret_cast<uintptr_t>(p.b) |
                               reinterpret_cast<uintptr_t>(p.branch) | reinterpret_cast<uintptr_t>(p.ls) |

@@ -143,13 +143,17 @@ def test_residual_add(oracle, xn, cuda, dtype, rows, cols, with_ls):
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
-@pytest.mark.parametrize("rows,cols", [(1000, 250), (64, 1002), (6, 2046), (33, 10), (257, 36), (4, 4094)])
-@pytest.mark.parametrize("variant", ["rms", "rms_residual_ls", "ln", "ln_residual_ls", "ln_no_mean"])
+@pytest.mark.parametrize("rows,cols", [(1000, 250), (64, 1002), (6, 2046), (33, 10), (257, 36), (4, 4094),
+                                       (512, 100), (1024, 170), (256, 126), (8, 250), (1002, 250)])
+@pytest.mark.parametrize("variant", ["rms", "rms_residual", "rms_residual_ls", "ln", "ln_residual_ls", "ln_no_mean"])
 def test_norm_narrow_accesses(oracle, xn, cuda, dtype, rows, cols, variant):
     """Rows whose byte width is a multiple of 8 or 4 but not 16 (16-bit rows of
-    even width such as Mimi's 250 scores, f32 rows of even width): 8- and
-    4-byte accesses with the vector kernel's arithmetic. Also a view whose
-    start is 4 bytes past a 16-byte boundary."""
+    even width such as Mimi's 250 scores, f32 rows of even width). RMSNorm
+    rows whose count divides into runs of 4 rows (f32: 2 or 4) that start on
+    16-byte boundaries (1000 x 250, 1024 x 170, 256 x 126, 8 x 250; f32 also
+    512 x 100) take the run kernel's 16-byte accesses, some holding the end of
+    one row and the start of the next; the rest (LayerNorm, 1002 x 250, ...)
+    take 8- and 4-byte accesses with the vector kernel's arithmetic."""
     x, br, w, b, ls = _inputs(rows * 5 + cols, rows, cols, dtype, ln=variant.startswith("ln"))
     eps = 1e-5
     branch = br if "residual" in variant else None
