@@ -448,11 +448,16 @@ __global__ void __launch_bounds__(256, 4) norm_run_kernel(const NormParams p) {
   T *lt = wt + run_len;
   const T *w = static_cast<const T *>(p.w);
   const T *ls = static_cast<const T *>(p.ls);
-  for (int e = threadIdx.x; e < run_len; e += blockDim.x) {
-    const int c = e % cols;
-    wt[e] = w != nullptr ? w[c] : Elem<T>::from_f32(1.f);
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+    const T wc = w != nullptr ? w[c] : Elem<T>::from_f32(1.f);
+#pragma unroll
+    for (int r = 0; r < R; ++r) wt[r * cols + c] = wc;
     if constexpr (kBranch) {
-      if (ls != nullptr) lt[e] = ls[c];
+      if (ls != nullptr) {
+        const T lc = ls[c];
+#pragma unroll
+        for (int r = 0; r < R; ++r) lt[r * cols + c] = lc;
+      }
     }
   }
   __syncthreads();
@@ -469,7 +474,9 @@ __global__ void __launch_bounds__(256, 4) norm_run_kernel(const NormParams p) {
 #pragma unroll
   for (int k = 0; k < NV; ++k) {
     const int e0 = (lr + k * tpr) * N;
-    r0[k] = e0 / cols;
+    r0[k] = 0;
+#pragma unroll
+    for (int r = 1; r < R; ++r) r0[k] += e0 >= r * cols;
     sp[k] = (r0[k] + 1) * cols - e0;
   }
   auto live = [&](int k) { return active && lr + k * tpr < p.nvec; };
@@ -547,15 +554,27 @@ __global__ void __launch_bounds__(256, 4) norm_run_kernel(const NormParams p) {
     P::unpack(opaque(h[k]), x);
     P::unpack(*reinterpret_cast<const uint4 *>(wt + vi * N), wv);
     const float m_lo = row_value(m, r0[k]), r_lo = row_value(rc, r0[k]);
-    const float m_hi = sp[k] >= N ? m_lo : row_value(m, r0[k] + 1);
-    const float r_hi = sp[k] >= N ? r_lo : row_value(rc, r0[k] + 1);
+    if (sp[k] >= N) {
+      // One row: the vector kernel's paired div_by steps.
+      const float2 nm2 = splat2(neg_divisor(m_lo)), r2 = splat2(r_lo);
 #pragma unroll
-    for (int j = 0; j < KP; ++j) {
-      // The quotient by div_by's steps, per element: the two elements of a
-      // pair may belong to different rows.
-      const bool fx = 2 * j < sp[k], fy = 2 * j + 1 < sp[k];
-      x[j].x = __fmul_rn(div_by(x[j].x, fx ? m_lo : m_hi, fx ? r_lo : r_hi), wv[j].x);
-      x[j].y = __fmul_rn(div_by(x[j].y, fy ? m_lo : m_hi, fy ? r_lo : r_hi), wv[j].y);
+      for (int j = 0; j < KP; ++j) {
+        const float2 q0 = __fmul2_rn(x[j], r2);
+        const float2 rem = __ffma2_rn(nm2, q0, x[j]);
+        float2 q = __ffma2_rn(rem, r2, q0);
+        q.x = copysignf(q.x, q0.x);
+        q.y = copysignf(q.y, q0.y);
+        x[j] = __fmul2_rn(q, wv[j]);
+      }
+    } else {
+      const float m_hi = row_value(m, r0[k] + 1), r_hi = row_value(rc, r0[k] + 1);
+#pragma unroll
+      for (int j = 0; j < KP; ++j) {
+        // Per element: the two elements of a pair may belong to different rows.
+        const bool fx = 2 * j < sp[k], fy = 2 * j + 1 < sp[k];
+        x[j].x = __fmul_rn(div_by(x[j].x, fx ? m_lo : m_hi, fx ? r_lo : r_hi), wv[j].x);
+        x[j].y = __fmul_rn(div_by(x[j].y, fy ? m_lo : m_hi, fy ? r_lo : r_hi), wv[j].y);
+      }
     }
     st_vec(dst + vi * N, P::pack(x));
   }
