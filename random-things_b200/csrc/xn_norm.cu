@@ -727,8 +727,9 @@ bool launch_regs(NormParams p, int nv, int block, int64_t grid, cudaStream_t st)
 // divides into runs, a run fits 32 threads of 4 accesses and its tiled
 // weights fit 48 KB of shared memory; false leaves the rows to the other
 // kernels. LayerNorm measured slower in this form (bf16 262144 x 250: 0.42
-// with 4-byte accesses, 0.29 here: its two reductions of R row values and the
-// per-access row selection cost more than the wider accesses save).
+// with 4-byte accesses, 0.33 here, f32 0.81 against 0.71: its two reductions
+// of R row values and the per-access row selections cost more than the wider
+// accesses save).
 template <typename T, bool kBranch>
 bool launch_norm_run_r(const NormParams &p, int r, int64_t grid, size_t smem, cudaStream_t st) {
   switch (r) {
